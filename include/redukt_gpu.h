@@ -1,0 +1,135 @@
+/*
+ * redukt_gpu.h -- C ABI of libredukt_gpu.so, the B200 (sm_100a) backbone engine.
+ *
+ * The library is a drop-in for redukt's GPU backbone plugin: it exports the FFI v1 and v2
+ * symbols with the reference's names, argument meaning and result codes, so the Rust host
+ * (src/infrastructure/plugin_backend/loader.rs:157-216) loads it unchanged.  Everything after
+ * the v2 block is additive: optional symbols an old host never looks up.
+ *
+ * Threading: like the reference plugin, one model per process (a global singleton), calls are
+ * single-threaded and not reentrant (docs/api/PLUGIN-FFI-V2.md section 3).  Select the GPU of a
+ * process with CUDA_VISIBLE_DEVICES; the host always passes device_id 0
+ * (src/application/model_loader.rs:436).
+ *
+ * Plain C types only: no torch or CUDA types cross this boundary.
+ */
+#ifndef REDUKT_GPU_H
+#define REDUKT_GPU_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Result codes: BackendResult, src/domain/backend_ffi.rs:25-41 (v2 adds 5). */
+typedef enum {
+    BACKEND_OK = 0,
+    BACKEND_INIT_FAILED = 1,
+    BACKEND_FORWARD_FAILED = 2,
+    BACKEND_VERSION_MISMATCH = 3,
+    BACKEND_WEIGHTS_NOT_FOUND = 4,
+    BACKEND_INVALID_ARGUMENT = 5
+} BackendResult;
+
+#define BACKEND_FFI_VERSION 1 /* BackendInfo.ffi_version (src/domain/backend_ffi.rs:16) */
+#define BACKEND_ABI_VERSION 2 /* redukt_backend_abi_version() (src/domain/backend_ffi.rs:19) */
+#define BACKEND_NAME_MAX 64
+
+/* BackendInfo, src/domain/backend_ffi.rs:61-72. */
+typedef struct {
+    uint32_t ffi_version;
+    uint32_t vocab_size;
+    uint32_t hidden_dim;
+    uint8_t name[BACKEND_NAME_MAX];
+} BackendInfo;
+
+/* ---- FFI v1 (src/domain/backend_ffi.rs:91-114; plugins/redukt-gpu-cuda/mamba_cuda.cu:675-731) ---- */
+
+/* Loads `weights_path` (a *.rbin file, or a directory holding model.rbin: mamba_cuda.cu:664-671)
+ * onto device `device_id` and allocates the private single-stream state.  WEIGHTS_NOT_FOUND for
+ * a missing/invalid file, INIT_FAILED for a CUDA failure.  Replaces mamba_cuda.cu:675-708. */
+BackendResult redukt_backend_init(const uint8_t* weights_path, int32_t device_id, BackendInfo* info_out);
+
+/* One step of the v1 stream; writes vocab_size logits.  Replaces mamba_cuda.cu:710-715. */
+BackendResult redukt_backend_forward(uint32_t token, float* out_logits, uint32_t vocab_size);
+
+/* Zeroes the v1 stream's recurrent state.  Replaces mamba_cuda.cu:717-722. */
+void redukt_backend_reset_state(void);
+
+/* Releases every device allocation, including the batch pool.  Replaces mamba_cuda.cu:724-727. */
+void redukt_backend_free(void);
+
+/* ---- FFI v2 (src/domain/backend_ffi.rs:137-177; docs/api/PLUGIN-FFI-V2.md; mamba_cuda.cu:731-761) ---- */
+
+/* Returns 2.  Replaces mamba_cuda.cu:731. */
+uint32_t redukt_backend_abi_version(void);
+
+/* (Re)allocates `max_streams` zeroed state slots (0 = release).  INVALID_ARGUMENT above 4096,
+ * INIT_FAILED without a model or on allocation failure.  Replaces mamba_cuda.cu:733-745. */
+int32_t redukt_backend_batch_init(uint32_t max_streams);
+
+/* Zeroes the state (and the periodic-reset counter) of the listed slots; NULL = every slot.
+ * Replaces mamba_cuda.cu:747-752. */
+int32_t redukt_backend_batch_reset(const uint32_t* slots, uint32_t n_slots);
+
+/* Advances each listed slot by one token and writes row b of out_logits [n_streams * vocab_size]
+ * for batch position b.  Synchronous.  INVALID_ARGUMENT (vocab mismatch, n > pool, slot >= pool,
+ * duplicate slot, token >= vocab, NULL pointer) returns before any launch with no state change.
+ * A stream's logits are bit-identical for every batch size, batch position and slot.
+ * Replaces mamba_cuda.cu:754-761. */
+int32_t redukt_backend_forward_batch(uint32_t n_streams, const uint32_t* slots, const uint32_t* tokens,
+                                     float* out_logits, uint32_t vocab_size);
+
+/* ---- Additive extensions (optional symbols; absent from the reference) ---- */
+
+/* Device-side periodic state reset: before a slot's token enters the model, the slot restarts
+ * from zero state if it has run `every` forwards since its last reset (0 = never, the default).
+ * The schedule is MambaState::maybe_periodic_reset (src/infrastructure/mamba/model.rs:315-320) and
+ * PluginState::tick (src/infrastructure/plugin_backend/model.rs:44-49); a host that sets it must
+ * stop calling batch_reset from its own tick.  Applies to the v1 stream and every batch slot. */
+int32_t redukt_backend_set_reset_every(uint32_t every);
+
+/* forward_batch that returns softmax probabilities (per row: exp(l - max) / sum) instead of
+ * logits, computed on the device from the same logits; used for parity and benchmarks. */
+int32_t redukt_backend_forward_batch_probs(uint32_t n_streams, const uint32_t* slots, const uint32_t* tokens,
+                                           float* out_probs, uint32_t vocab_size);
+
+/* forward_batch on device-resident inputs: d_slots/d_tokens/d_out are device pointers and the
+ * work is enqueued on `cuda_stream` (a cudaStream_t, NULL = the library's stream) without a host
+ * synchronisation.  Slots/tokens are checked on the device; a bad entry sets the error word read by
+ * redukt_b200_device_error() and its row is not computed.  Duplicate slots are the caller's
+ * responsibility.  probs != 0 writes probabilities instead of logits. */
+int32_t redukt_b200_forward_batch_device(uint32_t n_streams, const uint32_t* d_slots, const uint32_t* d_tokens,
+                                         float* d_out, uint32_t vocab_size, int32_t probs, void* cuda_stream);
+
+/* Reads and clears the device error word set by redukt_b200_forward_batch_device (0 = none). */
+int32_t redukt_b200_device_error(uint32_t* out_word);
+
+/* Copies one batch slot's recurrent state in the reference layout (MambaState,
+ * src/infrastructure/mamba/model.rs:278-284): conv [n_layer][d_inner][d_conv-1] and
+ * ssm [n_layer][d_inner][d_state].  Either pointer may be NULL.  slot = UINT32_MAX reads the v1 state. */
+int32_t redukt_b200_get_state(uint32_t slot, float* conv, float* ssm);
+
+/* Copies one quantised matrix as the engine holds it: which = 0 embedding, 1 head, 2 in_proj,
+ * 3 out_proj (layer).  q [rows][cols] int8, scales [rows][cols/64] f32 (per-row scales repeated). */
+int32_t redukt_b200_get_q8(int32_t which, uint32_t layer, int8_t* q, float* scales);
+
+/* Model and engine facts: out[0..11] = vocab, d_model, d_inner, d_state, d_conv, dt_rank, n_layer,
+ * flags, profile (0 F32, 1 Q8-g64, 2 Q8 per-row), pool capacity, reset_every, projection path. */
+int32_t redukt_b200_info(uint32_t* out, uint32_t n);
+
+/* Engine switches for tests and benchmarks:
+ *   "proj_path"  0 = automatic, 1 = CUDA-core projections, 2 = tensor-core projections
+ *   "graphs"     0/1 = replay each batch size's launch sequence from a captured CUDA graph
+ * Returns INVALID_ARGUMENT for an unknown key or value. */
+int32_t redukt_b200_set_option(const char* key, int64_t value);
+
+/* Last error message of this library (empty string when none). */
+const char* redukt_b200_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* REDUKT_GPU_H */

@@ -1,0 +1,803 @@
+// libredukt_gpu.so: the C-ABI of include/redukt_gpu.h over the sm_100a decode-step kernels.
+//
+// Host side of the engine: .rbin loading (with Q8 quantisation on the device), the slot pool,
+// argument validation with the reference's error behaviour, the launch sequence of one step
+// and CUDA-graph replay of that sequence per batch size.  The reference counterpart is
+// plugins/redukt-gpu-cuda/mamba_cuda.cu:385-761.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <new>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "../../include/redukt_gpu.h"
+#include "rk_kernels.cuh"
+
+namespace {
+
+using namespace rk;
+
+constexpr uint32_t kRbinMagic = 0x55504752u;
+constexpr uint32_t kFlagNormBias = 1u << 0;
+constexpr uint32_t kFlagUntiedHead = 1u << 1;
+constexpr uint32_t kFlagQ8 = 1u << 2;
+constexpr uint32_t kFlagQ8PerRow = 1u << 3;
+constexpr uint32_t kMaxStreams = 4096u;  // batch_init cap (mamba_cuda.cu:55)
+
+enum Profile { kF32 = 0, kQ8 = 1, kQ8Row = 2 };
+
+char g_err[1024] = "";
+
+void set_err(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    fprintf(stderr, "[redukt-b200] %s\n", g_err);
+}
+
+#define CK(call, code)                                                                        \
+    do {                                                                                      \
+        cudaError_t e_ = (call);                                                              \
+        if (e_ != cudaSuccess) {                                                              \
+            set_err("CUDA error %s at %s:%d (%s)", cudaGetErrorString(e_), __FILE__, __LINE__, #call); \
+            return (code);                                                                    \
+        }                                                                                     \
+    } while (0)
+
+struct RbinHeader {
+    uint32_t magic, version, vocab, d, di, ds, dc, dr, nl, flags, tokenizer;
+};
+
+// A projection matrix in the active profile.
+struct Mat {
+    int rows = 0, cols = 0;
+    float* f = nullptr;    // F32 [rows][cols]
+    int8_t* q = nullptr;   // Q8 [rows][cols]
+    float* s = nullptr;    // Q8 scales [rows][cols/64]
+};
+
+struct Layer {
+    float* norm_w = nullptr;
+    float* norm_b = nullptr;
+    Mat in_proj, out_proj;
+    float* conv_t = nullptr;   // [4][di]
+    float* conv_b = nullptr;
+    float* x_proj = nullptr;   // [xr][di]
+    float* dt_w = nullptr;     // [di][dr]
+    float* dt_b = nullptr;
+    float* a_t = nullptr;      // [16][di] = lane_exp(A_log)
+    float* dvec = nullptr;
+};
+
+struct Pool {
+    uint32_t cap = 0;
+    float* conv = nullptr;       // [L][cap][3][di]
+    float* ssm = nullptr;        // [L][cap][16][di]
+    uint32_t* since = nullptr;   // [cap]
+    // per-step scratch, indexed by batch position
+    float* x = nullptr;          // [cap][d]
+    float* act_f = nullptr;      // [cap][di] f32 activations (F32 profile)
+    int8_t* act_q = nullptr;     // [3][cap][di] digit planes (Q8)
+    float* act_e = nullptr;      // [cap][di/64]
+    float* conv_out = nullptr;   // [cap][di]
+    float* z = nullptr;          // [cap][di]
+    float* zp = nullptr;         // [cap][xr]
+    float* logits = nullptr;     // [cap][V]
+    float* red = nullptr;        // [cap][softmax partial slots] (max, sum) pairs
+    uint32_t* rflag = nullptr;   // [cap]
+    uint32_t* d_slots = nullptr;
+    uint32_t* d_tokens = nullptr;
+    uint32_t* h_slots = nullptr;   // pinned
+    uint32_t* h_tokens = nullptr;  // pinned
+    std::vector<uint8_t> seen;
+    std::map<uint64_t, cudaGraphExec_t> graphs;  // captured launch sequences, see graph_key()
+    std::set<uint64_t> eager_done;                 // keys already run once without a graph
+};
+
+struct Model {
+    RbinHeader h{};
+    Profile profile = kF32;
+    int V = 0, d = 0, di = 0, dr = 0, xr = 0, nl = 0;
+    Mat emb, head;
+    bool head_tied = true;
+    float* norm_f_w = nullptr;
+    float* norm_f_b = nullptr;
+    std::vector<Layer> layers;
+    std::vector<void*> allocs;
+    cudaStream_t stream = nullptr;
+    int device = 0;
+    Pool v1, batch;
+    uint32_t reset_every = 0;
+    uint32_t* d_err = nullptr;
+    int proj_path = 0;     // 0 auto, 1 CUDA cores, 2 tensor cores
+    bool use_graphs = true;
+    bool ready = false;
+};
+
+Model G;
+
+// ------------------------------------------------------------------------------------------
+// Allocation helpers
+// ------------------------------------------------------------------------------------------
+
+template <class T>
+bool dalloc(T** p, size_t count, bool zero = true) {
+    *p = nullptr;
+    if (count == 0) count = 1;
+    if (cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T)) != cudaSuccess) {
+        *p = nullptr;
+        return false;
+    }
+    if (zero && cudaMemset(*p, 0, count * sizeof(T)) != cudaSuccess) return false;
+    return true;
+}
+
+template <class T>
+bool model_alloc(T** p, size_t count) {
+    if (!dalloc(p, count)) return false;
+    G.allocs.push_back(*p);
+    return true;
+}
+
+void pool_free(Pool* p) {
+    for (auto& kv : p->graphs) cudaGraphExecDestroy(kv.second);
+    p->graphs.clear();
+    p->eager_done.clear();
+    void* bufs[] = {p->conv, p->ssm, p->since, p->x, p->act_f, p->act_q, p->act_e, p->conv_out, p->z,
+                    p->zp, p->logits, p->red, p->rflag, p->d_slots, p->d_tokens};
+    for (void* b : bufs) cudaFree(b);
+    if (p->h_slots) cudaFreeHost(p->h_slots);
+    if (p->h_tokens) cudaFreeHost(p->h_tokens);
+    *p = Pool();
+}
+
+constexpr int kSoftmaxTile = 2048;  // logits per partial (max, sum) of the probability pass
+
+bool pool_alloc(Pool* p, uint32_t cap) {
+    *p = Pool();
+    p->cap = cap;
+    size_t n = cap, L = G.nl, d = G.d, di = G.di, V = G.V;
+    size_t parts = (V + kSoftmaxTile - 1) / kSoftmaxTile;
+    bool ok = dalloc(&p->conv, L * n * 3 * di) && dalloc(&p->ssm, L * n * kDState * di) &&
+              dalloc(&p->since, n) && dalloc(&p->x, n * d) && dalloc(&p->conv_out, n * di) &&
+              dalloc(&p->z, n * di) && dalloc(&p->zp, n * G.xr) && dalloc(&p->logits, n * V) &&
+              dalloc(&p->red, n * parts * 2) && dalloc(&p->rflag, n) && dalloc(&p->d_slots, n) &&
+              dalloc(&p->d_tokens, n);
+    if (ok) {
+        if (G.profile == kF32) ok = dalloc(&p->act_f, n * di);
+        else ok = dalloc(&p->act_q, 3 * n * di) && dalloc(&p->act_e, n * (di / kGroup));
+    }
+    if (ok) ok = cudaHostAlloc(reinterpret_cast<void**>(&p->h_slots), n * sizeof(uint32_t), cudaHostAllocDefault) ==
+                 cudaSuccess;
+    if (ok) ok = cudaHostAlloc(reinterpret_cast<void**>(&p->h_tokens), n * sizeof(uint32_t), cudaHostAllocDefault) ==
+                 cudaSuccess;
+    p->seen.assign(n, 0);
+    if (!ok) {
+        pool_free(p);
+        return false;
+    }
+    return true;
+}
+
+void free_model() {
+    if (G.stream) cudaStreamSynchronize(G.stream);
+    pool_free(&G.v1);
+    pool_free(&G.batch);
+    for (void* a : G.allocs) cudaFree(a);
+    if (G.d_err) cudaFree(G.d_err);
+    if (G.stream) cudaStreamDestroy(G.stream);
+    G.~Model();
+    new (&G) Model();
+}
+
+// ------------------------------------------------------------------------------------------
+// Weight loading
+// ------------------------------------------------------------------------------------------
+
+struct Reader {
+    FILE* f = nullptr;
+    float* staging = nullptr;  // pinned
+    size_t staging_n = 0;
+    ~Reader() {
+        if (f) fclose(f);
+        if (staging) cudaFreeHost(staging);
+    }
+    // Reads `count` floats into the device buffer `dst`.
+    bool read_to(float* dst, size_t count) {
+        size_t done = 0;
+        while (done < count) {
+            size_t chunk = std::min(staging_n, count - done);
+            if (fread(staging, sizeof(float), chunk, f) != chunk) return false;
+            if (cudaMemcpy(dst + done, staging, chunk * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess)
+                return false;
+            done += chunk;
+        }
+        return true;
+    }
+};
+
+float* g_tmp = nullptr;  // load-time f32 staging on the device (largest matrix)
+
+bool load_f32(Reader& r, float** dst, size_t count) { return model_alloc(dst, count) && r.read_to(*dst, count); }
+
+// Loads a [rows][cols] matrix in the active profile.  Q8: quantised on the device with the
+// reference recipe (group 64, or per-row then broadcast to the 64-column groups).
+bool load_mat(Reader& r, Mat* m, int rows, int cols, bool quantise) {
+    m->rows = rows;
+    m->cols = cols;
+    size_t count = (size_t)rows * cols;
+    if (!quantise || G.profile == kF32) return load_f32(r, &m->f, count);
+    if (!r.read_to(g_tmp, count)) return false;
+    int groups = cols / kGroup;
+    if (!model_alloc(&m->q, count) || !model_alloc(&m->s, (size_t)rows * groups)) return false;
+    if (G.profile == kQ8) {
+        size_t ng = count / kGroup;
+        k_quantize_q8<<<(unsigned)((ng + 7) / 8), 256>>>(g_tmp, ng, kGroup, m->q, m->s);
+    } else {
+        float* row_s = nullptr;
+        if (!dalloc(&row_s, (size_t)rows)) return false;
+        k_quantize_q8<<<(unsigned)((rows + 7) / 8), 256>>>(g_tmp, (size_t)rows, cols, m->q, row_s);
+        size_t tot = (size_t)rows * groups;
+        k_broadcast_scales<<<(unsigned)((tot + 255) / 256), 256>>>(row_s, rows, groups, m->s);
+        cudaDeviceSynchronize();
+        cudaFree(row_s);
+    }
+    return cudaDeviceSynchronize() == cudaSuccess;
+}
+
+int validate_header(const RbinHeader& h) {
+    if (h.magic != kRbinMagic || (h.version != 1 && h.version != 2)) return -1;
+    if (!h.vocab || !h.d || !h.di || !h.nl || !h.dr) return -1;
+    if (h.version == 2 && h.tokenizer > 1) return -1;
+    if (h.version == 2 && h.tokenizer == 0 && h.vocab != 256) return -1;
+    // Engine limits: d_state 16 and d_conv 4 (every Mamba-1 checkpoint redukt ships), d_inner = 2 d,
+    // d a multiple of 64 (Q8 groups, 128-column vector tiles), d_inner <= 2048, dt_rank <= 256.
+    if (h.ds != (uint32_t)kDState || h.dc != (uint32_t)kDConv) return -2;
+    if (h.di != 2 * h.d || h.d % 64 != 0 || h.di > 2048 || h.dr > 256) return -2;
+    if (h.vocab >= (1u << 30)) return -2;
+    return 0;
+}
+
+int load_weights(const char* path) {
+    Reader r;
+    r.f = fopen(path, "rb");
+    if (!r.f) {
+        set_err("cannot open %s", path);
+        return BACKEND_WEIGHTS_NOT_FOUND;
+    }
+    RbinHeader h;
+    if (fread(&h, sizeof(h), 1, r.f) != 1) {
+        set_err("%s: short header", path);
+        return BACKEND_WEIGHTS_NOT_FOUND;
+    }
+    int v = validate_header(h);
+    if (v == -1) {
+        set_err("%s: bad .rbin header", path);
+        return BACKEND_WEIGHTS_NOT_FOUND;
+    }
+    if (v == -2) {
+        set_err("%s: model shape outside engine limits (d_state=%u d_conv=%u d=%u di=%u dr=%u)", path, h.ds, h.dc,
+                h.d, h.di, h.dr);
+        return BACKEND_WEIGHTS_NOT_FOUND;
+    }
+    G.h = h;
+    G.V = (int)h.vocab;
+    G.d = (int)h.d;
+    G.di = (int)h.di;
+    G.dr = (int)h.dr;
+    G.xr = (int)(h.dr + 2 * h.ds);
+    G.nl = (int)h.nl;
+    G.profile = (h.flags & kFlagQ8) ? ((h.flags & kFlagQ8PerRow) ? kQ8Row : kQ8) : kF32;
+    if (const char* e = getenv("REDUKT_B200_PROFILE")) {
+        if (!strcmp(e, "f32")) G.profile = kF32;
+        else if (!strcmp(e, "q8")) G.profile = kQ8;
+        else if (!strcmp(e, "q8row")) G.profile = kQ8Row;
+    }
+    // expected file size
+    size_t d = G.d, di = G.di, V = G.V, xr = G.xr, dr = G.dr;
+    bool nb = h.flags & kFlagNormBias, untied = h.flags & kFlagUntiedHead;
+    size_t per_layer = d * (nb ? 2 : 1) + 2 * di * d + di * kDConv + di + xr * di + di * dr + di + di * kDState +
+                       di + d * di;
+    size_t total = V * d + G.nl * per_layer + d * (nb ? 2 : 1) + (untied ? V * d : 0);
+    fseek(r.f, 0, SEEK_END);
+    long fsz = ftell(r.f);
+    fseek(r.f, (long)sizeof(h), SEEK_SET);
+    if (fsz < 0 || (size_t)fsz != sizeof(h) + total * 4) {
+        set_err("%s: size %ld does not match the header (%zu expected)", path, fsz, sizeof(h) + total * 4);
+        return BACKEND_WEIGHTS_NOT_FOUND;
+    }
+    r.staging_n = (size_t)16 << 20;
+    if (cudaHostAlloc(reinterpret_cast<void**>(&r.staging), r.staging_n * sizeof(float), cudaHostAllocDefault) !=
+        cudaSuccess) {
+        set_err("pinned staging allocation failed");
+        return BACKEND_INIT_FAILED;
+    }
+    if (G.profile != kF32 && !dalloc(&g_tmp, std::max(V * d, 2 * di * d), false)) {
+        set_err("device staging allocation failed");
+        return BACKEND_INIT_FAILED;
+    }
+    bool ok = load_mat(r, &G.emb, G.V, G.d, true);
+    float* a_log = nullptr;
+    float* conv_w = nullptr;
+    ok = ok && dalloc(&a_log, di * kDState, false) && dalloc(&conv_w, di * kDConv, false);
+    G.layers.resize(G.nl);
+    for (int i = 0; ok && i < G.nl; i++) {
+        Layer& L = G.layers[i];
+        ok = load_f32(r, &L.norm_w, d) && (!nb || load_f32(r, &L.norm_b, d)) &&
+             load_mat(r, &L.in_proj, 2 * G.di, G.d, true) && r.read_to(conv_w, di * kDConv) &&
+             load_f32(r, &L.conv_b, di) && load_f32(r, &L.x_proj, xr * di) && load_f32(r, &L.dt_w, di * dr) &&
+             load_f32(r, &L.dt_b, di) && r.read_to(a_log, di * kDState) && load_f32(r, &L.dvec, di) &&
+             load_mat(r, &L.out_proj, G.d, G.di, true);
+        ok = ok && model_alloc(&L.a_t, di * kDState) && model_alloc(&L.conv_t, di * kDConv);
+        if (ok) {
+            k_prep_layer<<<(unsigned)((di + 255) / 256), 256>>>(a_log, conv_w, G.di, L.a_t, L.conv_t);
+            ok = cudaDeviceSynchronize() == cudaSuccess;
+        }
+    }
+    ok = ok && load_f32(r, &G.norm_f_w, d) && (!nb || load_f32(r, &G.norm_f_b, d));
+    G.head_tied = !untied;
+    if (ok && untied) ok = load_mat(r, &G.head, G.V, G.d, true);
+    if (ok && !untied) G.head = G.emb;
+    cudaFree(a_log);
+    cudaFree(conv_w);
+    if (g_tmp) cudaFree(g_tmp);
+    g_tmp = nullptr;
+    if (!ok) {
+        set_err("%s: reading/uploading weights failed (%s)", path, cudaGetErrorString(cudaGetLastError()));
+        return BACKEND_WEIGHTS_NOT_FOUND;
+    }
+    return BACKEND_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Launch helpers
+// ------------------------------------------------------------------------------------------
+
+template <class Kern>
+void allow_smem(Kern k, size_t bytes) {
+    if (bytes > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+template <int RW, int NS, class Epi>
+void gemv_f32_ns(int M, int K, const float* W, const float* act, int ld, int n, Epi epi, cudaStream_t st) {
+    size_t smem = (size_t)NS * K * sizeof(float);
+    auto k = k_gemv_f32<RW, NS, Epi>;
+    allow_smem(k, smem);
+    dim3 grid((n + NS - 1) / NS, (M + 8 * RW - 1) / (8 * RW));
+    k<<<grid, 256, smem, st>>>(M, K, W, act, ld, n, epi);
+}
+
+template <int RW, class Epi>
+void gemv_f32(int M, int K, const float* W, const float* act, int ld, int n, Epi epi, cudaStream_t st) {
+    if (n >= 8) gemv_f32_ns<RW, 8>(M, K, W, act, ld, n, epi, st);
+    else if (n >= 4) gemv_f32_ns<RW, 4>(M, K, W, act, ld, n, epi, st);
+    else if (n >= 2) gemv_f32_ns<RW, 2>(M, K, W, act, ld, n, epi, st);
+    else gemv_f32_ns<RW, 1>(M, K, W, act, ld, n, epi, st);
+}
+
+template <int NS, int GI, class Epi>
+void gemv_q8_ns(const Mat& m, const int8_t* q, const float* e, int cap, int n, Epi epi, cudaStream_t st) {
+    constexpr int RW = 4;
+    int K = m.cols;
+    size_t smem = (size_t)NS * 3 * K + (size_t)NS * (K / kGroup) * sizeof(float);
+    auto k = k_gemv_q8<RW, NS, GI, Epi>;
+    allow_smem(k, smem);
+    dim3 grid((n + NS - 1) / NS, (m.rows + 8 * RW - 1) / (8 * RW));
+    k<<<grid, 256, smem, st>>>(m.rows, K, m.q, m.s, q, e, cap, n, epi);
+}
+
+template <int GI, class Epi>
+void gemv_q8_gi(const Mat& m, const int8_t* q, const float* e, int cap, int n, Epi epi, cudaStream_t st) {
+    if (n >= 8) gemv_q8_ns<8, GI>(m, q, e, cap, n, epi, st);
+    else if (n >= 4) gemv_q8_ns<4, GI>(m, q, e, cap, n, epi, st);
+    else if (n >= 2) gemv_q8_ns<2, GI>(m, q, e, cap, n, epi, st);
+    else gemv_q8_ns<1, GI>(m, q, e, cap, n, epi, st);
+}
+
+template <class Epi>
+void gemv_q8(const Mat& m, const int8_t* q, const float* e, int cap, int n, Epi epi, cudaStream_t st) {
+    int G8 = (m.cols / kGroup + 7) / 8;
+    if (G8 <= 1) gemv_q8_gi<1>(m, q, e, cap, n, epi, st);
+    else if (G8 == 2) gemv_q8_gi<2>(m, q, e, cap, n, epi, st);
+    else if (G8 == 3) gemv_q8_gi<3>(m, q, e, cap, n, epi, st);
+    else gemv_q8_gi<4>(m, q, e, cap, n, epi, st);
+}
+
+template <class Epi>
+void project(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st) {
+    if (G.profile == kF32) {
+        gemv_f32<4>(m.rows, m.cols, m.f, p.act_f, m.cols, n, epi, st);
+    } else {
+        gemv_q8(m, p.act_q, p.act_e, (int)p.cap, n, epi, st);
+    }
+}
+
+void launch_norm(const Pool& p, int n, const float* w, const float* b, int K_out, cudaStream_t st) {
+    ActOut out{p.act_f, p.act_q, p.act_e, (int)p.cap, K_out};
+    if (G.profile != kF32) out.f = nullptr;
+    else out.q = nullptr;
+    dim3 grid((n + 3) / 4);
+    int nc = (G.d + 127) / 128;
+    switch (nc) {
+        case 1: k_norm<1><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
+        case 2: k_norm<2><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
+        case 3: k_norm<3><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
+        case 4: k_norm<4><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
+        case 5: k_norm<5><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
+        case 6: k_norm<6><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
+        case 7: k_norm<7><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
+        default: k_norm<8><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
+    }
+}
+
+// Softmax over each row of `logits` written to `out` (may alias): partial (max, sum exp) per
+// 2048-logit tile, then a fixed-order combine.  exp is the reference's Cephes polynomial.
+__global__ void k_softmax_partial(const float* __restrict__ logits, int V, float* __restrict__ red, int parts) {
+    int b = blockIdx.y, t = blockIdx.x;
+    const float* l = logits + (size_t)b * V;
+    int v0 = t * kSoftmaxTile, v1 = min(V, v0 + kSoftmaxTile);
+    __shared__ float s_m[8], s_s[8];
+    float m = -INFINITY;
+    for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) m = fmaxf(m, l[v]);
+    m = warp_allmax(m);
+    int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) s_m[w] = m;
+    __syncthreads();
+    m = s_m[0];
+    for (int i = 1; i < (int)(blockDim.x >> 5); i++) m = fmaxf(m, s_m[i]);
+    float s = 0.0f;
+    for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) s = __fadd_rn(s, portable_expf(__fsub_rn(l[v], m)));
+    s = warp_allsum(s);
+    if (lane == 0) s_s[w] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float tot = 0.0f;
+        for (int i = 0; i < (int)(blockDim.x >> 5); i++) tot = __fadd_rn(tot, s_s[i]);
+        red[((size_t)b * parts + t) * 2] = m;
+        red[((size_t)b * parts + t) * 2 + 1] = tot;
+    }
+}
+
+__global__ void k_softmax_final(const float* __restrict__ logits, int V, const float* __restrict__ red, int parts,
+                                float* __restrict__ out) {
+    int b = blockIdx.y;
+    const float* rb = red + (size_t)b * parts * 2;
+    float M = -INFINITY;
+    for (int t = 0; t < parts; t++) M = fmaxf(M, rb[2 * t]);
+    float S = 0.0f;
+    for (int t = 0; t < parts; t++) S = __fadd_rn(S, __fmul_rn(rb[2 * t + 1], portable_expf(__fsub_rn(rb[2 * t], M))));
+    const float* l = logits + (size_t)b * V;
+    float* o = out + (size_t)b * V;
+    for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < V; v += gridDim.x * blockDim.x)
+        o[v] = __fdiv_rn(portable_expf(__fsub_rn(l[v], M)), S);
+}
+
+// Enqueues one decode step for n streams whose slots/tokens are already on the device.
+int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_tokens, float* d_out, bool probs,
+                 cudaStream_t st) {
+    StepArgs sa{n, (int)p.cap, d_slots, d_tokens, p.rflag, p.since, G.reset_every, G.d_err};
+    const Mat& emb = G.emb;
+    k_embed<<<n, 256, 0, st>>>(sa, emb.f, emb.q, emb.s, G.d, G.V, p.x);
+    for (int li = 0; li < G.nl; li++) {
+        const Layer& L = G.layers[li];
+        launch_norm(p, n, L.norm_w, L.norm_b, G.d, st);
+        EpiInProj ein{G.di, (int)p.cap, li, d_slots, p.rflag, p.conv, L.conv_t, L.conv_b, p.conv_out, p.z};
+        project(L.in_proj, p, n, ein, st);
+        gemv_f32<1>(G.xr, G.di, L.x_proj, p.conv_out, G.di, n, EpiStore{p.zp, G.xr}, st);
+        ScanArgs sc{G.di, G.dr, G.xr, (int)p.cap, li, d_slots, p.rflag, p.zp, p.conv_out, p.z,
+                    L.dt_w, L.dt_b, L.a_t, L.dvec, p.ssm};
+        ActOut ao{p.act_f, p.act_q, p.act_e, (int)p.cap, G.di};
+        if (G.profile != kF32) ao.f = nullptr;
+        else ao.q = nullptr;
+        k_scan<<<dim3((G.di + 255) / 256, n), 256, G.xr * sizeof(float), st>>>(sc, ao);
+        project(L.out_proj, p, n, EpiResidual{p.x, G.d}, st);
+    }
+    launch_norm(p, n, G.norm_f_w, G.norm_f_b, G.d, st);
+    float* lo = probs ? p.logits : d_out;
+    project(G.head, p, n, EpiStore{lo, G.V}, st);
+    if (probs) {
+        int parts = (G.V + kSoftmaxTile - 1) / kSoftmaxTile;
+        k_softmax_partial<<<dim3(parts, n), 256, 0, st>>>(lo, G.V, p.red, parts);
+        k_softmax_final<<<dim3(std::max(1, std::min(64, G.V / 1024)), n), 256, 0, st>>>(lo, G.V, p.red, parts,
+                                                                                       d_out);
+    }
+    CK(cudaGetLastError(), BACKEND_FORWARD_FAILED);
+    return BACKEND_OK;
+}
+
+uint64_t graph_key(int n, bool probs) {
+    return (uint64_t)n | ((uint64_t)probs << 13) | ((uint64_t)G.proj_path << 14) | ((uint64_t)G.reset_every << 16);
+}
+
+// Enqueue one step for this pool's fixed buffers.  The first call for a (n, probs, options)
+// key runs eagerly (it also sets every kernel attribute); later calls replay a CUDA graph of the
+// same launch sequence captured on the second call.
+int enqueue_pool_step(Pool& p, int n, bool probs) {
+    float* out = p.logits;
+    uint64_t key = graph_key(n, probs);
+    if (!G.use_graphs || !p.eager_done.count(key)) {
+        int rc = enqueue_step(p, n, p.d_slots, p.d_tokens, out, probs, G.stream);
+        if (rc == BACKEND_OK) p.eager_done.insert(key);
+        return rc;
+    }
+    auto it = p.graphs.find(key);
+    if (it == p.graphs.end()) {
+        cudaGraph_t graph = nullptr;
+        CK(cudaStreamBeginCapture(G.stream, cudaStreamCaptureModeThreadLocal), BACKEND_FORWARD_FAILED);
+        int rc = enqueue_step(p, n, p.d_slots, p.d_tokens, out, probs, G.stream);
+        cudaError_t e = cudaStreamEndCapture(G.stream, &graph);
+        if (rc != BACKEND_OK) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        CK(e, BACKEND_FORWARD_FAILED);
+        cudaGraphExec_t exec = nullptr;
+        e = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        CK(e, BACKEND_FORWARD_FAILED);
+        it = p.graphs.emplace(key, exec).first;
+    }
+    CK(cudaGraphLaunch(it->second, G.stream), BACKEND_FORWARD_FAILED);
+    return BACKEND_OK;
+}
+
+// Validates, uploads slots/tokens, runs the step and copies logits or probabilities to `out`
+// (mamba_cuda.cu:604-635 semantics: INVALID_ARGUMENT before any launch, synchronous return).
+int pool_forward(Pool& p, uint32_t n, const uint32_t* slots, const uint32_t* tokens, float* out, bool probs) {
+    std::fill(p.seen.begin(), p.seen.end(), 0);
+    for (uint32_t b = 0; b < n; b++) {
+        if (slots[b] >= p.cap || p.seen[slots[b]] || tokens[b] >= (uint32_t)G.V) return BACKEND_INVALID_ARGUMENT;
+        p.seen[slots[b]] = 1;
+        p.h_slots[b] = slots[b];
+        p.h_tokens[b] = tokens[b];
+    }
+    size_t ib = (size_t)n * sizeof(uint32_t);
+    CK(cudaMemcpyAsync(p.d_slots, p.h_slots, ib, cudaMemcpyHostToDevice, G.stream), BACKEND_FORWARD_FAILED);
+    CK(cudaMemcpyAsync(p.d_tokens, p.h_tokens, ib, cudaMemcpyHostToDevice, G.stream), BACKEND_FORWARD_FAILED);
+    int rc = enqueue_pool_step(p, (int)n, probs);
+    if (rc != BACKEND_OK) return rc;
+    CK(cudaMemcpyAsync(out, p.logits, (size_t)n * G.V * sizeof(float), cudaMemcpyDeviceToHost, G.stream),
+       BACKEND_FORWARD_FAILED);
+    CK(cudaStreamSynchronize(G.stream), BACKEND_FORWARD_FAILED);
+    return BACKEND_OK;
+}
+
+int pool_reset(Pool& p, const uint32_t* slots, uint32_t n) {
+    if (!slots) {
+        size_t L = G.nl, cap = p.cap, di = G.di;
+        CK(cudaMemsetAsync(p.conv, 0, L * cap * 3 * di * sizeof(float), G.stream), BACKEND_FORWARD_FAILED);
+        CK(cudaMemsetAsync(p.ssm, 0, L * cap * kDState * di * sizeof(float), G.stream), BACKEND_FORWARD_FAILED);
+        CK(cudaMemsetAsync(p.since, 0, cap * sizeof(uint32_t), G.stream), BACKEND_FORWARD_FAILED);
+        CK(cudaStreamSynchronize(G.stream), BACKEND_FORWARD_FAILED);
+        return BACKEND_OK;
+    }
+    for (uint32_t b = 0; b < n; b++) {
+        if (slots[b] >= p.cap) return BACKEND_INVALID_ARGUMENT;
+        p.h_slots[b] = slots[b];
+    }
+    if (n == 0) return BACKEND_OK;
+    CK(cudaMemcpyAsync(p.d_slots, p.h_slots, (size_t)n * sizeof(uint32_t), cudaMemcpyHostToDevice, G.stream),
+       BACKEND_FORWARD_FAILED);
+    int per = (3 + kDState) * G.di;
+    k_zero_slots<<<dim3((per + 255) / 256, n, G.nl), 256, 0, G.stream>>>(p.d_slots, (int)n, (int)p.cap, G.nl, G.di,
+                                                                         p.conv, p.ssm, p.since);
+    CK(cudaGetLastError(), BACKEND_FORWARD_FAILED);
+    CK(cudaStreamSynchronize(G.stream), BACKEND_FORWARD_FAILED);
+    return BACKEND_OK;
+}
+
+std::string rbin_path(const uint8_t* weights_path) {
+    std::string p(reinterpret_cast<const char*>(weights_path));
+    if (p.size() < 5 || p.compare(p.size() - 5, 5, ".rbin") != 0) p += "/model.rbin";
+    return p;
+}
+
+}  // namespace
+
+// ==========================================================================================
+// C ABI
+// ==========================================================================================
+extern "C" {
+
+BackendResult redukt_backend_init(const uint8_t* weights_path, int32_t device_id, BackendInfo* info_out) {
+    if (!weights_path || !info_out) return BACKEND_INIT_FAILED;
+    if (G.ready || G.stream) free_model();
+    g_err[0] = 0;
+    std::string path = rbin_path(weights_path);
+    G.device = device_id >= 0 ? device_id : 0;
+    if (cudaSetDevice(G.device) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&G.stream, cudaStreamNonBlocking) != cudaSuccess) {
+        set_err("no CUDA device %d (%s)", G.device, cudaGetErrorString(cudaGetLastError()));
+        free_model();
+        return BACKEND_INIT_FAILED;
+    }
+    int maj = 0, min = 0;
+    cudaDeviceGetAttribute(&maj, cudaDevAttrComputeCapabilityMajor, G.device);
+    cudaDeviceGetAttribute(&min, cudaDevAttrComputeCapabilityMinor, G.device);
+    if (maj != 10 || min != 0) {
+        set_err("device %d is sm_%d%d; this library is built for sm_100a (B200) only", G.device, maj, min);
+        free_model();
+        return BACKEND_INIT_FAILED;
+    }
+    int rc = load_weights(path.c_str());
+    if (rc != BACKEND_OK) {
+        free_model();
+        return (BackendResult)rc;
+    }
+    if (!dalloc(&G.d_err, 1) || !pool_alloc(&G.v1, 1)) {
+        set_err("device allocation failed");
+        free_model();
+        return BACKEND_INIT_FAILED;
+    }
+    if (const char* e = getenv("REDUKT_B200_GRAPHS")) G.use_graphs = atoi(e) != 0;
+    if (const char* e = getenv("REDUKT_B200_PROJ")) G.proj_path = atoi(e);
+    G.ready = true;
+    memset(info_out, 0, sizeof(*info_out));
+    info_out->ffi_version = BACKEND_FFI_VERSION;
+    info_out->vocab_size = (uint32_t)G.V;
+    info_out->hidden_dim = (uint32_t)G.d;
+    const char* name = G.profile == kF32 ? "b200-mamba-f32" : (G.profile == kQ8 ? "b200-mamba-q8" : "b200-mamba-q8row");
+    memcpy(info_out->name, name, strlen(name));
+    return BACKEND_OK;
+}
+
+BackendResult redukt_backend_forward(uint32_t token, float* out_logits, uint32_t vocab_size) {
+    if (!G.ready || !out_logits || vocab_size != (uint32_t)G.V) return BACKEND_FORWARD_FAILED;
+    uint32_t slot = 0;
+    int rc = pool_forward(G.v1, 1, &slot, &token, out_logits, false);
+    return rc == BACKEND_OK ? BACKEND_OK : BACKEND_FORWARD_FAILED;
+}
+
+void redukt_backend_reset_state(void) {
+    if (!G.ready) return;
+    uint32_t slot = 0;
+    if (pool_reset(G.v1, &slot, 1) != BACKEND_OK) fprintf(stderr, "[redukt-b200] reset_state failed\n");
+}
+
+void redukt_backend_free(void) { free_model(); }
+
+uint32_t redukt_backend_abi_version(void) { return BACKEND_ABI_VERSION; }
+
+int32_t redukt_backend_batch_init(uint32_t max_streams) {
+    if (!G.ready) return BACKEND_INIT_FAILED;
+    if (max_streams > kMaxStreams) return BACKEND_INVALID_ARGUMENT;
+    CK(cudaStreamSynchronize(G.stream), BACKEND_INIT_FAILED);
+    pool_free(&G.batch);
+    if (max_streams == 0) return BACKEND_OK;
+    if (!pool_alloc(&G.batch, max_streams)) {
+        set_err("batch pool of %u streams: device allocation failed", max_streams);
+        return BACKEND_INIT_FAILED;
+    }
+    return BACKEND_OK;
+}
+
+int32_t redukt_backend_batch_reset(const uint32_t* slots, uint32_t n_slots) {
+    if (!G.ready || G.batch.cap == 0) return BACKEND_INIT_FAILED;
+    if (slots && n_slots > G.batch.cap) return BACKEND_INVALID_ARGUMENT;
+    return pool_reset(G.batch, slots, n_slots);
+}
+
+static int32_t forward_batch_impl(uint32_t n, const uint32_t* slots, const uint32_t* tokens, float* out,
+                                  uint32_t vocab, bool probs) {
+    if (!G.ready || G.batch.cap == 0) return BACKEND_INIT_FAILED;
+    if (vocab != (uint32_t)G.V || n > G.batch.cap) return BACKEND_INVALID_ARGUMENT;
+    if (n == 0) return BACKEND_OK;
+    if (!slots || !tokens || !out) return BACKEND_INVALID_ARGUMENT;
+    return pool_forward(G.batch, n, slots, tokens, out, probs);
+}
+
+int32_t redukt_backend_forward_batch(uint32_t n_streams, const uint32_t* slots, const uint32_t* tokens,
+                                     float* out_logits, uint32_t vocab_size) {
+    return forward_batch_impl(n_streams, slots, tokens, out_logits, vocab_size, false);
+}
+
+int32_t redukt_backend_forward_batch_probs(uint32_t n_streams, const uint32_t* slots, const uint32_t* tokens,
+                                           float* out_probs, uint32_t vocab_size) {
+    return forward_batch_impl(n_streams, slots, tokens, out_probs, vocab_size, true);
+}
+
+int32_t redukt_backend_set_reset_every(uint32_t every) {
+    if (!G.ready) return BACKEND_INIT_FAILED;
+    if (every > (1u << 31)) return BACKEND_INVALID_ARGUMENT;
+    G.reset_every = every;
+    return BACKEND_OK;
+}
+
+int32_t redukt_b200_forward_batch_device(uint32_t n, const uint32_t* d_slots, const uint32_t* d_tokens, float* d_out,
+                                         uint32_t vocab, int32_t probs, void* cuda_stream) {
+    if (!G.ready || G.batch.cap == 0) return BACKEND_INIT_FAILED;
+    if (vocab != (uint32_t)G.V || n > G.batch.cap) return BACKEND_INVALID_ARGUMENT;
+    if (n == 0) return BACKEND_OK;
+    if (!d_slots || !d_tokens || !d_out) return BACKEND_INVALID_ARGUMENT;
+    cudaStream_t st = cuda_stream ? reinterpret_cast<cudaStream_t>(cuda_stream) : G.stream;
+    return enqueue_step(G.batch, (int)n, d_slots, d_tokens, d_out, probs != 0, st);
+}
+
+int32_t redukt_b200_device_error(uint32_t* out_word) {
+    if (!G.ready) return BACKEND_INIT_FAILED;
+    uint32_t w = 0;
+    CK(cudaStreamSynchronize(G.stream), BACKEND_FORWARD_FAILED);
+    CK(cudaMemcpy(&w, G.d_err, sizeof(w), cudaMemcpyDeviceToHost), BACKEND_FORWARD_FAILED);
+    CK(cudaMemset(G.d_err, 0, sizeof(uint32_t)), BACKEND_FORWARD_FAILED);
+    if (out_word) *out_word = w;
+    return BACKEND_OK;
+}
+
+int32_t redukt_b200_get_state(uint32_t slot, float* conv, float* ssm) {
+    if (!G.ready) return BACKEND_INIT_FAILED;
+    Pool* p = &G.batch;
+    if (slot == 0xffffffffu) {
+        p = &G.v1;
+        slot = 0;
+    }
+    if (slot >= p->cap) return BACKEND_INVALID_ARGUMENT;
+    CK(cudaStreamSynchronize(G.stream), BACKEND_FORWARD_FAILED);
+    size_t di = G.di, cap = p->cap;
+    std::vector<float> tmp((size_t)kDState * di);
+    for (int l = 0; l < G.nl; l++) {
+        if (conv) {
+            CK(cudaMemcpy(tmp.data(), p->conv + (((size_t)l * cap + slot) * 3) * di, 3 * di * sizeof(float),
+                          cudaMemcpyDeviceToHost), BACKEND_FORWARD_FAILED);
+            for (size_t j = 0; j < di; j++)
+                for (int k = 0; k < 3; k++) conv[((size_t)l * di + j) * 3 + k] = tmp[k * di + j];
+        }
+        if (ssm) {
+            CK(cudaMemcpy(tmp.data(), p->ssm + (((size_t)l * cap + slot) * kDState) * di,
+                          (size_t)kDState * di * sizeof(float), cudaMemcpyDeviceToHost), BACKEND_FORWARD_FAILED);
+            for (size_t j = 0; j < di; j++)
+                for (int k = 0; k < kDState; k++) ssm[((size_t)l * di + j) * kDState + k] = tmp[k * di + j];
+        }
+    }
+    return BACKEND_OK;
+}
+
+int32_t redukt_b200_get_q8(int32_t which, uint32_t layer, int8_t* q, float* scales) {
+    if (!G.ready) return BACKEND_INIT_FAILED;
+    if (G.profile == kF32) return BACKEND_INVALID_ARGUMENT;
+    const Mat* m = nullptr;
+    if (which == 0) m = &G.emb;
+    else if (which == 1) m = &G.head;
+    else if ((which == 2 || which == 3) && layer < (uint32_t)G.nl)
+        m = which == 2 ? &G.layers[layer].in_proj : &G.layers[layer].out_proj;
+    if (!m) return BACKEND_INVALID_ARGUMENT;
+    size_t count = (size_t)m->rows * m->cols;
+    if (q) CK(cudaMemcpy(q, m->q, count, cudaMemcpyDeviceToHost), BACKEND_FORWARD_FAILED);
+    if (scales)
+        CK(cudaMemcpy(scales, m->s, (size_t)m->rows * (m->cols / kGroup) * sizeof(float), cudaMemcpyDeviceToHost),
+           BACKEND_FORWARD_FAILED);
+    return BACKEND_OK;
+}
+
+int32_t redukt_b200_info(uint32_t* out, uint32_t n) {
+    if (!G.ready) return BACKEND_INIT_FAILED;
+    uint32_t v[12] = {(uint32_t)G.V, (uint32_t)G.d, (uint32_t)G.di, G.h.ds, G.h.dc, (uint32_t)G.dr, (uint32_t)G.nl,
+                      G.h.flags, (uint32_t)G.profile, G.batch.cap, G.reset_every, (uint32_t)G.proj_path};
+    for (uint32_t i = 0; i < n && i < 12; i++) out[i] = v[i];
+    return BACKEND_OK;
+}
+
+int32_t redukt_b200_set_option(const char* key, int64_t value) {
+    if (!key) return BACKEND_INVALID_ARGUMENT;
+    if (!strcmp(key, "proj_path")) {
+        if (value < 0 || value > 1) return BACKEND_INVALID_ARGUMENT;
+        G.proj_path = (int)value;
+        return BACKEND_OK;
+    }
+    if (!strcmp(key, "graphs")) {
+        G.use_graphs = value != 0;
+        return BACKEND_OK;
+    }
+    return BACKEND_INVALID_ARGUMENT;
+}
+
+const char* redukt_b200_last_error(void) { return g_err; }
+
+}  // extern "C"

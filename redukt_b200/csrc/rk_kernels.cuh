@@ -1,0 +1,545 @@
+// CUDA-core kernels of the Mamba-1 decode step (sm_100a).
+//
+// Step for n lockstep streams (reference: MambaModel::forward_multi,
+// src/infrastructure/mamba/model.rs:773-935; plugin pool_forward, mamba_cuda.cu:604-635):
+//   k_embed      token -> x (Q8: dequantised row), periodic-reset flag per stream
+//   per layer:
+//     k_norm       RMSNorm/LayerNorm of x -> f32 activation or Q8 digit planes
+//     in_proj      GEMV (f32 or Q8) whose epilogue runs the causal conv1d + SiLU on the
+//                  x-branch rows (updating the conv state) and stores the z-branch
+//     x_proj       f32 GEMV -> (dt_raw, B, C)
+//     k_scan       dt_proj + softplus + selective state update + D skip + z gate, emitting the
+//                  next projection's activation (f32 or digit planes)
+//     out_proj     GEMV whose epilogue adds the residual
+//   k_norm (final) + head GEMV -> logits
+//
+// Layouts in HBM (all row-major):
+//   weights      f32 [rows][K] or int8 [rows][K] + f32 scales [rows][K/64]
+//   conv state   f32 [layer][slot][dc-1][d_inner]   (channel fastest: coalesced per tap)
+//   ssm state    f32 [layer][slot][d_state][d_inner]
+//   activations  f32 [stream][K], or int8 digit planes [3][stream][K] + f32 2^e [stream][K/64]
+#pragma once
+#include "rk_math.cuh"
+
+namespace rk {
+
+constexpr int kDState = 16;
+constexpr int kDConv = 4;
+constexpr int kGroup = 64;
+
+// ------------------------------------------------------------------------------------------
+// Load-time kernels
+// ------------------------------------------------------------------------------------------
+
+// Q8wMatrix::quantize (src/domain/gemv.rs:256-273): one warp per group of `group` consecutive
+// floats; scale = max|w| / 127 (1 for an all-zero group), q = clamp(round(w * (1/scale))).
+// roundf rounds half away from zero like Rust's f32::round.
+__global__ void k_quantize_q8(const float* __restrict__ w, size_t n_groups, int group, int8_t* __restrict__ q,
+                              float* __restrict__ scales) {
+    size_t gi = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    int lane = threadIdx.x & 31;
+    if (gi >= n_groups) return;
+    const float* wg = w + gi * group;
+    float amax = 0.0f;
+    for (int i = lane; i < group; i += 32) amax = fmaxf(amax, fabsf(wg[i]));
+    amax = warp_allmax(amax);
+    float scale = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+    float inv = __fdiv_rn(1.0f, scale);
+    for (int i = lane; i < group; i += 32) {
+        float r = roundf(__fmul_rn(wg[i], inv));
+        r = fminf(fmaxf(r, -127.0f), 127.0f);
+        q[gi * group + i] = (int8_t)(int)r;
+    }
+    if (lane == 0) scales[gi] = scale;
+}
+
+// Per-row scales broadcast to every 64-column group, so one kernel serves both Q8 variants.
+__global__ void k_broadcast_scales(const float* __restrict__ row_scale, int rows, int groups,
+                                   float* __restrict__ out) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (size_t)rows * groups) out[i] = row_scale[i / groups];
+}
+
+// A = exp(A_log) as the reference's lane_expf computes it (tensor.rs:1314), stored [16][di];
+// conv weights transposed to [dc][di].
+__global__ void k_prep_layer(const float* __restrict__ a_log, const float* __restrict__ conv_w, int di,
+                             float* __restrict__ a_t, float* __restrict__ conv_t) {
+    int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= di) return;
+#pragma unroll
+    for (int n = 0; n < kDState; n++) a_t[n * di + j] = lane_expf(a_log[j * kDState + n]);
+#pragma unroll
+    for (int k = 0; k < kDConv; k++) conv_t[k * di + j] = conv_w[j * kDConv + k];
+}
+
+// ------------------------------------------------------------------------------------------
+// Per-step kernels
+// ------------------------------------------------------------------------------------------
+
+struct StepArgs {
+    int n;                        // streams in this step
+    int cap;                      // pool capacity (slots)
+    const uint32_t* slots;        // [n] device
+    const uint32_t* tokens;       // [n] device
+    uint32_t* rflag;              // [n] 1 = this stream's state restarts from zero this step
+    uint32_t* since;              // [cap] forwards since the slot's last reset
+    uint32_t reset_every;         // 0 = never (host-driven resets only)
+    uint32_t* err;                // device error word (bad slot/token seen on device)
+};
+
+// Embedding row + the periodic reset decision (MambaState::maybe_periodic_reset,
+// src/infrastructure/mamba/model.rs:315-320): reset when since >= every, then since += 1.
+// The state itself is never written here: every conv/scan read of a flagged stream uses zeros.
+__global__ void k_embed(StepArgs a, const float* __restrict__ emb_f, const int8_t* __restrict__ emb_q,
+                        const float* __restrict__ emb_s, int d, int vocab, float* __restrict__ x) {
+    int b = blockIdx.x;
+    if (b >= a.n) return;
+    uint32_t tok = a.tokens[b], slot = a.slots[b];
+    bool bad = tok >= (uint32_t)vocab || slot >= (uint32_t)a.cap;
+    if (threadIdx.x == 0) {
+        if (bad) {
+            atomicOr(a.err, 1u);
+            a.rflag[b] = 1u;
+        } else {
+            uint32_t s = a.since[slot];
+            uint32_t rf = (a.reset_every > 0 && s >= a.reset_every) ? 1u : 0u;
+            a.since[slot] = rf ? 1u : (s == 0xffffffffu ? s : s + 1u);
+            a.rflag[b] = rf;
+        }
+    }
+    float* xb = x + (size_t)b * d;
+    if (bad) {
+        for (int j = threadIdx.x; j < d; j += blockDim.x) xb[j] = 0.0f;
+        return;
+    }
+    if (emb_q) {  // dequant_row_into (src/domain/gemv.rs:284-295): q * scale
+        const int8_t* qr = emb_q + (size_t)tok * d;
+        const float* sr = emb_s + (size_t)tok * (d / kGroup);
+        for (int j = threadIdx.x; j < d; j += blockDim.x) xb[j] = __fmul_rn((float)qr[j], sr[j / kGroup]);
+    } else {
+        const float* er = emb_f + (size_t)tok * d;
+        for (int j = threadIdx.x; j < d; j += blockDim.x) xb[j] = er[j];
+    }
+}
+
+// Activation sink of a norm / scan: f32 vector or the three Q8 digit planes.
+struct ActOut {
+    float* f;       // [cap][K] f32, or nullptr
+    int8_t* q;      // [3][cap][K] digit planes, or nullptr
+    float* e;       // [cap][K/64] group scales 2^e
+    int cap;        // plane stride in streams
+    int K;
+};
+
+// Norm of one stream per warp (layer_norm_step, src/infrastructure/mamba/model.rs:193-200).
+// Lane l owns columns 128c + 4l .. 128c + 4l + 3; sums are sequential per lane, then a butterfly.
+// RMSNorm: x * (1 / sqrt(sum(x^2)/d + eps)) * w; LayerNorm: (x - mean) * inv_std * w + b.
+template <int NC>  // NC = d / 128 rounded up; d <= 128 * NC
+__global__ void k_norm(int n, const float* __restrict__ x, int d, const float* __restrict__ w,
+                       const float* __restrict__ bias, ActOut out) {
+    int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    int lane = threadIdx.x & 31;
+    if (b >= n) return;
+    const float* xb = x + (size_t)b * d;
+    float4 v[NC];
+#pragma unroll
+    for (int c = 0; c < NC; c++) {
+        int k = c * 128 + lane * 4;
+        v[c] = k < d ? *reinterpret_cast<const float4*>(xb + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float mean = 0.0f, inv;
+    if (bias) {
+        float s = 0.0f;
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            s = __fadd_rn(s, v[c].x); s = __fadd_rn(s, v[c].y); s = __fadd_rn(s, v[c].z); s = __fadd_rn(s, v[c].w);
+        }
+        s = warp_allsum(s);
+        mean = __fdiv_rn(s, (float)d);
+        float q = 0.0f;
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            int k = c * 128 + lane * 4;
+            if (k < d) {
+                float t;
+                t = __fsub_rn(v[c].x, mean); q = __fmaf_rn(t, t, q);
+                t = __fsub_rn(v[c].y, mean); q = __fmaf_rn(t, t, q);
+                t = __fsub_rn(v[c].z, mean); q = __fmaf_rn(t, t, q);
+                t = __fsub_rn(v[c].w, mean); q = __fmaf_rn(t, t, q);
+            }
+        }
+        q = warp_allsum(q);
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(q, (float)d), 1e-5f)));
+    } else {
+        float q = 0.0f;
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            q = __fmaf_rn(v[c].x, v[c].x, q); q = __fmaf_rn(v[c].y, v[c].y, q);
+            q = __fmaf_rn(v[c].z, v[c].z, q); q = __fmaf_rn(v[c].w, v[c].w, q);
+        }
+        q = warp_allsum(q);
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(q, (float)d), 1e-5f)));
+    }
+#pragma unroll
+    for (int c = 0; c < NC; c++) {
+        int k = c * 128 + lane * 4;
+        bool ok = k < d;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (ok) {
+            float4 wv = *reinterpret_cast<const float4*>(w + k);
+            if (bias) {
+                float4 bv = *reinterpret_cast<const float4*>(bias + k);
+                o.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[c].x, mean), inv), wv.x), bv.x);
+                o.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[c].y, mean), inv), wv.y), bv.y);
+                o.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[c].z, mean), inv), wv.z), bv.z);
+                o.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[c].w, mean), inv), wv.w), bv.w);
+            } else {
+                o.x = __fmul_rn(__fmul_rn(v[c].x, inv), wv.x);
+                o.y = __fmul_rn(__fmul_rn(v[c].y, inv), wv.y);
+                o.z = __fmul_rn(__fmul_rn(v[c].z, inv), wv.z);
+                o.w = __fmul_rn(__fmul_rn(v[c].w, inv), wv.w);
+            }
+        }
+        if (out.f) {
+            if (ok) *reinterpret_cast<float4*>(out.f + (size_t)b * out.K + k) = o;
+        } else {
+            // 64-column groups: lanes 0-15 hold group 2c, lanes 16-31 group 2c+1.
+            float m = fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w)));
+            m = warp_allmax(m, 16);
+            float ginv, gs = group_scale(m, &ginv);
+            if (ok) {
+                Digits3 a0 = split_digits(o.x, ginv), a1 = split_digits(o.y, ginv);
+                Digits3 a2 = split_digits(o.z, ginv), a3 = split_digits(o.w, ginv);
+                size_t plane = (size_t)out.cap * out.K;
+                int8_t* base = out.q + (size_t)b * out.K + k;
+                *reinterpret_cast<int*>(base) = pack4(a0.d1, a1.d1, a2.d1, a3.d1);
+                *reinterpret_cast<int*>(base + plane) = pack4(a0.d2, a1.d2, a2.d2, a3.d2);
+                *reinterpret_cast<int*>(base + 2 * plane) = pack4(a0.d3, a1.d3, a2.d3, a3.d3);
+                if ((lane & 15) == 0) out.e[(size_t)b * (out.K / kGroup) + (k / kGroup)] = gs;
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// GEMV epilogues: called once per (row, stream) with the finished dot product.
+// ------------------------------------------------------------------------------------------
+
+struct EpiStore {  // out[b][row] = v
+    float* out;
+    int ld;
+    __device__ __forceinline__ void operator()(int row, int b, float v) const { out[(size_t)b * ld + row] = v; }
+};
+
+struct EpiResidual {  // x[b][row] += v (src/infrastructure/mamba/model.rs:716-719)
+    float* x;
+    int ld;
+    __device__ __forceinline__ void operator()(int row, int b, float v) const {
+        float* p = x + (size_t)b * ld + row;
+        *p = __fadd_rn(*p, v);
+    }
+};
+
+// in_proj epilogue: rows [0, di) are the x-branch, fed straight into the causal conv1d + SiLU
+// (conv_silu_block, src/infrastructure/mamba/model.rs:134-153: val = sum_k st[k]*w[k] + x*w[3]
+// + b, shift, SiLU); rows [di, 2di) are the gate z.
+struct EpiInProj {
+    int di, cap, layer;
+    const uint32_t* slots;
+    const uint32_t* rflag;
+    float* conv_state;        // [layer][slot][3][di]
+    const float* conv_t;      // [4][di]
+    const float* conv_b;      // [di]
+    float* conv_out;          // [stream][di]
+    float* z;                 // [stream][di]
+    __device__ __forceinline__ void operator()(int row, int b, float v) const {
+        if (row >= di) {
+            z[(size_t)b * di + (row - di)] = v;
+            return;
+        }
+        int j = row;
+        uint32_t slot = slots[b];
+        if (slot >= (uint32_t)cap) return;  // rejected stream (device-side check in k_embed)
+        float* st = conv_state + (((size_t)layer * cap + slot) * 3) * di + j;
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+        if (!rflag[b]) {
+            s0 = st[0];
+            s1 = st[di];
+            s2 = st[2 * di];
+        }
+        float val = __fadd_rn(0.0f, __fmul_rn(s0, conv_t[j]));
+        val = __fadd_rn(val, __fmul_rn(s1, conv_t[di + j]));
+        val = __fadd_rn(val, __fmul_rn(s2, conv_t[2 * di + j]));
+        val = __fadd_rn(val, __fmul_rn(v, conv_t[3 * di + j]));
+        val = __fadd_rn(val, conv_b[j]);
+        st[0] = s1;
+        st[di] = s2;
+        st[2 * di] = v;
+        conv_out[(size_t)b * di + j] = __fmul_rn(val, lane_sigmoid(val));
+    }
+};
+
+// ------------------------------------------------------------------------------------------
+// F32 GEMV: y[b][r] = W[r] . act[b].  Per (row, stream) the recipe is fixed: lane l accumulates
+// columns 128c + 4l + i (c ascending, i = 0..3) with FMA from zero, then a butterfly sum.
+// The CTA tiles (streams x rows); rows within a warp share nothing in their arithmetic.
+// Grid: x = stream tiles (fastest, so CTAs reading the same weight rows run together and the
+// rows come from L2 after the first tile), y = row blocks of 8 * RW rows.
+// ------------------------------------------------------------------------------------------
+template <int RW, int NS, class Epi>
+__global__ void __launch_bounds__(256) k_gemv_f32(int M, int K, const float* __restrict__ W,
+                                                  const float* __restrict__ act, int ld_act, int n, Epi epi) {
+    extern __shared__ float4 smem_f4[];
+    float* xs = reinterpret_cast<float*>(smem_f4);  // [NS][K]
+    int b0 = blockIdx.x * NS;
+    int ns = min(NS, n - b0);
+    int K4 = K >> 2;
+    for (int i = threadIdx.x; i < ns * K4; i += blockDim.x) {
+        int s = i / K4, k4 = i - s * K4;
+        reinterpret_cast<float4*>(xs)[s * K4 + k4] =
+            reinterpret_cast<const float4*>(act + (size_t)(b0 + s) * ld_act)[k4];
+    }
+    __syncthreads();
+    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int r0 = blockIdx.y * (8 * RW) + warp * RW;
+    if (r0 >= M) return;
+    float acc[RW][NS];
+#pragma unroll
+    for (int r = 0; r < RW; r++)
+#pragma unroll
+        for (int s = 0; s < NS; s++) acc[r][s] = 0.0f;
+    int nch = (K + 127) >> 7;
+    for (int c = 0; c < nch; c++) {
+        int k = c * 128 + lane * 4;
+        if (k < K) {
+            float4 wv[RW];
+#pragma unroll
+            for (int r = 0; r < RW; r++)
+                wv[r] = (r0 + r < M) ? __ldg(reinterpret_cast<const float4*>(W + (size_t)(r0 + r) * K + k))
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int s = 0; s < NS; s++) {
+                if (s < ns) {
+                    float4 xv = *reinterpret_cast<const float4*>(xs + s * K + k);
+#pragma unroll
+                    for (int r = 0; r < RW; r++) {
+                        acc[r][s] = __fmaf_rn(wv[r].x, xv.x, acc[r][s]);
+                        acc[r][s] = __fmaf_rn(wv[r].y, xv.y, acc[r][s]);
+                        acc[r][s] = __fmaf_rn(wv[r].z, xv.z, acc[r][s]);
+                        acc[r][s] = __fmaf_rn(wv[r].w, xv.w, acc[r][s]);
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < RW; r++)
+#pragma unroll
+        for (int s = 0; s < NS; s++) acc[r][s] = warp_allsum(acc[r][s]);
+    // spread the epilogue over lanes: lane (r * NS + s) % 32 writes output (r, s)
+#pragma unroll
+    for (int r = 0; r < RW; r++)
+#pragma unroll
+        for (int s = 0; s < NS; s++)
+            if (((r * NS + s) & 31) == lane && s < ns && r0 + r < M) epi(r0 + r, b0 + s, acc[r][s]);
+}
+
+// ------------------------------------------------------------------------------------------
+// Q8 GEMV on CUDA cores (dp4a).  Lane l covers 16 bytes (quarter q = l & 3) of group slot
+// gs = l >> 2; a warp covers 8 groups (512 weight bytes) per load.  The three digit sums of a
+// group are exact int32, reduced across the 4 quarter lanes with integer shuffles; the row then
+// accumulates its groups sequentially, g = 0..G-1, with group_accumulate().  The tensor-core
+// kernel produces the same integers and runs the same combine, hence the same bits.
+// Smem: digit planes of the NS-stream tile [NS][3][K] and group scales [NS][G].
+// ------------------------------------------------------------------------------------------
+template <int RW, int NS, int GI, class Epi>
+__global__ void __launch_bounds__(256) k_gemv_q8(int M, int K, const int8_t* __restrict__ Wq,
+                                                 const float* __restrict__ Ws, const int8_t* __restrict__ actq,
+                                                 const float* __restrict__ acte, int cap, int n, Epi epi) {
+    extern __shared__ float4 smem_f4[];
+    int8_t* dq = reinterpret_cast<int8_t*>(smem_f4);                  // [NS][3][K]
+    float* de = reinterpret_cast<float*>(dq + (size_t)NS * 3 * K);    // [NS][G]
+    const int G = K / kGroup;
+    int b0 = blockIdx.x * NS;
+    int ns = min(NS, n - b0);
+    int K16 = K >> 4;
+    size_t plane = (size_t)cap * K;
+    for (int i = threadIdx.x; i < ns * 3 * K16; i += blockDim.x) {
+        int s = i / (3 * K16), rem = i - s * 3 * K16, p = rem / K16, k16 = rem - p * K16;
+        reinterpret_cast<int4*>(dq)[(s * 3 + p) * K16 + k16] =
+            reinterpret_cast<const int4*>(actq + p * plane + (size_t)(b0 + s) * K)[k16];
+    }
+    for (int i = threadIdx.x; i < ns * G; i += blockDim.x) {
+        int s = i / G, g = i - s * G;
+        de[s * G + g] = acte[(size_t)(b0 + s) * G + g];
+    }
+    __syncthreads();
+    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int gs = lane >> 2, qt = lane & 3;
+    int r0 = blockIdx.y * (8 * RW) + warp * RW;
+#pragma unroll 1
+    for (int r = r0; r < min(r0 + RW, M); r++) {
+        int4 wv[GI];
+#pragma unroll
+        for (int gi = 0; gi < GI; gi++) {
+            int g = gi * 8 + gs;
+            wv[gi] = g < G ? __ldg(reinterpret_cast<const int4*>(Wq + (size_t)r * K + g * kGroup + qt * 16))
+                           : make_int4(0, 0, 0, 0);
+        }
+#pragma unroll 1
+        for (int s = 0; s < ns; s++) {
+            float val[GI];
+#pragma unroll
+            for (int gi = 0; gi < GI; gi++) {
+                int g = gi * 8 + gs;
+                int a1 = 0, a2 = 0, a3 = 0;
+                if (g < G) {
+                    const int8_t* base = dq + (size_t)s * 3 * K + g * kGroup + qt * 16;
+                    int4 x1 = *reinterpret_cast<const int4*>(base);
+                    int4 x2 = *reinterpret_cast<const int4*>(base + K);
+                    int4 x3 = *reinterpret_cast<const int4*>(base + 2 * K);
+                    a1 = __dp4a(wv[gi].x, x1.x, a1); a1 = __dp4a(wv[gi].y, x1.y, a1);
+                    a1 = __dp4a(wv[gi].z, x1.z, a1); a1 = __dp4a(wv[gi].w, x1.w, a1);
+                    a2 = __dp4a(wv[gi].x, x2.x, a2); a2 = __dp4a(wv[gi].y, x2.y, a2);
+                    a2 = __dp4a(wv[gi].z, x2.z, a2); a2 = __dp4a(wv[gi].w, x2.w, a2);
+                    a3 = __dp4a(wv[gi].x, x3.x, a3); a3 = __dp4a(wv[gi].y, x3.y, a3);
+                    a3 = __dp4a(wv[gi].z, x3.z, a3); a3 = __dp4a(wv[gi].w, x3.w, a3);
+                }
+                a1 += __shfl_xor_sync(0xffffffffu, a1, 1); a1 += __shfl_xor_sync(0xffffffffu, a1, 2);
+                a2 += __shfl_xor_sync(0xffffffffu, a2, 1); a2 += __shfl_xor_sync(0xffffffffu, a2, 2);
+                a3 += __shfl_xor_sync(0xffffffffu, a3, 1); a3 += __shfl_xor_sync(0xffffffffu, a3, 2);
+                val[gi] = digit_value(a1, a2, a3);
+            }
+            float acc = 0.0f;
+#pragma unroll
+            for (int gi = 0; gi < GI; gi++) {
+#pragma unroll
+                for (int t = 0; t < 8; t++) {
+                    int g = gi * 8 + t;
+                    float v = __shfl_sync(0xffffffffu, val[gi], t * 4);
+                    if (g < G) acc = group_accumulate(acc, v, __ldg(Ws + (size_t)r * G + g), de[s * G + g]);
+                }
+            }
+            if (lane == (s & 31)) epi(r, b0 + s, acc);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Selective scan for one (stream, channel) per thread (scan_block + ssm_recurrence_d16_scalar,
+// src/infrastructure/mamba/model.rs:174-190, src/domain/tensor.rs:1301-1325):
+//   dt = softplus(dt_proj[j] . dt_raw + dt_bias[j])     (8-lane dot order of f32_rows)
+//   if |dt| >= 1e-6: s[n] = exp(0 - dt*A[n]) * s[n] + (dt*x) * B[n]   (A = exp(A_log))
+//   y = hsum_ssm(s[l]*C[l] + s[l+8]*C[l+8]) + D[j]*x;  gated = y * (z * sigmoid(z))
+// Grid (d_inner / 256, n), 256 threads; the gated vector leaves as f32 or Q8 digit planes.
+// ------------------------------------------------------------------------------------------
+struct ScanArgs {
+    int di, dr, xr, cap, layer;
+    const uint32_t* slots;
+    const uint32_t* rflag;
+    const float* zp;       // [stream][xr] = (dt_raw, B, C)
+    const float* conv_out; // [stream][di]
+    const float* z;        // [stream][di]
+    const float* dt_w;     // [di][dr]
+    const float* dt_b;     // [di]
+    const float* a_t;      // [16][di]
+    const float* dvec;     // [di]
+    float* ssm;            // [layer][slot][16][di]
+};
+
+__global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
+    extern __shared__ float4 smem_f4[];
+    float* zs = reinterpret_cast<float*>(smem_f4);  // [xr]
+    __shared__ float s_max[8];
+    int b = blockIdx.y;
+    int j = blockIdx.x * blockDim.x + threadIdx.x;
+    const float* zpb = a.zp + (size_t)b * a.xr;
+    for (int i = threadIdx.x; i < a.xr; i += blockDim.x) zs[i] = zpb[i];
+    __syncthreads();
+    uint32_t slot = a.slots[b];
+    bool ok = j < a.di && slot < (uint32_t)a.cap;
+    float gated = 0.0f;
+    if (ok) {
+        // dt_proj row in dot_avx2_order: 8 lanes over the 8-aligned body, hsum8, tail
+        const float* wr = a.dt_w + (size_t)j * a.dr;
+        float l[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        int body = a.dr & ~7;
+        for (int c = 0; c < body; c += 8) {
+#pragma unroll
+            for (int t = 0; t < 8; t++) l[t] = __fadd_rn(l[t], __fmul_rn(wr[c + t], zs[c + t]));
+        }
+        float s0 = __fadd_rn(l[0], l[4]), s1 = __fadd_rn(l[1], l[5]), s2 = __fadd_rn(l[2], l[6]),
+              s3 = __fadd_rn(l[3], l[7]);
+        float dt = __fadd_rn(__fadd_rn(s0, s2), __fadd_rn(s1, s3));
+        for (int c = body; c < a.dr; c++) dt = __fadd_rn(dt, __fmul_rn(wr[c], zs[c]));
+        dt = softplus(__fadd_rn(dt, a.dt_b[j]));
+
+        const float* B = zs + a.dr;
+        const float* C = zs + a.dr + kDState;
+        float xv = a.conv_out[(size_t)b * a.di + j];
+        float* st = a.ssm + (((size_t)a.layer * a.cap + slot) * kDState) * a.di + j;
+        float s[kDState];
+        bool fresh = a.rflag[b] != 0;
+#pragma unroll
+        for (int n2 = 0; n2 < kDState; n2++) s[n2] = fresh ? 0.0f : st[(size_t)n2 * a.di];
+        bool update = !(fabsf(dt) < 1e-6f);
+        if (update) {
+            float dtx = __fmul_rn(dt, xv);
+#pragma unroll
+            for (int n2 = 0; n2 < kDState; n2++) {
+                float da = lane_expf(__fsub_rn(0.0f, __fmul_rn(dt, a.a_t[(size_t)n2 * a.di + j])));
+                s[n2] = __fadd_rn(__fmul_rn(da, s[n2]), __fmul_rn(dtx, B[n2]));
+            }
+        }
+        if (update || fresh) {
+#pragma unroll
+            for (int n2 = 0; n2 < kDState; n2++) st[(size_t)n2 * a.di] = s[n2];
+        }
+        float ln[8];
+#pragma unroll
+        for (int t = 0; t < 8; t++) ln[t] = __fadd_rn(__fmul_rn(s[t], C[t]), __fmul_rn(s[t + 8], C[t + 8]));
+        float h0 = __fadd_rn(ln[0], ln[4]), h1 = __fadd_rn(ln[1], ln[5]), h2 = __fadd_rn(ln[2], ln[6]),
+              h3 = __fadd_rn(ln[3], ln[7]);
+        float y = __fadd_rn(__fadd_rn(__fadd_rn(h0, h1), __fadd_rn(h2, h3)), __fmul_rn(a.dvec[j], xv));
+        float zv = a.z[(size_t)b * a.di + j];
+        gated = __fmul_rn(y, __fmul_rn(zv, lane_sigmoid(zv)));
+    }
+    if (out.f) {
+        if (ok) out.f[(size_t)b * out.K + j] = gated;
+        return;
+    }
+    // digit planes over 64-channel groups: two warps per group
+    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float m = warp_allmax(fabsf(gated));
+    if (lane == 0) s_max[warp] = m;
+    __syncthreads();
+    m = fmaxf(s_max[warp & ~1], s_max[warp | 1]);
+    if (!ok) return;
+    float ginv, gs = group_scale(m, &ginv);
+    Digits3 dg = split_digits(gated, ginv);
+    size_t plane = (size_t)out.cap * out.K;
+    int8_t* base = out.q + (size_t)b * out.K + j;
+    base[0] = (int8_t)dg.d1;
+    base[plane] = (int8_t)dg.d2;
+    base[2 * plane] = (int8_t)dg.d3;
+    if ((j & (kGroup - 1)) == 0) out.e[(size_t)b * (out.K / kGroup) + j / kGroup] = gs;
+}
+
+// Zero the conv and SSM state of the listed slots in every layer, and their reset counters.
+__global__ void k_zero_slots(const uint32_t* __restrict__ slots, int n_slots, int cap, int layers, int di,
+                             float* __restrict__ conv, float* __restrict__ ssm, uint32_t* __restrict__ since) {
+    int per = (3 + kDState) * di;
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    int k = blockIdx.y;
+    int layer = blockIdx.z;
+    if (k >= n_slots) return;
+    uint32_t slot = slots[k];
+    if (slot >= (uint32_t)cap) return;
+    if (i < per) {
+        if (i < 3 * di) conv[((size_t)layer * cap + slot) * 3 * di + i] = 0.0f;
+        else ssm[((size_t)layer * cap + slot) * kDState * di + (i - 3 * di)] = 0.0f;
+    }
+    if (i == 0 && layer == 0) since[slot] = 0u;
+}
+
+}  // namespace rk

@@ -1,0 +1,177 @@
+// Device arithmetic shared by every kernel of the decode step.
+//
+// Two rules hold throughout:
+//  * Element-wise math (exp, ln, softplus, sigmoid, the conv tap sum, the SSM update) is the
+//    reference CPU path's own operation sequence written with explicitly rounded IEEE
+//    operations (__fmul_rn, __fadd_rn, __fdiv_rn, __fsqrt_rn), so nvcc cannot contract or
+//    reorder it.  Given the same inputs these produce the reference's bits
+//    (src/domain/tensor.rs:765-861 Cephes exp / musl ln / softplus, :877-891 lane sigmoid).
+//  * Reductions use fixed trees that depend only on the element's own data, never on the
+//    batch size, the batch position or the slot, and no float atomics anywhere.  That is what
+//    makes a stream's logits bit-identical for every n (the determinism contract of
+//    docs/api/PLUGIN-FFI-V2.md section 4).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace rk {
+
+// ---- Cephes exp (tensor.rs:765-794) -------------------------------------------------------
+constexpr float kExpLo = -87.3365447505531f;
+constexpr float kExpHi = 88.3762626647949f;
+
+__device__ __forceinline__ float cephes_exp_core(float x) {
+    const float LOG2E = 1.44269504088896341f;
+    const float LN2_HI = 6.93145751953125E-1f;
+    const float LN2_LO = 1.42860682030941723212E-6f;
+    const float P0 = 1.9875691500E-4f, P1 = 1.3981999507E-3f, P2 = 8.3334519073E-3f;
+    const float P3 = 4.1665795894E-2f, P4 = 1.6666665459E-1f, P5 = 5.0000001201E-1f;
+    float fx = __fmul_rn(x, LOG2E);
+    float nf = rintf(fx);  // round half to even, as the reference's 2^23 magic-constant trick
+    int n = __float2int_rz(nf);
+    float r = __fsub_rn(__fsub_rn(x, __fmul_rn(nf, LN2_HI)), __fmul_rn(nf, LN2_LO));
+    float r2 = __fmul_rn(r, r);
+    float y = P0;
+    y = __fadd_rn(__fmul_rn(y, r), P1);
+    y = __fadd_rn(__fmul_rn(y, r), P2);
+    y = __fadd_rn(__fmul_rn(y, r), P3);
+    y = __fadd_rn(__fmul_rn(y, r), P4);
+    y = __fadd_rn(__fmul_rn(y, r), P5);
+    y = __fadd_rn(__fadd_rn(__fmul_rn(y, r2), r), 1.0f);
+    float pow2n = __int_as_float((int)(((unsigned)(n + 127)) << 23));
+    return __fmul_rn(y, pow2n);
+}
+
+// portable_expf: clamp keeps NaN as NaN.
+__device__ __forceinline__ float portable_expf(float x) {
+    x = x < kExpLo ? kExpLo : (x > kExpHi ? kExpHi : x);
+    return cephes_exp_core(x);
+}
+
+// lane_expf (tensor.rs:877-879): one lane of the SIMD exp, a NaN lane becomes exp(kExpLo).
+__device__ __forceinline__ float lane_expf(float x) {
+    x = (x != x) ? kExpLo : x;
+    x = x < kExpLo ? kExpLo : (x > kExpHi ? kExpHi : x);
+    return cephes_exp_core(x);
+}
+
+// ---- musl/FreeBSD logf (tensor.rs:799-837) ------------------------------------------------
+__device__ __forceinline__ float portable_lnf(float x) {
+    const float LN2_HI = 6.9313812256e-01f, LN2_LO = 9.0580006145e-06f;
+    const float LG1 = 0.66666662693f, LG2 = 0.40000972152f, LG3 = 0.28498786688f, LG4 = 0.24279078841f;
+    unsigned ix = __float_as_uint(x);
+    int k = 0;
+    if (ix < 0x00800000u || (ix >> 31) != 0) {
+        if ((ix << 1) == 0) return __int_as_float(0xff800000);  // -inf
+        if ((ix >> 31) != 0) return __int_as_float(0x7fc00000);  // NaN
+        k -= 25;
+        ix = __float_as_uint(__fmul_rn(x, __uint_as_float(0x4c000000u)));
+    } else if (ix >= 0x7f800000u) {
+        return x;
+    } else if (ix == 0x3f800000u) {
+        return 0.0f;
+    }
+    ix = ix + (0x3f800000u - 0x3f3504f3u);
+    k += (int)(ix >> 23) - 0x7f;
+    ix = (ix & 0x007fffffu) + 0x3f3504f3u;
+    float xn = __uint_as_float(ix);
+    float f = __fsub_rn(xn, 1.0f);
+    float s = __fdiv_rn(f, __fadd_rn(2.0f, f));
+    float dk = (float)k;
+    float z = __fmul_rn(s, s);
+    float w = __fmul_rn(z, z);
+    float t1 = __fmul_rn(w, __fadd_rn(LG2, __fmul_rn(w, LG4)));
+    float t2 = __fmul_rn(z, __fadd_rn(LG1, __fmul_rn(w, LG3)));
+    float r = __fadd_rn(t2, t1);
+    float hfsq = __fmul_rn(__fmul_rn(0.5f, f), f);
+    // s * (hfsq + r) + dk * LN2_LO - hfsq + f + dk * LN2_HI, evaluated left to right
+    float acc = __fmul_rn(s, __fadd_rn(hfsq, r));
+    acc = __fadd_rn(acc, __fmul_rn(dk, LN2_LO));
+    acc = __fsub_rn(acc, hfsq);
+    acc = __fadd_rn(acc, f);
+    return __fadd_rn(acc, __fmul_rn(dk, LN2_HI));
+}
+
+// portable_softplus (tensor.rs:859-861): threshold 20.
+__device__ __forceinline__ float softplus(float x) {
+    return x > 20.0f ? x : portable_lnf(__fadd_rn(1.0f, portable_expf(x)));
+}
+
+// lane_sigmoidf (tensor.rs:881-885): 1 / (1 + exp(0 - x)).
+__device__ __forceinline__ float lane_sigmoid(float x) {
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, lane_expf(__fsub_rn(0.0f, x))));
+}
+
+// ---- Fixed reduction trees ----------------------------------------------------------------
+
+// Butterfly sum over the 32 lanes: every lane ends with the same value (float addition is
+// commutative, and each level pairs equal partial sums), independent of any other warp.
+__device__ __forceinline__ float warp_allsum(float v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+
+__device__ __forceinline__ float warp_allmax(float v, int width = 32) {
+    for (int off = width >> 1; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+
+// ---- Activation digits for the Q8 projections ---------------------------------------------
+//
+// A Q8 projection computes y[r] = sum_g scale[r,g] * sum_{c in g} q[r,c] * x[c] over 64-column
+// groups g (Q8_GROUP, src/infrastructure/mamba/model.rs:50-56).  The engine evaluates each
+// group sum with exact integer arithmetic: x restricted to group g is written as
+//     x ~= 2^e * (d1 + d2 * 2^-7 + d3 * 2^-14),  d1, d2, d3 integers in [-64, 64],
+// where 2^e is chosen so that max|x_g| * 2^-e lies in [32, 64).  The three int8 digit planes
+// multiply the int8 weights with int32 accumulation (dp4a on CUDA cores, tcgen05 kind::i8 on
+// the tensor cores); |sum| <= 64*127*64 < 2^24, so every group sum is exact, in any order, on
+// any unit.  The digits keep 20 significant bits relative to the group maximum.  Only the
+// per-group combine below rounds, and it runs in the same order on every path, so the CUDA-core
+// and tensor-core projections produce identical bits at every batch size.
+
+constexpr float kDigitTiny = 7.888609052210118e-31f;  // 2^-100: smaller groups encode as zero
+
+struct Digits3 {
+    int d1, d2, d3;
+};
+
+// e_bits: exponent scale for a group whose max |x| is m.  Returns 2^e as a float and
+// 2^-e in *inv (both exact powers of two); a zero (or below 2^-100) group gives 0 / 0.
+__device__ __forceinline__ float group_scale(float m, float* inv) {
+    if (!(m >= kDigitTiny)) {  // also maps NaN to a zero group
+        *inv = 0.0f;
+        return 0.0f;
+    }
+    int E = (int)((__float_as_uint(m) >> 23) & 0xff) - 127;  // floor(log2 m) for normal m
+    int e = E - 5;                                             // m * 2^-e in [32, 64)
+    *inv = __uint_as_float((unsigned)(127 - e) << 23);
+    return __uint_as_float((unsigned)(127 + e) << 23);
+}
+
+__device__ __forceinline__ Digits3 split_digits(float x, float inv) {
+    float t = __fmul_rn(x, inv);  // exact: power-of-two scaling
+    float d1 = rintf(t);
+    float t2 = __fmul_rn(__fsub_rn(t, d1), 128.0f);  // both exact
+    float d2 = rintf(t2);
+    float t3 = __fmul_rn(__fsub_rn(t2, d2), 128.0f);
+    float d3 = rintf(t3);
+    return {(int)d1, (int)d2, (int)d3};
+}
+
+// Combine the three exact digit sums of one group: ((a1 + a2 * 2^-7) + a3 * 2^-14).
+__device__ __forceinline__ float digit_value(int a1, int a2, int a3) {
+    float v = __fadd_rn((float)a1, __fmul_rn((float)a2, 0.0078125f));
+    return __fadd_rn(v, __fmul_rn((float)a3, 6.103515625e-05f));
+}
+
+// One step of the sequential group accumulation of a row: acc + v * (w_scale * 2^e).
+__device__ __forceinline__ float group_accumulate(float acc, float v, float w_scale, float a_scale) {
+    return __fadd_rn(acc, __fmul_rn(v, __fmul_rn(w_scale, a_scale)));
+}
+
+__device__ __forceinline__ int pack4(int a, int b, int c, int d) {
+    return (a & 0xff) | ((b & 0xff) << 8) | ((c & 0xff) << 16) | ((d & 0xff) << 24);
+}
+
+}  // namespace rk

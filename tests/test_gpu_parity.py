@@ -1,0 +1,227 @@
+"""GPU parity of libredukt_gpu.so against the CPU oracle, through the C ABI.
+
+Mirrors the reference's GPU validation (notebooks/redukt-gpu-cuda-test.py:254-289): v1 vs a CPU
+reference, v1 == forward_batch bits with the stream in an arbitrary slot, reset-then-step0, duplicate
+slot rejection; plus the reference's lockstep test (src/infrastructure/mamba/model.rs:1091-1134):
+every stream of a batch is bit-identical to the same stream run alone, for every batch size.
+Tolerance against the oracle: max |delta log p| <= 1e-3 nats per token (the engine's parity bar).
+"""
+import numpy as np
+import pytest
+
+from conftest import max_dlogp, q8
+from oracle import oracle as O
+from redukt_b200.plugin import BackendResult, PluginBackend
+from redukt_b200.workload import zipf_tokens
+
+pytestmark = pytest.mark.gpu
+
+TOL_NATS = 1e-3
+
+_BACKEND = {}
+
+
+def backend(path):
+    """The plugin is a process-global singleton: re-init only when the model changes."""
+    b = _BACKEND.get("b")
+    if b is not None and _BACKEND.get("path") == path:
+        return b
+    if b is not None:
+        b.close()
+    b = PluginBackend(path)
+    _BACKEND.update(b=b, path=path)
+    return b
+
+
+def oracle_model(path, profile):
+    return O.Model(path, profile, 64)
+
+
+def bits(a):
+    return np.ascontiguousarray(a).view(np.uint32)
+
+
+@pytest.mark.parametrize("quant", ["f32", "q8"])
+def test_v1_matches_oracle_reference_test_model(ref_test_rbin, quant):
+    path = ref_test_rbin if quant == "f32" else q8(ref_test_rbin)
+    b = backend(path)
+    m = oracle_model(path, O.PROFILE_F32 if quant == "f32" else O.PROFILE_Q8)
+    st = m.new_state()
+    b.reset_state()
+    worst = 0.0
+    for t in range(12):
+        tok = (t * 977 + 7) % m.vocab
+        g = b.forward(tok)
+        r = m.forward(tok, st)
+        worst = max(worst, max_dlogp(g, r))
+    assert worst <= TOL_NATS, worst
+
+
+@pytest.mark.parametrize("quant", ["f32", "q8"])
+def test_batch_bit_identical_to_v1_every_batch_size(ref_test_rbin, quant):
+    path = ref_test_rbin if quant == "f32" else q8(ref_test_rbin)
+    b = backend(path)
+    V = b.vocab_size
+    steps = 6
+    nmax = 17
+    toks = np.array([[(s * 131 + t * 977 + 7) % V for t in range(steps)] for s in range(nmax)], np.uint32)
+    # each stream alone through v1
+    single = np.empty((nmax, steps, V), np.float32)
+    for s in range(nmax):
+        b.reset_state()
+        for t in range(steps):
+            single[s, t] = b.forward(int(toks[s, t]))
+    for n in (1, 2, 3, 5, 9, 17):
+        b.batch_init(32)
+        slots = [(7 * s + 3) % 32 for s in range(n)]  # arbitrary distinct slots
+        for t in range(steps):
+            out = b.forward_batch(slots, toks[:n, t])
+            for s in range(n):
+                assert np.array_equal(bits(out[s]), bits(single[s, t])), (quant, n, s, t)
+
+
+def test_reset_then_step0_and_invalid_arguments(ref_test_rbin):
+    b = backend(ref_test_rbin)
+    V = b.vocab_size
+    b.batch_init(8)
+    first = b.forward_batch([5], [11])[0].copy()
+    b.forward_batch([5], [12])
+    b.batch_reset([5])
+    again = b.forward_batch([5], [11])[0]
+    assert np.array_equal(bits(first), bits(again))
+    # duplicate slot, slot out of range, token out of range, vocab mismatch: rejected, no state change
+    out = np.zeros((2, V), np.float32)
+    assert b.forward_batch_raw(np.array([1, 1], np.uint32), np.array([0, 0], np.uint32), out) == BackendResult.INVALID_ARGUMENT
+    assert b.forward_batch_raw(np.array([8], np.uint32), np.array([0], np.uint32), out[:1]) == BackendResult.INVALID_ARGUMENT
+    assert b.forward_batch_raw(np.array([0], np.uint32), np.array([V], np.uint32), out[:1]) == BackendResult.INVALID_ARGUMENT
+    c_before, s_before = b.get_state(5)
+    rc = b.lib.redukt_backend_forward_batch(1, None, None, None, V)
+    assert rc == BackendResult.INVALID_ARGUMENT
+    c_after, s_after = b.get_state(5)
+    assert np.array_equal(c_before, c_after) and np.array_equal(s_before, s_after)
+    assert b.lib.redukt_backend_batch_init(4097) == BackendResult.INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("quant", ["f32", "q8"])
+def test_state_matches_oracle(small_gauss_rbin, quant):
+    path = small_gauss_rbin if quant == "f32" else q8(small_gauss_rbin)
+    b = backend(path)
+    m = oracle_model(path, O.PROFILE_F32 if quant == "f32" else O.PROFILE_Q8)
+    b.batch_init(4)
+    toks = zipf_tokens(3, 10, vocab=m.vocab)
+    states = [m.new_state() for _ in range(3)]
+    worst = 0.0
+    for t in range(10):
+        g = b.forward_batch([0, 2, 3], toks[:, t])
+        r = m.forward_multi(toks[:, t].tolist(), states)
+        worst = max(worst, max_dlogp(g, r))
+    assert worst <= TOL_NATS
+    conv_g, ssm_g = b.get_state(2)
+    conv_r, ssm_r = states[1].export()
+    assert np.allclose(conv_g, conv_r, rtol=1e-3, atol=1e-5)
+    assert np.allclose(ssm_g, ssm_r, rtol=1e-3, atol=1e-5)
+
+
+@pytest.mark.parametrize("per_row", [False, True])
+def test_q8_weights_bit_exact_with_reference_quantizer(small_gauss_rbin, per_row):
+    path = q8(small_gauss_rbin, per_row)
+    b = backend(path)
+    m = O.Model(path, O.PROFILE_Q8, 0 if per_row else 64)
+    for which, layer in (("emb", 0), ("in_proj", 1), ("out_proj", 2)):
+        qg, sg = b.get_q8(which, layer)
+        qr, sr = m.q8(which, layer)
+        assert np.array_equal(qg, qr), which
+        if per_row:
+            assert np.array_equal(bits(sg), bits(np.repeat(sr, sg.shape[1], axis=1))), which
+        else:
+            assert np.array_equal(bits(sg), bits(sr)), which
+
+
+def test_device_periodic_reset_matches_oracle(ref_test_rbin):
+    b = backend(ref_test_rbin)
+    m = oracle_model(ref_test_rbin, O.PROFILE_F32)
+    every = 3
+    b.batch_init(4)
+    b.set_reset_every(every)
+    try:
+        states = [m.new_state(every) for _ in range(2)]
+        toks = zipf_tokens(2, 10, vocab=m.vocab, seed_base=99)
+        for t in range(10):
+            g = b.forward_batch([1, 3], toks[:, t])
+            r = m.forward_multi(toks[:, t].tolist(), states)
+            assert max_dlogp(g, r) <= TOL_NATS, t
+        # device reset == host-driven reset (PluginState::tick) bit for bit
+        b.batch_init(4)
+        b.set_reset_every(0)
+        host = []
+        since = 0
+        for t in range(10):
+            if since >= every:
+                b.batch_reset([1])
+                since = 0
+            since += 1
+            host.append(b.forward_batch([1], toks[:1, t])[0].copy())
+        b.batch_init(4)
+        b.set_reset_every(every)
+        for t in range(10):
+            dev = b.forward_batch([1], toks[:1, t])[0]
+            assert np.array_equal(bits(dev), bits(host[t])), t
+    finally:
+        b.set_reset_every(0)
+
+
+def test_probs_match_softmax_of_logits(ref_test_rbin):
+    b = backend(ref_test_rbin)
+    b.batch_init(4)
+    lg = b.forward_batch([0, 1], [3, 4])
+    b.batch_reset(None)
+    pr = b.forward_batch_probs([0, 1], [3, 4])
+    assert np.allclose(pr.sum(axis=1), 1.0, atol=1e-5)
+    ref = np.stack([O.softmax(x) for x in lg])
+    assert np.max(np.abs(np.log(pr.astype(np.float64)) - np.log(ref.astype(np.float64)))) < 1e-5
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("quant", ["q8", "f32"])
+def test_mamba130m_matches_oracle(mamba130m_rbin, quant):
+    path = mamba130m_rbin if quant == "f32" else q8(mamba130m_rbin)
+    b = backend(path)
+    m = oracle_model(path, O.PROFILE_F32 if quant == "f32" else O.PROFILE_Q8)
+    n, T = 4, 6
+    b.batch_init(n)
+    toks = zipf_tokens(n, T)
+    states = [m.new_state() for _ in range(n)]
+    worst = 0.0
+    for t in range(T):
+        g = b.forward_batch(list(range(n)), toks[:, t])
+        r = m.forward_multi(toks[:, t].tolist(), states)
+        worst = max(worst, max_dlogp(g, r))
+    print(f"mamba130m {quant}: max |dlogp| = {worst:.3e}")
+    assert worst <= TOL_NATS
+
+
+def test_reference_plugin_agrees_with_oracle(ref_test_rbin):
+    """The reference's own CUDA plugin (rebuilt for sm_100a by oracle/Makefile) vs the oracle."""
+    import os
+    if not os.path.exists(O.REF_PLUGIN_PATH):
+        pytest.skip("reference plugin not built")
+    import subprocess, sys, json
+    code = f"""
+import sys, json, numpy as np
+sys.path.insert(0, {repr(str(__import__('os').path.dirname(__import__('os').path.dirname(__file__))))})
+from redukt_b200.plugin import PluginBackend, PluginLibrary
+from oracle import oracle as O
+from conftest import max_dlogp
+b = PluginBackend({ref_test_rbin!r}, library=PluginLibrary({O.REF_PLUGIN_PATH!r}))
+m = O.Model({ref_test_rbin!r}, O.PROFILE_F32)
+st = m.new_state(); worst = 0.0
+for t in range(8):
+    tok = (t * 977 + 7) % m.vocab
+    worst = max(worst, max_dlogp(b.forward(tok), m.forward(tok, st)))
+print(json.dumps(worst))
+"""
+    env = dict(os.environ, PYTHONPATH=os.path.dirname(__file__))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    worst = json.loads(r.stdout.strip().splitlines()[-1])
+    assert worst <= TOL_NATS, worst
