@@ -1,0 +1,442 @@
+#!/usr/bin/env python3
+"""Benchmark of the Mamba-130M lockstep decode step on B200 (one JSON line on stdout).
+
+Workload: Mamba-130M, Q8 weight-only (group 64, the reference recipe),
+32 lockstep streams per GPU, each a seeded Zipf(1.1) token window; a step advances every stream
+by one token.  Weights are seeded random (no checkpoint is available); tokens are synthetic.
+
+  value  tokens/s of the whole job, inputs resident in HBM (device entry point, CUDA-graph replay)
+  e2e    the same through the plugin C ABI with host buffers: H2D of slots/tokens and D2H of the
+         logits inside the timed region
+Extra keys: per-kernel CUDA-event times, the roofline of the dominant kernel, the batch sweep
+(1/128/1024 streams, Q8 and F32) at N=1, and the CPU baseline (the reference CPU path restated in
+C, oracle/, timed on this host's cores).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+Multi-GPU: launch under torch.distributed.run; each rank owns its own windows (weak scaling, no
+collective on the data path); times are the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from redukt_b200 import rbin  # noqa: E402
+from redukt_b200.workload import ZIPF_SEED_BASE, zipf_tokens  # noqa: E402
+
+WINDOW = 2700          # tokens per stream window (configs[0-1])
+STREAMS = 32           # lockstep streams per GPU
+L2_BYTES = 126 * 2**20
+METRIC = "Mamba-130M decode tok/s (Q8, 32 lockstep streams per GPU)"
+SWEEP_N = (1, 128, 1024)
+
+
+# ---------------------------------------------------------------------------------------------
+# Algorithmic bytes (weights read once per step + per-stream compulsory traffic)
+# ---------------------------------------------------------------------------------------------
+
+def dims_bytes(dims: rbin.MambaDims, profile: str):
+    d, di, xr, dr, V, L = dims.d_model, dims.d_inner, dims.xr, dims.dt_rank, dims.vocab, dims.n_layer
+    q8 = profile != "f32"
+
+    def mat(rows, cols):
+        return rows * cols + rows * (cols // 64) * 4 if q8 else rows * cols * 4
+    small = (d + 4 * di + di + xr * di + di * dr + di + 16 * di + di) * 4
+    layer = mat(2 * di, d) + mat(d, di) + small
+    weights = L * layer + mat(V, d) + d * 4
+    emb_row = (d + (d // 64) * 4) if q8 else d * 4
+    per_stream = 2 * dims.state_bytes() + V * 4 + emb_row
+    return weights, per_stream
+
+
+def kernel_bytes(cls: str, n: int, dims: rbin.MambaDims, profile: str) -> int:
+    """Algorithmic bytes of ONE launch of a kernel class for n streams."""
+    d, di, xr, dr, V = dims.d_model, dims.d_inner, dims.xr, dims.dt_rank, dims.vocab
+    q8 = profile != "f32"
+    act = (lambda K: n * (3 * K + (K // 64) * 4)) if q8 else (lambda K: n * K * 4)
+    mat = (lambda r, c: r * c + r * (c // 64) * 4) if q8 else (lambda r, c: r * c * 4)
+    if cls == "scan":
+        return (n * di * 16 * 4 * 2 + (di * dr + di + 16 * di + di) * 4 + n * (xr + 2 * di) * 4 + act(di))
+    if cls == "in_proj":
+        return mat(2 * di, d) + act(d) + n * di * 3 * 4 * 2 + 5 * di * 4 + n * 2 * di * 4
+    if cls == "out_proj":
+        return mat(d, di) + act(di) + n * d * 4 * 2
+    if cls == "head":
+        return mat(V, d) + act(d) + n * V * 4
+    if cls == "x_proj":
+        return xr * di * 4 + n * di * 4 + n * xr * 4
+    if cls == "norm":
+        return n * d * 4 + d * 4 + act(d)
+    if cls == "embed":
+        return n * ((d + (d // 64) * 4) if q8 else d * 4) + n * d * 4
+    return 0
+
+
+# ---------------------------------------------------------------------------------------------
+# Environment helpers
+# ---------------------------------------------------------------------------------------------
+
+def model_paths(rank: int, world: int, barrier):
+    cache = os.environ.get("REDUKT_B200_MODEL_CACHE", os.path.join(tempfile.gettempdir(), "redukt_b200_models"))
+    os.makedirs(cache, exist_ok=True)
+    f32 = os.path.join(cache, "mamba130m.rbin")
+    q8 = os.path.join(cache, "mamba130m.q8.rbin")
+    if rank == 0:
+        rbin.ensure_model(f32, rbin.MAMBA_130M, kind="gaussian")
+        rbin.with_flags(f32, q8, rbin.FLAG_Q8)
+    barrier()
+    return f32, q8
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running."""
+
+    def __init__(self, index: int):
+        self.path = tempfile.mktemp(suffix=".csv")
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def load_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return {"hbm_gbs": float(j["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def load_traffic() -> dict:
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU baseline: the reference CPU path (restated in C, oracle/) on this host's cores
+# ---------------------------------------------------------------------------------------------
+
+def cpu_baseline(q8_path: str, n: int, budget_s: float, min_steps: int = 2):
+    from oracle import oracle as O
+    m = O.Model(q8_path, O.PROFILE_Q8, 64)
+    toks = zipf_tokens(n, WINDOW, vocab=m.vocab)
+    states = [m.new_state(4096) for _ in range(n)]
+    m.forward_multi(toks[:, 0].tolist(), states)  # warm-up (page in weights, start the pool)
+    t0 = time.perf_counter()
+    steps = 0
+    while steps < min_steps or time.perf_counter() - t0 < budget_s:
+        m.forward_multi(toks[:, 1 + steps].tolist(), states)
+        steps += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n * steps / dt, 2), "unit": "tok/s", "cores": O.get_threads(), "kind": "port",
+            "sample": f"{steps} lockstep steps x {n} streams (Q8 group 64, Mamba-130M, {dt:.1f} s), "
+                      f"C restatement of the reference CPU path (oracle/mamba_oracle.c, AVX2 lane order), "
+                      f"{O.get_threads()} threads on {os.cpu_count()} host CPUs"}
+
+
+# ---------------------------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------------------------
+
+def run_b200(args, rank, world, local, dist):
+    import torch
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    from redukt_b200.plugin import PluginBackend
+    f32_path, q8_path = model_paths(rank, world, barrier)
+    dims = rbin.MAMBA_130M
+    n, K, W = args.streams, args.steps, args.warmup
+    b = PluginBackend(q8_path, device_id=local)
+    b.batch_init(n)
+    b.set_reset_every(4096)
+    V = b.vocab_size
+    windows = zipf_tokens(n, WINDOW, vocab=V, seed_base=ZIPF_SEED_BASE + rank * n)
+    d_windows = torch.from_numpy(windows.T.copy().astype(np.int32)).to(dev)  # [T, n]
+    d_slots = torch.arange(n, dtype=torch.int32, device=dev)
+    d_tok = torch.empty(n, dtype=torch.int32, device=dev)
+    d_out = torch.empty((n, V), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    def dev_step(t):
+        d_tok.copy_(d_windows[t % WINDOW])
+        b.forward_batch_device(n, d_slots.data_ptr(), d_tok.data_ptr(), d_out.data_ptr(), stream=sh)
+
+    t = 0
+    for _ in range(W):
+        dev_step(t)
+        t += 1
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        dev_step(t)
+        t += 1
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dev_ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    barrier()
+    torch.cuda.synchronize()
+    dev_ms = max_over_ranks(dev_ms)
+    launches_per_step = b.info_words()["launches_per_step"]
+
+    # per-kernel event times over K further steps (eager launches, each bracketed)
+    b.kernel_times(True)
+    for _ in range(K):
+        dev_step(t)
+        t += 1
+    kt = b.kernel_times(False)
+
+    # e2e through the C ABI with host buffers (pinned output)
+    h_out = torch.empty((n, V), dtype=torch.float32, pin_memory=True).numpy()
+    slots = list(range(n))
+    for i in range(W):
+        b.forward_batch(slots, windows[:, t % WINDOW], out=h_out)
+        t += 1
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(K):
+        b.forward_batch(slots, windows[:, t % WINDOW], out=h_out)
+        t += 1
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+
+    wbytes, per_stream = dims_bytes(dims, "q8")
+    step_bytes = wbytes + n * per_stream
+    peaks = load_peaks()
+    ms_step = dev_ms / K
+    value = world * n * K / (dev_ms / 1e3)
+    res = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 weights x f32 activations (exact int8 digit products), f32 state", "data": "synthetic",
+        "config": {"workload": "configs[1]: Mamba-130M Q8 (group 64) lockstep decode", "model": "Mamba-130M",
+                   "streams_per_gpu": n, "global_batch": n * world, "window_tokens": WINDOW,
+                   "reset_every": 4096, "parallelism": f"windows sharded over {world} GPU(s), no collective",
+                   "l2": f"working set {step_bytes / 1e6:.0f} MB per step > {L2_BYTES / 2**20:.0f} MiB L2 (no flush)"},
+        "clocks": clk,
+        "gpu_launches": launches_per_step * K,
+        "e2e": {"value": round(world * n * K / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": n * 8,
+                "d2h_bytes_per_step": n * V * 4},
+        "step_roofline": {"bound": "hbm", "algorithmic_bytes": step_bytes,
+                          "achieved_gbs": round(step_bytes / (ms_step / 1e3) / 1e9, 1), "peak_gbs": peaks["hbm_gbs"],
+                          "frac": round(step_bytes / (ms_step / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+                          "peak_source": peaks["source"]},
+    }
+    # dominant kernel
+    kernels = {}
+    for cls, (ms, nl) in kt.items():
+        if nl:
+            by = kernel_bytes(cls, n, dims, "q8")
+            avg_us = ms / nl * 1e3
+            kernels[cls] = {"launches": nl, "total_ms": round(ms, 4), "avg_us": round(avg_us, 3),
+                            "bytes_per_launch": by, "gbs": round(by / (avg_us / 1e6) / 1e9, 1) if by else None}
+    tot = sum(k["total_ms"] for k in kernels.values()) or 1.0
+    for k in kernels.values():
+        k["share"] = round(k["total_ms"] / tot, 4)
+    top = max(kernels, key=lambda c: kernels[c]["total_ms"])
+    tr = load_traffic().get(f"q8_n{n}", {}).get(top)
+    kd = kernels[top]
+    res["roofline"] = {"kernel": top, "bound": "hbm", "achieved": kd["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                       "frac": round(kd["gbs"] / peaks["hbm_gbs"], 4), "traffic": tr,
+                       "algorithmic_bytes_per_launch": kd["bytes_per_launch"], "peak_source": peaks["source"]}
+    res["kernels"] = kernels
+
+    if world == 1 and not args.no_sweep:
+        res["sweep"] = sweep(b, f32_path, q8_path, dims, args, dev, peaks)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        b.close()
+        res["cpu_baseline"] = cpu_baseline(q8_path, n, args.cpu_seconds)
+    else:
+        b.close()
+    return res
+
+
+def sweep(b, f32_path, q8_path, dims, args, dev, peaks):
+    """Device tok/s at 1/128/1024 streams, Q8 and F32 (each from fresh zero state)."""
+    import torch
+    from redukt_b200.plugin import PluginBackend
+    out = {}
+    for prof, path in (("q8", q8_path), ("f32", f32_path)):
+        if prof == "f32":
+            b.close()
+            b = PluginBackend(path, device_id=dev.index)
+        for n in SWEEP_N:
+            b.batch_init(n)
+            toks = torch.from_numpy(zipf_tokens(n, 64, vocab=b.vocab_size).T.copy().astype(np.int32)).to(dev)
+            slots = torch.arange(n, dtype=torch.int32, device=dev)
+            tok = torch.empty(n, dtype=torch.int32, device=dev)
+            o = torch.empty((n, b.vocab_size), dtype=torch.float32, device=dev)
+            sh = torch.cuda.current_stream(dev).cuda_stream
+
+            def step(i):
+                tok.copy_(toks[i % 64])
+                b.forward_batch_device(n, slots.data_ptr(), tok.data_ptr(), o.data_ptr(), stream=sh)
+            for i in range(max(3, args.warmup)):
+                step(i)
+            torch.cuda.synchronize()
+            K = max(5, min(args.steps, int(2000 / max(1, n))))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(K):
+                step(i)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / K
+            wb, ps = dims_bytes(dims, prof)
+            by = wb + n * ps
+            out[f"{prof}_n{n}"] = {"tok_s": round(n / ms * 1e3, 1), "ms_per_step": round(ms, 4), "steps": K,
+                                   "hbm_frac": round(by / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)}
+            del o, toks
+    b.close()
+    return out
+
+
+# ---------------------------------------------------------------------------------------------
+# Reference arm: the reference CPU path (C restatement) on this host's cores
+# ---------------------------------------------------------------------------------------------
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    from oracle import oracle as O
+    f32, q8 = model_paths(0, 1, lambda: None)
+    m = O.Model(q8, O.PROFILE_Q8, 64)
+    n = args.streams
+    toks = zipf_tokens(n, WINDOW, vocab=m.vocab)
+    states = [m.new_state(4096) for _ in range(n)]
+    t = 0
+    # bound the whole run to about two minutes: shrink the streams per step if needed
+    t0 = time.perf_counter()
+    m.forward_multi(toks[:, t].tolist(), states)
+    t += 1
+    per_step = time.perf_counter() - t0
+    ns = n
+    if per_step * (args.steps + args.warmup) > 120.0:
+        ns = max(1, int(n * 120.0 / (per_step * (args.steps + args.warmup))))
+        states = states[:ns]
+    for _ in range(args.warmup):
+        m.forward_multi(toks[:ns, t % WINDOW].tolist(), states)
+        t += 1
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        m.forward_multi(toks[:ns, t % WINDOW].tolist(), states)
+        t += 1
+    dt = time.perf_counter() - t0
+    v = ns * args.steps / dt
+    sample = (f"{args.steps} lockstep steps x {ns} streams (of {n}) of Mamba-130M Q8 group 64; "
+              f"C restatement of the reference CPU path (oracle/mamba_oracle.c), {O.get_threads()} threads")
+    return {"impl": "reference", "metric": METRIC, "value": round(v, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 weights x f32",
+            "data": "synthetic",
+            "config": {"workload": "configs[1]: Mamba-130M Q8 (group 64) lockstep decode", "model": "Mamba-130M",
+                       "streams_per_gpu": n, "window_tokens": WINDOW, "parallelism": "host CPU, rank 0 only"},
+            "cpu_baseline": {"value": round(v, 2), "unit": "tok/s", "cores": O.get_threads(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(v, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--streams", type=int, default=STREAMS)
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as D
+        torch.cuda.set_device(local)
+        D.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                             device_id=torch.device("cuda", local))
+        dist = D
+    try:
+        res = run_b200(args, rank, world, local, dist)
+    finally:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

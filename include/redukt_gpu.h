@@ -115,8 +115,9 @@ int32_t redukt_b200_get_state(uint32_t slot, float* conv, float* ssm);
  * 3 out_proj (layer).  q [rows][cols] int8, scales [rows][cols/64] f32 (per-row scales repeated). */
 int32_t redukt_b200_get_q8(int32_t which, uint32_t layer, int8_t* q, float* scales);
 
-/* Model and engine facts: out[0..11] = vocab, d_model, d_inner, d_state, d_conv, dt_rank, n_layer,
- * flags, profile (0 F32, 1 Q8-g64, 2 Q8 per-row), pool capacity, reset_every, projection path. */
+/* Model and engine facts: out[0..12] = vocab, d_model, d_inner, d_state, d_conv, dt_rank, n_layer,
+ * flags, profile (0 F32, 1 Q8-g64, 2 Q8 per-row), pool capacity, reset_every, projection path,
+ * kernel launches of the last enqueued step. */
 int32_t redukt_b200_info(uint32_t* out, uint32_t n);
 
 /* Engine switches for tests and benchmarks:
@@ -124,6 +125,12 @@ int32_t redukt_b200_info(uint32_t* out, uint32_t n);
  *   "graphs"     0/1 = replay each batch size's launch sequence from a captured CUDA graph
  * Returns INVALID_ARGUMENT for an unknown key or value. */
 int32_t redukt_b200_set_option(const char* key, int64_t value);
+
+/* Per-kernel-class device time: returns the CUDA-event time (ms) and launch count accumulated per
+ * class since the previous call (0 embed, 1 norm, 2 in_proj, 3 x_proj, 4 scan, 5 out_proj, 6 head,
+ * 7 softmax), then turns event bracketing on (enable != 0) or off.  While on, steps run without
+ * CUDA graphs so each launch can be bracketed.  Synchronises the device. */
+int32_t redukt_b200_kernel_times(int32_t enable, double* ms, uint32_t* launches, uint32_t n_classes);
 
 /* Last error message of this library (empty string when none). */
 const char* redukt_b200_last_error(void);

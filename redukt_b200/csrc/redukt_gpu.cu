@@ -187,8 +187,11 @@ bool pool_alloc(Pool* p, uint32_t cap) {
     return true;
 }
 
+void clear_dev_graphs();
+
 void free_model() {
     if (G.stream) cudaStreamSynchronize(G.stream);
+    clear_dev_graphs();
     pool_free(&G.v1);
     pool_free(&G.batch);
     for (void* a : G.allocs) cudaFree(a);
@@ -480,36 +483,127 @@ __global__ void k_softmax_final(const float* __restrict__ logits, int V, const f
         o[v] = __fdiv_rn(portable_expf(__fsub_rn(l[v], M)), S);
 }
 
+// Kernel classes for the optional per-launch CUDA-event timing (redukt_b200_kernel_times).
+enum KClass { kKEmbed = 0, kKNorm, kKInProj, kKXProj, kKScan, kKOutProj, kKHead, kKSoftmax, kKClasses };
+
+struct KTiming {
+    bool on = false;
+    std::vector<cudaEvent_t> pool;  // created lazily, reused
+    std::vector<std::pair<int, size_t>> marks;  // (class, index of the start event; stop = +1)
+    size_t used = 0;
+    cudaEvent_t next() {
+        if (used == pool.size()) {
+            cudaEvent_t e;
+            cudaEventCreate(&e);
+            pool.push_back(e);
+        }
+        return pool[used++];
+    }
+};
+KTiming g_kt;
+
+// Brackets the launches of one kernel class with events when timing is on (eager path only).
+struct KScope {
+    int cls;
+    cudaStream_t st;
+    size_t idx = 0;
+    bool active;
+    KScope(int c, cudaStream_t s) : cls(c), st(s), active(g_kt.on) {
+        if (active) {
+            idx = g_kt.used;
+            cudaEventRecord(g_kt.next(), st);
+        }
+    }
+    ~KScope() {
+        if (active) {
+            cudaEventRecord(g_kt.next(), st);
+            g_kt.marks.push_back({cls, idx});
+        }
+    }
+};
+
+int g_launches_per_step = 0;
+
 // Enqueues one decode step for n streams whose slots/tokens are already on the device.
 int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_tokens, float* d_out, bool probs,
                  cudaStream_t st) {
     StepArgs sa{n, (int)p.cap, d_slots, d_tokens, p.rflag, p.since, G.reset_every, G.d_err};
     const Mat& emb = G.emb;
-    k_embed<<<n, 256, 0, st>>>(sa, emb.f, emb.q, emb.s, G.d, G.V, p.x);
+    int launches = 0;
+    {
+        KScope k(kKEmbed, st);
+        k_embed<<<n, 256, 0, st>>>(sa, emb.f, emb.q, emb.s, G.d, G.V, p.x);
+        launches++;
+    }
     for (int li = 0; li < G.nl; li++) {
         const Layer& L = G.layers[li];
-        launch_norm(p, n, L.norm_w, L.norm_b, G.d, st);
-        EpiInProj ein{G.di, (int)p.cap, li, d_slots, p.rflag, p.conv, L.conv_t, L.conv_b, p.conv_out, p.z};
-        project(L.in_proj, p, n, ein, st);
-        gemv_f32<1>(G.xr, G.di, L.x_proj, p.conv_out, G.di, n, EpiStore{p.zp, G.xr}, st);
-        ScanArgs sc{G.di, G.dr, G.xr, (int)p.cap, li, d_slots, p.rflag, p.zp, p.conv_out, p.z,
-                    L.dt_w, L.dt_b, L.a_t, L.dvec, p.ssm};
-        ActOut ao{p.act_f, p.act_q, p.act_e, (int)p.cap, G.di};
-        if (G.profile != kF32) ao.f = nullptr;
-        else ao.q = nullptr;
-        k_scan<<<dim3((G.di + 255) / 256, n), 256, G.xr * sizeof(float), st>>>(sc, ao);
-        project(L.out_proj, p, n, EpiResidual{p.x, G.d}, st);
+        {
+            KScope k(kKNorm, st);
+            launch_norm(p, n, L.norm_w, L.norm_b, G.d, st);
+        }
+        {
+            KScope k(kKInProj, st);
+            EpiInProj ein{G.di, (int)p.cap, li, d_slots, p.rflag, p.conv, L.conv_t, L.conv_b, p.conv_out, p.z};
+            project(L.in_proj, p, n, ein, st);
+        }
+        {
+            KScope k(kKXProj, st);
+            gemv_f32<1>(G.xr, G.di, L.x_proj, p.conv_out, G.di, n, EpiStore{p.zp, G.xr}, st);
+        }
+        {
+            KScope k(kKScan, st);
+            ScanArgs sc{G.di, G.dr, G.xr, (int)p.cap, li, d_slots, p.rflag, p.zp, p.conv_out, p.z,
+                        L.dt_w, L.dt_b, L.a_t, L.dvec, p.ssm};
+            ActOut ao{p.act_f, p.act_q, p.act_e, (int)p.cap, G.di};
+            if (G.profile != kF32) ao.f = nullptr;
+            else ao.q = nullptr;
+            k_scan<<<dim3((G.di + 255) / 256, n), 256, G.xr * sizeof(float), st>>>(sc, ao);
+        }
+        {
+            KScope k(kKOutProj, st);
+            project(L.out_proj, p, n, EpiResidual{p.x, G.d}, st);
+        }
+        launches += 5;
     }
-    launch_norm(p, n, G.norm_f_w, G.norm_f_b, G.d, st);
+    {
+        KScope k(kKNorm, st);
+        launch_norm(p, n, G.norm_f_w, G.norm_f_b, G.d, st);
+    }
     float* lo = probs ? p.logits : d_out;
-    project(G.head, p, n, EpiStore{lo, G.V}, st);
+    {
+        KScope k(kKHead, st);
+        project(G.head, p, n, EpiStore{lo, G.V}, st);
+    }
+    launches += 2;
     if (probs) {
+        KScope k(kKSoftmax, st);
         int parts = (G.V + kSoftmaxTile - 1) / kSoftmaxTile;
         k_softmax_partial<<<dim3(parts, n), 256, 0, st>>>(lo, G.V, p.red, parts);
         k_softmax_final<<<dim3(std::max(1, std::min(64, G.V / 1024)), n), 256, 0, st>>>(lo, G.V, p.red, parts,
                                                                                        d_out);
+        launches += 2;
     }
+    g_launches_per_step = launches;
     CK(cudaGetLastError(), BACKEND_FORWARD_FAILED);
+    return BACKEND_OK;
+}
+
+// Captures `enqueue_step` with these exact pointers into an executable graph.
+int capture_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_tokens, float* d_out, bool probs,
+                 cudaGraphExec_t* exec_out) {
+    cudaStream_t cs = G.stream;
+    cudaGraph_t graph = nullptr;
+    CK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal), BACKEND_FORWARD_FAILED);
+    int rc = enqueue_step(p, n, d_slots, d_tokens, d_out, probs, cs);
+    cudaError_t e = cudaStreamEndCapture(cs, &graph);
+    if (rc != BACKEND_OK) {
+        if (graph) cudaGraphDestroy(graph);
+        return rc;
+    }
+    CK(e, BACKEND_FORWARD_FAILED);
+    e = cudaGraphInstantiate(exec_out, graph, 0);
+    cudaGraphDestroy(graph);
+    CK(e, BACKEND_FORWARD_FAILED);
     return BACKEND_OK;
 }
 
@@ -519,34 +613,44 @@ uint64_t graph_key(int n, bool probs) {
 
 // Enqueue one step for this pool's fixed buffers.  The first call for a (n, probs, options)
 // key runs eagerly (it also sets every kernel attribute); later calls replay a CUDA graph of the
-// same launch sequence captured on the second call.
+// same launch sequence captured on the second call.  Timing mode always runs eagerly.
 int enqueue_pool_step(Pool& p, int n, bool probs) {
     float* out = p.logits;
     uint64_t key = graph_key(n, probs);
-    if (!G.use_graphs || !p.eager_done.count(key)) {
+    if (!G.use_graphs || g_kt.on || !p.eager_done.count(key)) {
         int rc = enqueue_step(p, n, p.d_slots, p.d_tokens, out, probs, G.stream);
         if (rc == BACKEND_OK) p.eager_done.insert(key);
         return rc;
     }
     auto it = p.graphs.find(key);
     if (it == p.graphs.end()) {
-        cudaGraph_t graph = nullptr;
-        CK(cudaStreamBeginCapture(G.stream, cudaStreamCaptureModeThreadLocal), BACKEND_FORWARD_FAILED);
-        int rc = enqueue_step(p, n, p.d_slots, p.d_tokens, out, probs, G.stream);
-        cudaError_t e = cudaStreamEndCapture(G.stream, &graph);
-        if (rc != BACKEND_OK) {
-            if (graph) cudaGraphDestroy(graph);
-            return rc;
-        }
-        CK(e, BACKEND_FORWARD_FAILED);
         cudaGraphExec_t exec = nullptr;
-        e = cudaGraphInstantiate(&exec, graph, 0);
-        cudaGraphDestroy(graph);
-        CK(e, BACKEND_FORWARD_FAILED);
+        int rc = capture_step(p, n, p.d_slots, p.d_tokens, out, probs, &exec);
+        if (rc != BACKEND_OK) return rc;
         it = p.graphs.emplace(key, exec).first;
     }
     CK(cudaGraphLaunch(it->second, G.stream), BACKEND_FORWARD_FAILED);
     return BACKEND_OK;
+}
+
+// Graphs of the device-resident entry point, keyed by the caller's pointers as well.
+struct DevKey {
+    uint64_t key;
+    const void *s, *t, *o;
+    bool operator<(const DevKey& b) const {
+        if (key != b.key) return key < b.key;
+        if (s != b.s) return s < b.s;
+        if (t != b.t) return t < b.t;
+        return o < b.o;
+    }
+};
+std::map<DevKey, cudaGraphExec_t> g_dev_graphs;
+std::set<DevKey> g_dev_eager;
+
+void clear_dev_graphs() {
+    for (auto& kv : g_dev_graphs) cudaGraphExecDestroy(kv.second);
+    g_dev_graphs.clear();
+    g_dev_eager.clear();
 }
 
 // Validates, uploads slots/tokens, runs the step and copies logits or probabilities to `out`
@@ -670,6 +774,7 @@ int32_t redukt_backend_batch_init(uint32_t max_streams) {
     if (!G.ready) return BACKEND_INIT_FAILED;
     if (max_streams > kMaxStreams) return BACKEND_INVALID_ARGUMENT;
     CK(cudaStreamSynchronize(G.stream), BACKEND_INIT_FAILED);
+    clear_dev_graphs();
     pool_free(&G.batch);
     if (max_streams == 0) return BACKEND_OK;
     if (!pool_alloc(&G.batch, max_streams)) {
@@ -718,7 +823,51 @@ int32_t redukt_b200_forward_batch_device(uint32_t n, const uint32_t* d_slots, co
     if (n == 0) return BACKEND_OK;
     if (!d_slots || !d_tokens || !d_out) return BACKEND_INVALID_ARGUMENT;
     cudaStream_t st = cuda_stream ? reinterpret_cast<cudaStream_t>(cuda_stream) : G.stream;
-    return enqueue_step(G.batch, (int)n, d_slots, d_tokens, d_out, probs != 0, st);
+    DevKey k{graph_key((int)n, probs != 0), d_slots, d_tokens, d_out};
+    if (!G.use_graphs || g_kt.on || !g_dev_eager.count(k)) {
+        int rc = enqueue_step(G.batch, (int)n, d_slots, d_tokens, d_out, probs != 0, st);
+        if (rc == BACKEND_OK) g_dev_eager.insert(k);
+        return rc;
+    }
+    auto it = g_dev_graphs.find(k);
+    if (it == g_dev_graphs.end()) {
+        if (g_dev_graphs.size() >= 64) clear_dev_graphs();
+        // capture on the library stream, ordered after the caller's stream
+        cudaEvent_t ev;
+        CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), BACKEND_FORWARD_FAILED);
+        cudaEventRecord(ev, st);
+        cudaStreamWaitEvent(G.stream, ev, 0);
+        cudaEventDestroy(ev);
+        cudaGraphExec_t exec = nullptr;
+        int rc = capture_step(G.batch, (int)n, d_slots, d_tokens, d_out, probs != 0, &exec);
+        if (rc != BACKEND_OK) return rc;
+        it = g_dev_graphs.emplace(k, exec).first;
+    }
+    CK(cudaGraphLaunch(it->second, st), BACKEND_FORWARD_FAILED);
+    return BACKEND_OK;
+}
+
+int32_t redukt_b200_kernel_times(int32_t enable, double* ms, uint32_t* launches, uint32_t n_classes) {
+    if (!G.ready) return BACKEND_INIT_FAILED;
+    CK(cudaDeviceSynchronize(), BACKEND_FORWARD_FAILED);
+    if (ms && launches) {
+        for (uint32_t c = 0; c < n_classes; c++) {
+            ms[c] = 0.0;
+            launches[c] = 0;
+        }
+        for (auto& m : g_kt.marks) {
+            if ((uint32_t)m.first >= n_classes) continue;
+            float t = 0.f;
+            if (cudaEventElapsedTime(&t, g_kt.pool[m.second], g_kt.pool[m.second + 1]) == cudaSuccess) {
+                ms[m.first] += t;
+                launches[m.first] += 1;
+            }
+        }
+    }
+    g_kt.marks.clear();
+    g_kt.used = 0;
+    g_kt.on = enable != 0;
+    return BACKEND_OK;
 }
 
 int32_t redukt_b200_device_error(uint32_t* out_word) {
@@ -778,9 +927,10 @@ int32_t redukt_b200_get_q8(int32_t which, uint32_t layer, int8_t* q, float* scal
 
 int32_t redukt_b200_info(uint32_t* out, uint32_t n) {
     if (!G.ready) return BACKEND_INIT_FAILED;
-    uint32_t v[12] = {(uint32_t)G.V, (uint32_t)G.d, (uint32_t)G.di, G.h.ds, G.h.dc, (uint32_t)G.dr, (uint32_t)G.nl,
-                      G.h.flags, (uint32_t)G.profile, G.batch.cap, G.reset_every, (uint32_t)G.proj_path};
-    for (uint32_t i = 0; i < n && i < 12; i++) out[i] = v[i];
+    uint32_t v[13] = {(uint32_t)G.V, (uint32_t)G.d, (uint32_t)G.di, G.h.ds, G.h.dc, (uint32_t)G.dr, (uint32_t)G.nl,
+                      G.h.flags, (uint32_t)G.profile, G.batch.cap, G.reset_every, (uint32_t)G.proj_path,
+                      (uint32_t)g_launches_per_step};
+    for (uint32_t i = 0; i < n && i < 13; i++) out[i] = v[i];
     return BACKEND_OK;
 }
 

@@ -32,7 +32,9 @@ V2_SYMBOLS = ("redukt_backend_abi_version", "redukt_backend_batch_init", "redukt
               "redukt_backend_forward_batch")
 EXT_SYMBOLS = ("redukt_backend_set_reset_every", "redukt_backend_forward_batch_probs",
                "redukt_b200_forward_batch_device", "redukt_b200_device_error", "redukt_b200_get_state",
-               "redukt_b200_get_q8", "redukt_b200_info", "redukt_b200_set_option", "redukt_b200_last_error")
+               "redukt_b200_get_q8", "redukt_b200_info", "redukt_b200_set_option", "redukt_b200_kernel_times",
+               "redukt_b200_last_error")
+KERNEL_CLASSES = ("embed", "norm", "in_proj", "x_proj", "scan", "out_proj", "head", "softmax")
 
 
 class BackendResult(enum.IntEnum):
@@ -47,10 +49,9 @@ class BackendResult(enum.IntEnum):
     def from_code(cls, code: int) -> "BackendResult":
         """Unknown codes map to FORWARD_FAILED (backend_ffi.rs:48-57)."""
         try:
-            r = cls(code)
+            return cls(code)
         except ValueError:
             return cls.FORWARD_FAILED
-        return cls.FORWARD_FAILED if r == cls.FORWARD_FAILED else r
 
 
 class BackendInfo(ctypes.Structure):
@@ -129,6 +130,8 @@ class PluginLibrary:
             L.redukt_b200_info.argtypes, L.redukt_b200_info.restype = [u32p, u32], i32
             L.redukt_b200_set_option.argtypes = [ctypes.c_char_p, ctypes.c_int64]
             L.redukt_b200_set_option.restype = i32
+            L.redukt_b200_kernel_times.argtypes = [i32, ctypes.POINTER(ctypes.c_double), u32p, u32]
+            L.redukt_b200_kernel_times.restype = i32
             L.redukt_b200_last_error.argtypes, L.redukt_b200_last_error.restype = [], ctypes.c_char_p
 
     def last_error(self) -> str:
@@ -251,13 +254,23 @@ class PluginBackend:
             raise PluginError("redukt_b200_device_error", code, self.libobj.last_error())
         return int(w[0])
 
+    def kernel_times(self, enable: bool) -> dict:
+        """{class: (ms, launches)} accumulated since the last call; then event timing on/off."""
+        ms = np.zeros(len(KERNEL_CLASSES), np.float64)
+        ln = np.zeros(len(KERNEL_CLASSES), np.uint32)
+        code = BackendResult.from_code(self.lib.redukt_b200_kernel_times(
+            1 if enable else 0, ms.ctypes.data_as(ctypes.POINTER(ctypes.c_double)), _u32p(ln), len(KERNEL_CLASSES)))
+        if code != BackendResult.OK:
+            raise PluginError("redukt_b200_kernel_times", code, self.libobj.last_error())
+        return {k: (float(ms[i]), int(ln[i])) for i, k in enumerate(KERNEL_CLASSES)}
+
     def info_words(self) -> dict:
-        w = np.zeros(12, np.uint32)
-        code = BackendResult.from_code(self.lib.redukt_b200_info(_u32p(w), 12))
+        w = np.zeros(13, np.uint32)
+        code = BackendResult.from_code(self.lib.redukt_b200_info(_u32p(w), 13))
         if code != BackendResult.OK:
             raise PluginError("redukt_b200_info", code, self.libobj.last_error())
         keys = ("vocab", "d_model", "d_inner", "d_state", "d_conv", "dt_rank", "n_layer", "flags", "profile",
-                "pool", "reset_every", "proj_path")
+                "pool", "reset_every", "proj_path", "launches_per_step")
         return dict(zip(keys, (int(x) for x in w)))
 
     def get_state(self, slot: int):

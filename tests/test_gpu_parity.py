@@ -225,3 +225,16 @@ print(json.dumps(worst))
     assert r.returncode == 0, r.stderr[-2000:]
     worst = json.loads(r.stdout.strip().splitlines()[-1])
     assert worst <= TOL_NATS, worst
+
+
+@pytest.mark.parametrize("name", ["reftest", "gauss_small", "gauss_ln_untied"])
+def test_gpu_matches_reference_numpy_golden(name, model_dir):
+    """The engine against the reference's own NumPy Mamba (committed fixtures, tests/golden)."""
+    import golden_cases
+    path, toks, golden = golden_cases.load(name, model_dir)
+    b = backend(path)
+    b.reset_state()
+    got = np.stack([b.forward(int(t)).copy() for t in toks])
+    assert max_dlogp(got, golden) <= TOL_NATS
+    rel = np.max(np.abs(got - golden)) / np.max(np.abs(golden))
+    assert rel < 1e-3, rel  # the reference notebook's bar for its own plugin (max rel err < 1e-3)
