@@ -170,7 +170,7 @@ def cpu_baseline(q8_path: str, n: int, budget_s: float, min_steps: int = 2):
     t0 = time.perf_counter()
     steps = 0
     while steps < min_steps or time.perf_counter() - t0 < budget_s:
-        m.forward_multi(toks[:, 1 + steps].tolist(), states)
+        m.forward_multi(toks[:, (1 + steps) % WINDOW].tolist(), states)
         steps += 1
     dt = time.perf_counter() - t0
     return {"value": round(n * steps / dt, 2), "unit": "tok/s", "cores": O.get_threads(), "kind": "port",
@@ -212,8 +212,9 @@ def run_b200(args, rank, world, local, dist):
     d_slots = torch.arange(n, dtype=torch.int32, device=dev)
     d_tok = torch.empty(n, dtype=torch.int32, device=dev)
     d_out = torch.empty((n, V), dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream(dev)
+    stream = torch.cuda.Stream(dev)  # a real stream: handle 0 would select the library's own stream
     sh = stream.cuda_stream
+    torch.cuda.set_stream(stream)
 
     def dev_step(t):
         d_tok.copy_(d_windows[t % WINDOW])
@@ -241,12 +242,11 @@ def run_b200(args, rank, world, local, dist):
     dev_ms = max_over_ranks(dev_ms)
     launches_per_step = b.info_words()["launches_per_step"]
 
-    # per-kernel event times over K further steps (eager launches, each bracketed)
-    b.kernel_times(True)
-    for _ in range(K):
-        dev_step(t)
-        t += 1
-    kt = b.kernel_times(False)
+    # per-kernel device times: each class's launches of one step replayed in isolation (CUDA graph,
+    # L2 flushed before each replay), timed with CUDA events
+    kt = {c: b.time_kernel(c, n, reps=5) for c in ("embed", "norm", "in_proj", "x_proj", "scan", "out_proj", "head")}
+    per_step_launches = {"embed": 1, "norm": dims.n_layer + 1, "in_proj": dims.n_layer, "x_proj": dims.n_layer,
+                         "scan": dims.n_layer, "out_proj": dims.n_layer, "head": 1}
 
     # e2e through the C ABI with host buffers (pinned output)
     h_out = torch.empty((n, V), dtype=torch.float32, pin_memory=True).numpy()
@@ -286,16 +286,16 @@ def run_b200(args, rank, world, local, dist):
     }
     # dominant kernel
     kernels = {}
-    for cls, (ms, nl) in kt.items():
-        if nl:
-            by = kernel_bytes(cls, n, dims, "q8")
-            avg_us = ms / nl * 1e3
-            kernels[cls] = {"launches": nl, "total_ms": round(ms, 4), "avg_us": round(avg_us, 3),
-                            "bytes_per_launch": by, "gbs": round(by / (avg_us / 1e6) / 1e9, 1) if by else None}
-    tot = sum(k["total_ms"] for k in kernels.values()) or 1.0
+    for cls, ms in kt.items():
+        nl = per_step_launches[cls]
+        by = kernel_bytes(cls, n, dims, "q8")
+        avg_us = ms * 1e3
+        kernels[cls] = {"launches_per_step": nl, "avg_us": round(avg_us, 3), "step_us": round(avg_us * nl, 2),
+                        "bytes_per_launch": by, "gbs": round(by / (avg_us / 1e6) / 1e9, 1)}
+    tot = sum(k["step_us"] for k in kernels.values()) or 1.0
     for k in kernels.values():
-        k["share"] = round(k["total_ms"] / tot, 4)
-    top = max(kernels, key=lambda c: kernels[c]["total_ms"])
+        k["share"] = round(k["step_us"] / tot, 4)
+    top = max(kernels, key=lambda c: kernels[c]["step_us"])
     tr = load_traffic().get(f"q8_n{n}", {}).get(top)
     kd = kernels[top]
     res["roofline"] = {"kernel": top, "bound": "hbm", "achieved": kd["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -329,6 +329,7 @@ def sweep(b, f32_path, q8_path, dims, args, dev, peaks):
             tok = torch.empty(n, dtype=torch.int32, device=dev)
             o = torch.empty((n, b.vocab_size), dtype=torch.float32, device=dev)
             sh = torch.cuda.current_stream(dev).cuda_stream
+            assert sh != 0, "the sweep must run on a non-default stream"
 
             def step(i):
                 tok.copy_(toks[i % 64])
@@ -338,10 +339,10 @@ def sweep(b, f32_path, q8_path, dims, args, dev, peaks):
             torch.cuda.synchronize()
             K = max(5, min(args.steps, int(2000 / max(1, n))))
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
+            e0.record(torch.cuda.current_stream(dev))
             for i in range(K):
                 step(i)
-            e1.record()
+            e1.record(torch.cuda.current_stream(dev))
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / K
             wb, ps = dims_bytes(dims, prof)

@@ -132,6 +132,12 @@ int32_t redukt_b200_set_option(const char* key, int64_t value);
  * CUDA graphs so each launch can be bracketed.  Synchronises the device. */
 int32_t redukt_b200_kernel_times(int32_t enable, double* ms, uint32_t* launches, uint32_t n_classes);
 
+/* Device time of one kernel class in isolation, in ms per launch: the class's launches of one
+ * step for n streams (every layer; the embedding and head once) replayed as a CUDA graph after an
+ * L2 flush, `reps` times.  cls as in redukt_b200_kernel_times (0-6).  Needs a batch pool of at least
+ * n slots and overwrites its scratch and the state of slots 0..n-1. */
+int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* ms_per_launch);
+
 /* Last error message of this library (empty string when none). */
 const char* redukt_b200_last_error(void);
 

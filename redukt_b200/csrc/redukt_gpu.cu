@@ -4,6 +4,7 @@
 // argument validation with the reference's error behaviour, the launch sequence of one step
 // and CUDA-graph replay of that sequence per batch size.  The reference counterpart is
 // plugins/redukt-gpu-cuda/mamba_cuda.cu:385-761.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -19,6 +20,7 @@
 
 #include "../../include/redukt_gpu.h"
 #include "rk_kernels.cuh"
+#include "rk_tc.cuh"
 
 namespace {
 
@@ -62,6 +64,7 @@ struct Mat {
     float* f = nullptr;    // F32 [rows][cols]
     int8_t* q = nullptr;   // Q8 [rows][cols]
     float* s = nullptr;    // Q8 scales [rows][cols/64]
+    CUtensorMap tm;        // Q8: TMA map of q, box 64 bytes x 128 rows, 64-byte swizzle
 };
 
 struct Layer {
@@ -97,6 +100,8 @@ struct Pool {
     uint32_t* d_tokens = nullptr;
     uint32_t* h_slots = nullptr;   // pinned
     uint32_t* h_tokens = nullptr;  // pinned
+    uint32_t* h_err = nullptr;     // pinned copy of the device error word
+    CUtensorMap tm_act[2][3];      // digit planes, [K = d | d_inner][N tile 16 | 32 | 64]
     std::vector<uint8_t> seen;
     std::map<uint64_t, cudaGraphExec_t> graphs;  // captured launch sequences, see graph_key()
     std::set<uint64_t> eager_done;                 // keys already run once without a graph
@@ -156,10 +161,41 @@ void pool_free(Pool* p) {
     for (void* b : bufs) cudaFree(b);
     if (p->h_slots) cudaFreeHost(p->h_slots);
     if (p->h_tokens) cudaFreeHost(p->h_tokens);
+    if (p->h_err) cudaFreeHost(p->h_err);
     *p = Pool();
 }
 
 constexpr int kSoftmaxTile = 2048;  // logits per partial (max, sum) of the probability pass
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2D int8 map over [rows][K] with a box of 64 bytes x box_rows and the 64-byte swizzle.
+bool make_i8_map(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {K, rows};
+    cuuint64_t strides[1] = {K};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 bool pool_alloc(Pool* p, uint32_t cap) {
     *p = Pool();
@@ -179,6 +215,13 @@ bool pool_alloc(Pool* p, uint32_t cap) {
                  cudaSuccess;
     if (ok) ok = cudaHostAlloc(reinterpret_cast<void**>(&p->h_tokens), n * sizeof(uint32_t), cudaHostAllocDefault) ==
                  cudaSuccess;
+    if (ok) ok = cudaHostAlloc(reinterpret_cast<void**>(&p->h_err), sizeof(uint32_t), cudaHostAllocDefault) == cudaSuccess;
+    if (ok && G.profile != kF32) {
+        const int Ks[2] = {G.d, G.di};
+        const uint32_t bns[3] = {16, 32, 64};
+        for (int k = 0; k < 2 && ok; k++)
+            for (int t = 0; t < 3 && ok; t++) ok = make_i8_map(&p->tm_act[k][t], p->act_q, (uint64_t)Ks[k], 3ull * n, bns[t]);
+    }
     p->seen.assign(n, 0);
     if (!ok) {
         pool_free(p);
@@ -241,6 +284,7 @@ bool load_mat(Reader& r, Mat* m, int rows, int cols, bool quantise) {
     if (!r.read_to(g_tmp, count)) return false;
     int groups = cols / kGroup;
     if (!model_alloc(&m->q, count) || !model_alloc(&m->s, (size_t)rows * groups)) return false;
+    if (!make_i8_map(&m->tm, m->q, (uint64_t)cols, (uint64_t)rows, tc::kBM)) return false;
     if (G.profile == kQ8) {
         size_t ng = count / kGroup;
         k_quantize_q8<<<(unsigned)((ng + 7) / 8), 256>>>(g_tmp, ng, kGroup, m->q, m->s);
@@ -414,10 +458,31 @@ void gemv_q8(const Mat& m, const int8_t* q, const float* e, int cap, int n, Epi 
     else gemv_q8_gi<4>(m, q, e, cap, n, epi, st);
 }
 
+// Tensor cores for the Q8 projections once the batch makes them worthwhile (or when forced).
+bool use_tc(int n) {
+    if (G.profile == kF32 || G.proj_path == 1) return false;
+    if (G.proj_path == 2) return true;
+    return n >= tc::kAutoMinStreams;
+}
+
+template <int BN, class Epi>
+void project_tc_bn(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st, int tslot) {
+    auto k = tc::k_proj_q8_tc<BN, Epi>;
+    size_t smem = tc::launch_smem<BN>();
+    allow_smem(k, smem);
+    const CUtensorMap& act = p.tm_act[m.cols == G.d ? 0 : 1][tslot];
+    dim3 grid((n + BN - 1) / BN, (m.rows + tc::kBM - 1) / tc::kBM);
+    k<<<grid, tc::kThreads, smem, st>>>(m.tm, act, m.rows, m.cols, (int)p.cap, n, m.s, p.act_e, G.d_err, epi);
+}
+
 template <class Epi>
 void project(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st) {
     if (G.profile == kF32) {
         gemv_f32<4>(m.rows, m.cols, m.f, p.act_f, m.cols, n, epi, st);
+    } else if (use_tc(n)) {
+        if (n <= 16) project_tc_bn<16>(m, p, n, epi, st, 0);
+        else if (n <= 32) project_tc_bn<32>(m, p, n, epi, st, 1);
+        else project_tc_bn<64>(m, p, n, epi, st, 2);
     } else {
         gemv_q8(m, p.act_q, p.act_e, (int)p.cap, n, epi, st);
     }
@@ -670,7 +735,13 @@ int pool_forward(Pool& p, uint32_t n, const uint32_t* slots, const uint32_t* tok
     if (rc != BACKEND_OK) return rc;
     CK(cudaMemcpyAsync(out, p.logits, (size_t)n * G.V * sizeof(float), cudaMemcpyDeviceToHost, G.stream),
        BACKEND_FORWARD_FAILED);
+    CK(cudaMemcpyAsync(p.h_err, G.d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, G.stream), BACKEND_FORWARD_FAILED);
     CK(cudaStreamSynchronize(G.stream), BACKEND_FORWARD_FAILED);
+    if (*p.h_err) {
+        set_err("device error word 0x%x (2 = a tensor-core pipeline wait timed out)", *p.h_err);
+        cudaMemset(G.d_err, 0, sizeof(uint32_t));
+        return BACKEND_FORWARD_FAILED;
+    }
     return BACKEND_OK;
 }
 
@@ -925,6 +996,95 @@ int32_t redukt_b200_get_q8(int32_t which, uint32_t layer, int8_t* q, float* scal
     return BACKEND_OK;
 }
 
+// Times one kernel class in isolation: the class's launches for every layer of one step (the
+// head or embedding once) are captured into a CUDA graph over the batch pool's buffers with
+// slots 0..n-1; each replay follows an L2 flush (a 256 MiB memset) so weights come from HBM as
+// in a real step.  Overwrites the pool's scratch and the state of slots 0..n-1.
+int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* ms_per_launch) {
+    if (!G.ready || G.batch.cap == 0) return BACKEND_INIT_FAILED;
+    if (n == 0 || n > G.batch.cap || !ms_per_launch || cls < 0 || cls >= (int)kKSoftmax) return BACKEND_INVALID_ARGUMENT;
+    Pool& p = G.batch;
+    std::vector<uint32_t> idx(n);
+    for (uint32_t i = 0; i < n; i++) idx[i] = i;
+    CK(cudaMemcpy(p.d_slots, idx.data(), n * 4, cudaMemcpyHostToDevice), BACKEND_FORWARD_FAILED);
+    std::fill(idx.begin(), idx.end(), 1u);
+    CK(cudaMemcpy(p.d_tokens, idx.data(), n * 4, cudaMemcpyHostToDevice), BACKEND_FORWARD_FAILED);
+    void* flush = nullptr;
+    const size_t flush_bytes = (size_t)256 << 20;
+    CK(cudaMalloc(&flush, flush_bytes), BACKEND_FORWARD_FAILED);
+    cudaStream_t st = G.stream;
+    int nn = (int)n;
+    int launches = 0;
+    auto body = [&]() {
+        StepArgs sa{nn, (int)p.cap, p.d_slots, p.d_tokens, p.rflag, p.since, 0u, G.d_err};
+        launches = 0;
+        if (cls == kKEmbed) {
+            k_embed<<<nn, 256, 0, st>>>(sa, G.emb.f, G.emb.q, G.emb.s, G.d, G.V, p.x);
+            launches = 1;
+        } else if (cls == kKHead) {
+            project(G.head, p, nn, EpiStore{p.logits, G.V}, st);
+            launches = 1;
+        } else {
+            for (int li = 0; li < G.nl; li++) {
+                const Layer& L = G.layers[li];
+                if (cls == kKNorm) launch_norm(p, nn, L.norm_w, L.norm_b, G.d, st);
+                if (cls == kKInProj) {
+                    EpiInProj ein{G.di, (int)p.cap, li, p.d_slots, p.rflag, p.conv, L.conv_t, L.conv_b, p.conv_out, p.z};
+                    project(L.in_proj, p, nn, ein, st);
+                }
+                if (cls == kKXProj) gemv_f32<1>(G.xr, G.di, L.x_proj, p.conv_out, G.di, nn, EpiStore{p.zp, G.xr}, st);
+                if (cls == kKScan) {
+                    ScanArgs sc{G.di, G.dr, G.xr, (int)p.cap, li, p.d_slots, p.rflag, p.zp, p.conv_out, p.z,
+                                L.dt_w, L.dt_b, L.a_t, L.dvec, p.ssm};
+                    ActOut ao{p.act_f, p.act_q, p.act_e, (int)p.cap, G.di};
+                    if (G.profile != kF32) ao.f = nullptr;
+                    else ao.q = nullptr;
+                    k_scan<<<dim3((G.di + 255) / 256, nn), 256, G.xr * sizeof(float), st>>>(sc, ao);
+                }
+                if (cls == kKOutProj) project(L.out_proj, p, nn, EpiResidual{p.x, G.d}, st);
+                launches++;
+            }
+        }
+    };
+    body();  // eager once: sets kernel attributes, fills rflag via embed-free path
+    CK(cudaMemsetAsync(p.rflag, 0, n * sizeof(uint32_t), st), BACKEND_FORWARD_FAILED);
+    CK(cudaStreamSynchronize(st), BACKEND_FORWARD_FAILED);
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), BACKEND_FORWARD_FAILED);
+    body();
+    CK(cudaStreamEndCapture(st, &graph), BACKEND_FORWARD_FAILED);
+    cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    CK(e, BACKEND_FORWARD_FAILED);
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    double total = 0.0;
+    uint32_t R = reps ? reps : 5;
+    for (uint32_t r = 0; r <= R; r++) {
+        cudaMemsetAsync(flush, r & 0xff, flush_bytes, st);
+        cudaEventRecord(e0, st);
+        cudaGraphLaunch(exec, st);
+        cudaEventRecord(e1, st);
+        cudaError_t se = cudaEventSynchronize(e1);
+        if (se != cudaSuccess) {
+            set_err("time_kernel: %s", cudaGetErrorString(se));
+            break;
+        }
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        if (r > 0) total += ms;  // replay 0 warms the graph
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaGraphExecDestroy(exec);
+    cudaFree(flush);
+    CK(cudaGetLastError(), BACKEND_FORWARD_FAILED);
+    *ms_per_launch = (float)(total / R / launches);
+    return BACKEND_OK;
+}
+
 int32_t redukt_b200_info(uint32_t* out, uint32_t n) {
     if (!G.ready) return BACKEND_INIT_FAILED;
     uint32_t v[13] = {(uint32_t)G.V, (uint32_t)G.d, (uint32_t)G.di, G.h.ds, G.h.dc, (uint32_t)G.dr, (uint32_t)G.nl,
@@ -937,7 +1097,7 @@ int32_t redukt_b200_info(uint32_t* out, uint32_t n) {
 int32_t redukt_b200_set_option(const char* key, int64_t value) {
     if (!key) return BACKEND_INVALID_ARGUMENT;
     if (!strcmp(key, "proj_path")) {
-        if (value < 0 || value > 1) return BACKEND_INVALID_ARGUMENT;
+        if (value < 0 || value > 2) return BACKEND_INVALID_ARGUMENT;
         G.proj_path = (int)value;
         return BACKEND_OK;
     }

@@ -33,7 +33,7 @@ V2_SYMBOLS = ("redukt_backend_abi_version", "redukt_backend_batch_init", "redukt
 EXT_SYMBOLS = ("redukt_backend_set_reset_every", "redukt_backend_forward_batch_probs",
                "redukt_b200_forward_batch_device", "redukt_b200_device_error", "redukt_b200_get_state",
                "redukt_b200_get_q8", "redukt_b200_info", "redukt_b200_set_option", "redukt_b200_kernel_times",
-               "redukt_b200_last_error")
+               "redukt_b200_time_kernel", "redukt_b200_last_error")
 KERNEL_CLASSES = ("embed", "norm", "in_proj", "x_proj", "scan", "out_proj", "head", "softmax")
 
 
@@ -132,6 +132,8 @@ class PluginLibrary:
             L.redukt_b200_set_option.restype = i32
             L.redukt_b200_kernel_times.argtypes = [i32, ctypes.POINTER(ctypes.c_double), u32p, u32]
             L.redukt_b200_kernel_times.restype = i32
+            L.redukt_b200_time_kernel.argtypes = [i32, u32, u32, ctypes.POINTER(ctypes.c_float)]
+            L.redukt_b200_time_kernel.restype = i32
             L.redukt_b200_last_error.argtypes, L.redukt_b200_last_error.restype = [], ctypes.c_char_p
 
     def last_error(self) -> str:
@@ -241,7 +243,9 @@ class PluginBackend:
 
     def forward_batch_device(self, n: int, d_slots: int, d_tokens: int, d_out: int, probs: bool = False,
                              stream: int = 0) -> None:
-        """Device-resident step: pointers are raw device addresses (e.g. torch tensor.data_ptr())."""
+        """Device-resident step: pointers are raw device addresses (e.g. torch tensor.data_ptr()).
+        `stream` is a cudaStream_t handle; 0 selects the library's own stream (not the legacy
+        default stream), so callers that time with events must pass their own non-zero stream."""
         code = BackendResult.from_code(self.lib.redukt_b200_forward_batch_device(
             n, d_slots, d_tokens, d_out, self.vocab_size, 1 if probs else 0, stream or None))
         if code != BackendResult.OK:
@@ -263,6 +267,15 @@ class PluginBackend:
         if code != BackendResult.OK:
             raise PluginError("redukt_b200_kernel_times", code, self.libobj.last_error())
         return {k: (float(ms[i]), int(ln[i])) for i, k in enumerate(KERNEL_CLASSES)}
+
+    def time_kernel(self, cls: str, n: int, reps: int = 5) -> float:
+        """ms per launch of one kernel class in isolation (see redukt_b200_time_kernel)."""
+        out = ctypes.c_float(0.0)
+        code = BackendResult.from_code(self.lib.redukt_b200_time_kernel(KERNEL_CLASSES.index(cls), n, reps,
+                                                                        ctypes.byref(out)))
+        if code != BackendResult.OK:
+            raise PluginError("redukt_b200_time_kernel", code, self.libobj.last_error())
+        return float(out.value)
 
     def info_words(self) -> dict:
         w = np.zeros(13, np.uint32)

@@ -238,3 +238,24 @@ def test_gpu_matches_reference_numpy_golden(name, model_dir):
     assert max_dlogp(got, golden) <= TOL_NATS
     rel = np.max(np.abs(got - golden)) / np.max(np.abs(golden))
     assert rel < 1e-3, rel  # the reference notebook's bar for its own plugin (max rel err < 1e-3)
+
+
+@pytest.mark.parametrize("quant", ["q8", "q8row"])
+def test_tensor_core_and_cuda_core_projections_bit_identical(small_gauss_rbin, mamba130m_rbin, quant):
+    """The tcgen05 kind::i8 projections and the dp4a projections compute the same exact int32 digit
+    sums and run the same combine: every logit and every state element must agree bit for bit."""
+    for path in (q8(small_gauss_rbin, quant == "q8row"), q8(mamba130m_rbin, quant == "q8row")):
+        b = backend(path)
+        V = b.vocab_size
+        for n in (4, 16, 17, 33, 64, 100):
+            toks = zipf_tokens(n, 3, vocab=V, seed_base=7 * n)
+            outs = {}
+            for mode in (1, 2):
+                b.set_option("proj_path", mode)
+                b.batch_init(n)
+                for t in range(3):
+                    outs[mode] = b.forward_batch(list(range(n)), toks[:, t]).copy()
+                outs[(mode, "state")] = b.get_state(n - 1)
+            b.set_option("proj_path", 0)
+            assert np.array_equal(bits(outs[1]), bits(outs[2])), (path, n)
+            assert np.array_equal(bits(outs[(1, "state")][1]), bits(outs[(2, "state")][1])), (path, n)
