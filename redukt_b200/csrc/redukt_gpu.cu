@@ -4,7 +4,6 @@
 // argument validation with the reference's error behaviour, the launch sequence of one step
 // and CUDA-graph replay of that sequence per batch size.  The reference counterpart is
 // plugins/redukt-gpu-cuda/mamba_cuda.cu:385-761.
-#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -62,9 +61,8 @@ struct RbinHeader {
 struct Mat {
     int rows = 0, cols = 0;
     float* f = nullptr;    // F32 [rows][cols]
-    int8_t* q = nullptr;   // Q8 [rows][cols]
+    int8_t* q = nullptr;   // Q8, tiled [cols/64][rows rounded up to 128][64 B] (rk_math.cuh)
     float* s = nullptr;    // Q8 scales [rows][cols/64]
-    CUtensorMap tm;        // Q8: TMA map of q, box 64 bytes x 128 rows, 64-byte swizzle
 };
 
 struct Layer {
@@ -74,7 +72,7 @@ struct Layer {
     float* conv_t = nullptr;   // [4][di]
     float* conv_b = nullptr;
     float* x_proj = nullptr;   // [xr][di]
-    float* dt_w = nullptr;     // [di][dr]
+    float* dt_wt = nullptr;    // [dr][di] (transposed)
     float* dt_b = nullptr;
     float* a_t = nullptr;      // [16][di] = lane_exp(A_log)
     float* dvec = nullptr;
@@ -88,7 +86,8 @@ struct Pool {
     // per-step scratch, indexed by batch position
     float* x = nullptr;          // [cap][d]
     float* act_f = nullptr;      // [cap][di] f32 activations (F32 profile)
-    int8_t* act_q = nullptr;     // [3][cap][di] digit planes (Q8)
+    int8_t* act_q = nullptr;     // tiled digit planes [di/64][3][cap_pad][64] (Q8)
+    int cap_pad = 0;             // cap rounded up to 64
     float* act_e = nullptr;      // [cap][di/64]
     float* conv_out = nullptr;   // [cap][di]
     float* z = nullptr;          // [cap][di]
@@ -101,7 +100,6 @@ struct Pool {
     uint32_t* h_slots = nullptr;   // pinned
     uint32_t* h_tokens = nullptr;  // pinned
     uint32_t* h_err = nullptr;     // pinned copy of the device error word
-    CUtensorMap tm_act[2][3];      // digit planes, [K = d | d_inner][N tile 16 | 32 | 64]
     std::vector<uint8_t> seen;
     std::map<uint64_t, cudaGraphExec_t> graphs;  // captured launch sequences, see graph_key()
     std::set<uint64_t> eager_done;                 // keys already run once without a graph
@@ -124,6 +122,7 @@ struct Model {
     uint32_t* d_err = nullptr;
     int proj_path = 0;     // 0 auto, 1 CUDA cores, 2 tensor cores
     bool use_graphs = true;
+    bool use_pdl = true;   // programmatic dependent launch between the step's kernels
     bool ready = false;
 };
 
@@ -167,36 +166,6 @@ void pool_free(Pool* p) {
 
 constexpr int kSoftmaxTile = 2048;  // logits per partial (max, sum) of the probability pass
 
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time libcuda).
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    }
-    return fn;
-}
-
-// 2D int8 map over [rows][K] with a box of 64 bytes x box_rows and the 64-byte swizzle.
-bool make_i8_map(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint32_t box_rows) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return false;
-    cuuint64_t dims[2] = {K, rows};
-    cuuint64_t strides[1] = {K};
-    cuuint32_t box[2] = {64, box_rows};
-    cuuint32_t es[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 bool pool_alloc(Pool* p, uint32_t cap) {
     *p = Pool();
     p->cap = cap;
@@ -209,19 +178,17 @@ bool pool_alloc(Pool* p, uint32_t cap) {
               dalloc(&p->d_tokens, n);
     if (ok) {
         if (G.profile == kF32) ok = dalloc(&p->act_f, n * di);
-        else ok = dalloc(&p->act_q, 3 * n * di) && dalloc(&p->act_e, n * (di / kGroup));
+        else {
+            p->cap_pad = round_up((int)cap, 64);
+            ok = dalloc(&p->act_q, 3 * (size_t)p->cap_pad * di) && dalloc(&p->act_e, n * (di / kGroup));
+        }
     }
     if (ok) ok = cudaHostAlloc(reinterpret_cast<void**>(&p->h_slots), n * sizeof(uint32_t), cudaHostAllocDefault) ==
                  cudaSuccess;
     if (ok) ok = cudaHostAlloc(reinterpret_cast<void**>(&p->h_tokens), n * sizeof(uint32_t), cudaHostAllocDefault) ==
                  cudaSuccess;
     if (ok) ok = cudaHostAlloc(reinterpret_cast<void**>(&p->h_err), sizeof(uint32_t), cudaHostAllocDefault) == cudaSuccess;
-    if (ok && G.profile != kF32) {
-        const int Ks[2] = {G.d, G.di};
-        const uint32_t bns[3] = {16, 32, 64};
-        for (int k = 0; k < 2 && ok; k++)
-            for (int t = 0; t < 3 && ok; t++) ok = make_i8_map(&p->tm_act[k][t], p->act_q, (uint64_t)Ks[k], 3ull * n, bns[t]);
-    }
+
     p->seen.assign(n, 0);
     if (!ok) {
         pool_free(p);
@@ -283,21 +250,33 @@ bool load_mat(Reader& r, Mat* m, int rows, int cols, bool quantise) {
     if (!quantise || G.profile == kF32) return load_f32(r, &m->f, count);
     if (!r.read_to(g_tmp, count)) return false;
     int groups = cols / kGroup;
-    if (!model_alloc(&m->q, count) || !model_alloc(&m->s, (size_t)rows * groups)) return false;
-    if (!make_i8_map(&m->tm, m->q, (uint64_t)cols, (uint64_t)rows, tc::kBM)) return false;
+    const int rows_pad = round_up(rows, tc::kBM);
+    int8_t* q_rm = nullptr;  // row-major quantised copy, then tiled
+    if (!dalloc(&q_rm, count, false)) return false;
+    if (!model_alloc(&m->q, (size_t)rows_pad * cols) || !model_alloc(&m->s, (size_t)rows * groups)) {
+        cudaFree(q_rm);
+        return false;
+    }
     if (G.profile == kQ8) {
         size_t ng = count / kGroup;
-        k_quantize_q8<<<(unsigned)((ng + 7) / 8), 256>>>(g_tmp, ng, kGroup, m->q, m->s);
+        k_quantize_q8<<<(unsigned)((ng + 7) / 8), 256>>>(g_tmp, ng, kGroup, q_rm, m->s);
     } else {
         float* row_s = nullptr;
-        if (!dalloc(&row_s, (size_t)rows)) return false;
-        k_quantize_q8<<<(unsigned)((rows + 7) / 8), 256>>>(g_tmp, (size_t)rows, cols, m->q, row_s);
+        if (!dalloc(&row_s, (size_t)rows)) {
+            cudaFree(q_rm);
+            return false;
+        }
+        k_quantize_q8<<<(unsigned)((rows + 7) / 8), 256>>>(g_tmp, (size_t)rows, cols, q_rm, row_s);
         size_t tot = (size_t)rows * groups;
         k_broadcast_scales<<<(unsigned)((tot + 255) / 256), 256>>>(row_s, rows, groups, m->s);
         cudaDeviceSynchronize();
         cudaFree(row_s);
     }
-    return cudaDeviceSynchronize() == cudaSuccess;
+    size_t chunks = count / 16;
+    k_tile_q8<<<(unsigned)((chunks + 255) / 256), 256>>>(q_rm, rows, cols, rows_pad, m->q);
+    bool ok = cudaDeviceSynchronize() == cudaSuccess;
+    cudaFree(q_rm);
+    return ok;
 }
 
 int validate_header(const RbinHeader& h) {
@@ -374,18 +353,22 @@ int load_weights(const char* path) {
     bool ok = load_mat(r, &G.emb, G.V, G.d, true);
     float* a_log = nullptr;
     float* conv_w = nullptr;
-    ok = ok && dalloc(&a_log, di * kDState, false) && dalloc(&conv_w, di * kDConv, false);
+    float* dt_w = nullptr;
+    ok = ok && dalloc(&a_log, di * kDState, false) && dalloc(&conv_w, di * kDConv, false) &&
+         dalloc(&dt_w, di * dr, false);
     G.layers.resize(G.nl);
     for (int i = 0; ok && i < G.nl; i++) {
         Layer& L = G.layers[i];
         ok = load_f32(r, &L.norm_w, d) && (!nb || load_f32(r, &L.norm_b, d)) &&
              load_mat(r, &L.in_proj, 2 * G.di, G.d, true) && r.read_to(conv_w, di * kDConv) &&
-             load_f32(r, &L.conv_b, di) && load_f32(r, &L.x_proj, xr * di) && load_f32(r, &L.dt_w, di * dr) &&
+             load_f32(r, &L.conv_b, di) && load_f32(r, &L.x_proj, xr * di) && r.read_to(dt_w, di * dr) &&
              load_f32(r, &L.dt_b, di) && r.read_to(a_log, di * kDState) && load_f32(r, &L.dvec, di) &&
              load_mat(r, &L.out_proj, G.d, G.di, true);
-        ok = ok && model_alloc(&L.a_t, di * kDState) && model_alloc(&L.conv_t, di * kDConv);
+        ok = ok && model_alloc(&L.a_t, di * kDState) && model_alloc(&L.conv_t, di * kDConv) &&
+             model_alloc(&L.dt_wt, di * dr);
         if (ok) {
-            k_prep_layer<<<(unsigned)((di + 255) / 256), 256>>>(a_log, conv_w, G.di, L.a_t, L.conv_t);
+            k_prep_layer<<<(unsigned)((di + 255) / 256), 256>>>(a_log, conv_w, dt_w, G.di, G.dr, L.a_t, L.conv_t,
+                                                                 L.dt_wt);
             ok = cudaDeviceSynchronize() == cudaSuccess;
         }
     }
@@ -395,6 +378,7 @@ int load_weights(const char* path) {
     if (ok && !untied) G.head = G.emb;
     cudaFree(a_log);
     cudaFree(conv_w);
+    cudaFree(dt_w);
     if (g_tmp) cudaFree(g_tmp);
     g_tmp = nullptr;
     if (!ok) {
@@ -408,18 +392,50 @@ int load_weights(const char* path) {
 // Launch helpers
 // ------------------------------------------------------------------------------------------
 
+// Launches a step kernel; with PDL the kernel may start while its predecessor drains (every step
+// kernel calls griddepcontrol.wait before touching data an earlier kernel wrote).
+template <class... KArgs, class... Args>
+void launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = G.use_pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 template <class Kern>
 void allow_smem(Kern k, size_t bytes) {
     if (bytes > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
-template <int RW, int NS, class Epi>
-void gemv_f32_ns(int M, int K, const float* W, const float* act, int ld, int n, Epi epi, cudaStream_t st) {
+template <int RW, int NS, int NCH, class Epi>
+void gemv_f32_nch(int M, int K, const float* W, const float* act, int ld, int n, Epi epi, cudaStream_t st) {
     size_t smem = (size_t)NS * K * sizeof(float);
-    auto k = k_gemv_f32<RW, NS, Epi>;
+    auto k = k_gemv_f32<RW, NS, NCH, Epi>;
     allow_smem(k, smem);
     dim3 grid((n + NS - 1) / NS, (M + 8 * RW - 1) / (8 * RW));
-    k<<<grid, 256, smem, st>>>(M, K, W, act, ld, n, epi);
+    launch(k, grid, dim3(256), smem, st, M, K, W, act, ld, n, epi);
+}
+
+// K <= 128 * NCH; the chunk loop is unrolled so every weight load of a row is issued at once.
+template <int RW, int NS, class Epi>
+void gemv_f32_ns(int M, int K, const float* W, const float* act, int ld, int n, Epi epi, cudaStream_t st) {
+    if (RW > 1) {  // many rows per warp: a rolled chunk loop keeps the register count moderate
+        gemv_f32_nch<RW, NS, 0>(M, K, W, act, ld, n, epi, st);
+        return;
+    }
+    int nch = (K + 127) / 128;
+    if (nch <= 1) gemv_f32_nch<RW, NS, 1>(M, K, W, act, ld, n, epi, st);
+    else if (nch <= 2) gemv_f32_nch<RW, NS, 2>(M, K, W, act, ld, n, epi, st);
+    else if (nch <= 6) gemv_f32_nch<RW, NS, 6>(M, K, W, act, ld, n, epi, st);
+    else if (nch <= 12) gemv_f32_nch<RW, NS, 12>(M, K, W, act, ld, n, epi, st);
+    else gemv_f32_nch<RW, NS, 16>(M, K, W, act, ld, n, epi, st);
 }
 
 template <int RW, class Epi>
@@ -430,32 +446,40 @@ void gemv_f32(int M, int K, const float* W, const float* act, int ld, int n, Epi
     else gemv_f32_ns<RW, 1>(M, K, W, act, ld, n, epi, st);
 }
 
+// x_proj: few rows (dt_rank + 32), so streams are tiled finely to fill the GPU.
+template <class Epi>
+void gemv_f32_small_m(int M, int K, const float* W, const float* act, int ld, int n, Epi epi, cudaStream_t st) {
+    if (n >= 4) gemv_f32_ns<1, 4>(M, K, W, act, ld, n, epi, st);
+    else if (n >= 2) gemv_f32_ns<1, 2>(M, K, W, act, ld, n, epi, st);
+    else gemv_f32_ns<1, 1>(M, K, W, act, ld, n, epi, st);
+}
+
 template <int NS, int GI, class Epi>
-void gemv_q8_ns(const Mat& m, const int8_t* q, const float* e, int cap, int n, Epi epi, cudaStream_t st) {
+void gemv_q8_ns(const Mat& m, const int8_t* q, const float* e, int cap_pad, int n, Epi epi, cudaStream_t st) {
     constexpr int RW = 4;
     int K = m.cols;
     size_t smem = (size_t)NS * 3 * K + (size_t)NS * (K / kGroup) * sizeof(float);
     auto k = k_gemv_q8<RW, NS, GI, Epi>;
     allow_smem(k, smem);
     dim3 grid((n + NS - 1) / NS, (m.rows + 8 * RW - 1) / (8 * RW));
-    k<<<grid, 256, smem, st>>>(m.rows, K, m.q, m.s, q, e, cap, n, epi);
+    launch(k, grid, dim3(256), smem, st, m.rows, K, (const int8_t*)m.q, (const float*)m.s, q, e, cap_pad, n, epi);
 }
 
 template <int GI, class Epi>
-void gemv_q8_gi(const Mat& m, const int8_t* q, const float* e, int cap, int n, Epi epi, cudaStream_t st) {
-    if (n >= 8) gemv_q8_ns<8, GI>(m, q, e, cap, n, epi, st);
-    else if (n >= 4) gemv_q8_ns<4, GI>(m, q, e, cap, n, epi, st);
-    else if (n >= 2) gemv_q8_ns<2, GI>(m, q, e, cap, n, epi, st);
-    else gemv_q8_ns<1, GI>(m, q, e, cap, n, epi, st);
+void gemv_q8_gi(const Mat& m, const int8_t* q, const float* e, int cap_pad, int n, Epi epi, cudaStream_t st) {
+    if (n >= 8) gemv_q8_ns<8, GI>(m, q, e, cap_pad, n, epi, st);
+    else if (n >= 4) gemv_q8_ns<4, GI>(m, q, e, cap_pad, n, epi, st);
+    else if (n >= 2) gemv_q8_ns<2, GI>(m, q, e, cap_pad, n, epi, st);
+    else gemv_q8_ns<1, GI>(m, q, e, cap_pad, n, epi, st);
 }
 
 template <class Epi>
-void gemv_q8(const Mat& m, const int8_t* q, const float* e, int cap, int n, Epi epi, cudaStream_t st) {
+void gemv_q8(const Mat& m, const int8_t* q, const float* e, int cap_pad, int n, Epi epi, cudaStream_t st) {
     int G8 = (m.cols / kGroup + 7) / 8;
-    if (G8 <= 1) gemv_q8_gi<1>(m, q, e, cap, n, epi, st);
-    else if (G8 == 2) gemv_q8_gi<2>(m, q, e, cap, n, epi, st);
-    else if (G8 == 3) gemv_q8_gi<3>(m, q, e, cap, n, epi, st);
-    else gemv_q8_gi<4>(m, q, e, cap, n, epi, st);
+    if (G8 <= 1) gemv_q8_gi<1>(m, q, e, cap_pad, n, epi, st);
+    else if (G8 == 2) gemv_q8_gi<2>(m, q, e, cap_pad, n, epi, st);
+    else if (G8 == 3) gemv_q8_gi<3>(m, q, e, cap_pad, n, epi, st);
+    else gemv_q8_gi<4>(m, q, e, cap_pad, n, epi, st);
 }
 
 // Tensor cores for the Q8 projections once the batch makes them worthwhile (or when forced).
@@ -466,13 +490,13 @@ bool use_tc(int n) {
 }
 
 template <int BN, class Epi>
-void project_tc_bn(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st, int tslot) {
+void project_tc_bn(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st) {
     auto k = tc::k_proj_q8_tc<BN, Epi>;
     size_t smem = tc::launch_smem<BN>();
     allow_smem(k, smem);
-    const CUtensorMap& act = p.tm_act[m.cols == G.d ? 0 : 1][tslot];
     dim3 grid((n + BN - 1) / BN, (m.rows + tc::kBM - 1) / tc::kBM);
-    k<<<grid, tc::kThreads, smem, st>>>(m.tm, act, m.rows, m.cols, (int)p.cap, n, m.s, p.act_e, G.d_err, epi);
+    launch(k, grid, dim3(tc::kThreads), smem, st, (const int8_t*)m.q, (const int8_t*)p.act_q, m.rows, m.cols,
+           p.cap_pad, n, (const float*)m.s, (const float*)p.act_e, G.d_err, epi);
 }
 
 template <class Epi>
@@ -480,35 +504,38 @@ void project(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st) {
     if (G.profile == kF32) {
         gemv_f32<4>(m.rows, m.cols, m.f, p.act_f, m.cols, n, epi, st);
     } else if (use_tc(n)) {
-        if (n <= 16) project_tc_bn<16>(m, p, n, epi, st, 0);
-        else if (n <= 32) project_tc_bn<32>(m, p, n, epi, st, 1);
-        else project_tc_bn<64>(m, p, n, epi, st, 2);
+        // narrow stream tiles at small n put more CTAs on the weights (re-reads hit L2)
+        if (n <= 64) project_tc_bn<16>(m, p, n, epi, st);
+        else if (n <= 256) project_tc_bn<32>(m, p, n, epi, st);
+        else project_tc_bn<64>(m, p, n, epi, st);
     } else {
-        gemv_q8(m, p.act_q, p.act_e, (int)p.cap, n, epi, st);
+        gemv_q8(m, p.act_q, p.act_e, p.cap_pad, n, epi, st);
     }
 }
 
 void launch_norm(const Pool& p, int n, const float* w, const float* b, int K_out, cudaStream_t st) {
-    ActOut out{p.act_f, p.act_q, p.act_e, (int)p.cap, K_out};
+    ActOut out{p.act_f, p.act_q, p.act_e, p.cap_pad, K_out};
     if (G.profile != kF32) out.f = nullptr;
     else out.q = nullptr;
     dim3 grid((n + 3) / 4);
     int nc = (G.d + 127) / 128;
     switch (nc) {
-        case 1: k_norm<1><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
-        case 2: k_norm<2><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
-        case 3: k_norm<3><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
-        case 4: k_norm<4><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
-        case 5: k_norm<5><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
-        case 6: k_norm<6><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
-        case 7: k_norm<7><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
-        default: k_norm<8><<<grid, 128, 0, st>>>(n, p.x, G.d, w, b, out); break;
+        case 1: launch(k_norm<1>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
+        case 2: launch(k_norm<2>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
+        case 3: launch(k_norm<3>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
+        case 4: launch(k_norm<4>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
+        case 5: launch(k_norm<5>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
+        case 6: launch(k_norm<6>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
+        case 7: launch(k_norm<7>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
+        default: launch(k_norm<8>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
     }
 }
 
 // Softmax over each row of `logits` written to `out` (may alias): partial (max, sum exp) per
 // 2048-logit tile, then a fixed-order combine.  exp is the reference's Cephes polynomial.
 __global__ void k_softmax_partial(const float* __restrict__ logits, int V, float* __restrict__ red, int parts) {
+    pdl_wait();
+    pdl_trigger();
     int b = blockIdx.y, t = blockIdx.x;
     const float* l = logits + (size_t)b * V;
     int v0 = t * kSoftmaxTile, v1 = min(V, v0 + kSoftmaxTile);
@@ -536,6 +563,8 @@ __global__ void k_softmax_partial(const float* __restrict__ logits, int V, float
 
 __global__ void k_softmax_final(const float* __restrict__ logits, int V, const float* __restrict__ red, int parts,
                                 float* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     int b = blockIdx.y;
     const float* rb = red + (size_t)b * parts * 2;
     float M = -INFINITY;
@@ -597,7 +626,8 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
     int launches = 0;
     {
         KScope k(kKEmbed, st);
-        k_embed<<<n, 256, 0, st>>>(sa, emb.f, emb.q, emb.s, G.d, G.V, p.x);
+        launch(k_embed, dim3(n), dim3(256), 0, st, sa, (const float*)emb.f, (const int8_t*)emb.q, (const float*)emb.s, G.d,
+               G.V, p.x);
         launches++;
     }
     for (int li = 0; li < G.nl; li++) {
@@ -613,16 +643,16 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
         }
         {
             KScope k(kKXProj, st);
-            gemv_f32<1>(G.xr, G.di, L.x_proj, p.conv_out, G.di, n, EpiStore{p.zp, G.xr}, st);
+            gemv_f32_small_m(G.xr, G.di, L.x_proj, p.conv_out, G.di, n, EpiStore{p.zp, G.xr}, st);
         }
         {
             KScope k(kKScan, st);
             ScanArgs sc{G.di, G.dr, G.xr, (int)p.cap, li, d_slots, p.rflag, p.zp, p.conv_out, p.z,
-                        L.dt_w, L.dt_b, L.a_t, L.dvec, p.ssm};
-            ActOut ao{p.act_f, p.act_q, p.act_e, (int)p.cap, G.di};
+                        L.dt_wt, L.dt_b, L.a_t, L.dvec, p.ssm};
+            ActOut ao{p.act_f, p.act_q, p.act_e, p.cap_pad, G.di};
             if (G.profile != kF32) ao.f = nullptr;
             else ao.q = nullptr;
-            k_scan<<<dim3((G.di + 255) / 256, n), 256, G.xr * sizeof(float), st>>>(sc, ao);
+            launch(k_scan, dim3(G.di / 64, n), dim3(256), G.xr * sizeof(float), st, sc, ao);
         }
         {
             KScope k(kKOutProj, st);
@@ -643,9 +673,9 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
     if (probs) {
         KScope k(kKSoftmax, st);
         int parts = (G.V + kSoftmaxTile - 1) / kSoftmaxTile;
-        k_softmax_partial<<<dim3(parts, n), 256, 0, st>>>(lo, G.V, p.red, parts);
-        k_softmax_final<<<dim3(std::max(1, std::min(64, G.V / 1024)), n), 256, 0, st>>>(lo, G.V, p.red, parts,
-                                                                                       d_out);
+        launch(k_softmax_partial, dim3(parts, n), dim3(256), 0, st, (const float*)lo, G.V, p.red, parts);
+        launch(k_softmax_final, dim3(std::max(1, std::min(64, G.V / 1024)), n), dim3(256), 0, st, (const float*)lo, G.V,
+               (const float*)p.red, parts, d_out);
         launches += 2;
     }
     g_launches_per_step = launches;
@@ -814,6 +844,7 @@ BackendResult redukt_backend_init(const uint8_t* weights_path, int32_t device_id
     }
     if (const char* e = getenv("REDUKT_B200_GRAPHS")) G.use_graphs = atoi(e) != 0;
     if (const char* e = getenv("REDUKT_B200_PROJ")) G.proj_path = atoi(e);
+    if (const char* e = getenv("REDUKT_B200_PDL")) G.use_pdl = atoi(e) != 0;
     G.ready = true;
     memset(info_out, 0, sizeof(*info_out));
     info_out->ffi_version = BACKEND_FFI_VERSION;
@@ -989,7 +1020,14 @@ int32_t redukt_b200_get_q8(int32_t which, uint32_t layer, int8_t* q, float* scal
         m = which == 2 ? &G.layers[layer].in_proj : &G.layers[layer].out_proj;
     if (!m) return BACKEND_INVALID_ARGUMENT;
     size_t count = (size_t)m->rows * m->cols;
-    if (q) CK(cudaMemcpy(q, m->q, count, cudaMemcpyDeviceToHost), BACKEND_FORWARD_FAILED);
+    if (q) {
+        const int rows_pad = round_up(m->rows, tc::kBM);
+        std::vector<int8_t> tiled((size_t)rows_pad * m->cols);
+        CK(cudaMemcpy(tiled.data(), m->q, tiled.size(), cudaMemcpyDeviceToHost), BACKEND_FORWARD_FAILED);
+        for (int r = 0; r < m->rows; r++)
+            for (int k = 0; k < m->cols; k++) q[(size_t)r * m->cols + k] = tiled[wq_off(rows_pad, r, k)];
+    }
+    (void)count;
     if (scales)
         CK(cudaMemcpy(scales, m->s, (size_t)m->rows * (m->cols / kGroup) * sizeof(float), cudaMemcpyDeviceToHost),
            BACKEND_FORWARD_FAILED);
@@ -1019,7 +1057,8 @@ int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* m
         StepArgs sa{nn, (int)p.cap, p.d_slots, p.d_tokens, p.rflag, p.since, 0u, G.d_err};
         launches = 0;
         if (cls == kKEmbed) {
-            k_embed<<<nn, 256, 0, st>>>(sa, G.emb.f, G.emb.q, G.emb.s, G.d, G.V, p.x);
+            launch(k_embed, dim3(nn), dim3(256), 0, st, sa, (const float*)G.emb.f, (const int8_t*)G.emb.q,
+                   (const float*)G.emb.s, G.d, G.V, p.x);
             launches = 1;
         } else if (cls == kKHead) {
             project(G.head, p, nn, EpiStore{p.logits, G.V}, st);
@@ -1032,14 +1071,14 @@ int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* m
                     EpiInProj ein{G.di, (int)p.cap, li, p.d_slots, p.rflag, p.conv, L.conv_t, L.conv_b, p.conv_out, p.z};
                     project(L.in_proj, p, nn, ein, st);
                 }
-                if (cls == kKXProj) gemv_f32<1>(G.xr, G.di, L.x_proj, p.conv_out, G.di, nn, EpiStore{p.zp, G.xr}, st);
+                if (cls == kKXProj) gemv_f32_small_m(G.xr, G.di, L.x_proj, p.conv_out, G.di, nn, EpiStore{p.zp, G.xr}, st);
                 if (cls == kKScan) {
                     ScanArgs sc{G.di, G.dr, G.xr, (int)p.cap, li, p.d_slots, p.rflag, p.zp, p.conv_out, p.z,
-                                L.dt_w, L.dt_b, L.a_t, L.dvec, p.ssm};
-                    ActOut ao{p.act_f, p.act_q, p.act_e, (int)p.cap, G.di};
+                                L.dt_wt, L.dt_b, L.a_t, L.dvec, p.ssm};
+                    ActOut ao{p.act_f, p.act_q, p.act_e, p.cap_pad, G.di};
                     if (G.profile != kF32) ao.f = nullptr;
                     else ao.q = nullptr;
-                    k_scan<<<dim3((G.di + 255) / 256, nn), 256, G.xr * sizeof(float), st>>>(sc, ao);
+                    launch(k_scan, dim3(G.di / 64, nn), dim3(256), G.xr * sizeof(float), st, sc, ao);
                 }
                 if (cls == kKOutProj) project(L.out_proj, p, nn, EpiResidual{p.x, G.d}, st);
                 launches++;
@@ -1103,6 +1142,15 @@ int32_t redukt_b200_set_option(const char* key, int64_t value) {
     }
     if (!strcmp(key, "graphs")) {
         G.use_graphs = value != 0;
+        return BACKEND_OK;
+    }
+    if (!strcmp(key, "pdl")) {
+        G.use_pdl = value != 0;
+        for (Pool* p : {&G.v1, &G.batch}) {  // captured graphs hold the old launch attributes
+            for (auto& kv : p->graphs) cudaGraphExecDestroy(kv.second);
+            p->graphs.clear();
+        }
+        clear_dev_graphs();
         return BACKEND_OK;
     }
     return BACKEND_INVALID_ARGUMENT;

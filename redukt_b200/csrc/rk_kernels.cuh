@@ -60,16 +60,28 @@ __global__ void k_broadcast_scales(const float* __restrict__ row_scale, int rows
     if (i < (size_t)rows * groups) out[i] = row_scale[i / groups];
 }
 
+// Row-major int8 [rows][cols] -> tiled [cols/64][rows_pad][64] (rows >= rows are left as they are:
+// the destination is zeroed first).
+__global__ void k_tile_q8(const int8_t* __restrict__ src, int rows, int cols, int rows_pad, int8_t* __restrict__ dst) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;  // one 16-byte chunk
+    size_t per_row = (size_t)cols / 16;
+    if (i >= (size_t)rows * per_row) return;
+    int r = (int)(i / per_row), k = (int)(i - (size_t)r * per_row) * 16;
+    *reinterpret_cast<int4*>(dst + wq_off(rows_pad, r, k)) = *reinterpret_cast<const int4*>(src + (size_t)r * cols + k);
+}
+
 // A = exp(A_log) as the reference's lane_expf computes it (tensor.rs:1314), stored [16][di];
-// conv weights transposed to [dc][di].
-__global__ void k_prep_layer(const float* __restrict__ a_log, const float* __restrict__ conv_w, int di,
-                             float* __restrict__ a_t, float* __restrict__ conv_t) {
+// conv weights transposed to [dc][di]; dt_proj weights transposed to [dr][di].
+__global__ void k_prep_layer(const float* __restrict__ a_log, const float* __restrict__ conv_w,
+                             const float* __restrict__ dt_w, int di, int dr, float* __restrict__ a_t,
+                             float* __restrict__ conv_t, float* __restrict__ dt_wt) {
     int j = blockIdx.x * blockDim.x + threadIdx.x;
     if (j >= di) return;
 #pragma unroll
     for (int n = 0; n < kDState; n++) a_t[n * di + j] = lane_expf(a_log[j * kDState + n]);
 #pragma unroll
     for (int k = 0; k < kDConv; k++) conv_t[k * di + j] = conv_w[j * kDConv + k];
+    for (int c = 0; c < dr; c++) dt_wt[(size_t)c * di + j] = dt_w[(size_t)j * dr + c];
 }
 
 // ------------------------------------------------------------------------------------------
@@ -92,6 +104,8 @@ struct StepArgs {
 // The state itself is never written here: every conv/scan read of a flagged stream uses zeros.
 __global__ void k_embed(StepArgs a, const float* __restrict__ emb_f, const int8_t* __restrict__ emb_q,
                         const float* __restrict__ emb_s, int d, int vocab, float* __restrict__ x) {
+    pdl_wait();
+    pdl_trigger();
     int b = blockIdx.x;
     if (b >= a.n) return;
     uint32_t tok = a.tokens[b], slot = a.slots[b];
@@ -112,10 +126,11 @@ __global__ void k_embed(StepArgs a, const float* __restrict__ emb_f, const int8_
         for (int j = threadIdx.x; j < d; j += blockDim.x) xb[j] = 0.0f;
         return;
     }
-    if (emb_q) {  // dequant_row_into (src/domain/gemv.rs:284-295): q * scale
-        const int8_t* qr = emb_q + (size_t)tok * d;
+    if (emb_q) {  // dequant_row_into (src/domain/gemv.rs:284-295): q * scale (tiled int8 rows)
+        const int vpad = round_up(vocab, 128);
         const float* sr = emb_s + (size_t)tok * (d / kGroup);
-        for (int j = threadIdx.x; j < d; j += blockDim.x) xb[j] = __fmul_rn((float)qr[j], sr[j / kGroup]);
+        for (int j = threadIdx.x; j < d; j += blockDim.x)
+            xb[j] = __fmul_rn((float)emb_q[wq_off(vpad, (int)tok, j)], sr[j / kGroup]);
     } else {
         const float* er = emb_f + (size_t)tok * d;
         for (int j = threadIdx.x; j < d; j += blockDim.x) xb[j] = er[j];
@@ -125,9 +140,9 @@ __global__ void k_embed(StepArgs a, const float* __restrict__ emb_f, const int8_
 // Activation sink of a norm / scan: f32 vector or the three Q8 digit planes.
 struct ActOut {
     float* f;       // [cap][K] f32, or nullptr
-    int8_t* q;      // [3][cap][K] digit planes, or nullptr
+    int8_t* q;      // tiled digit planes [K/64][3][cap_pad][64], or nullptr
     float* e;       // [cap][K/64] group scales 2^e
-    int cap;        // plane stride in streams
+    int cap_pad;    // streams per plane, rounded up to 64
     int K;
 };
 
@@ -137,6 +152,8 @@ struct ActOut {
 template <int NC>  // NC = d / 128 rounded up; d <= 128 * NC
 __global__ void k_norm(int n, const float* __restrict__ x, int d, const float* __restrict__ w,
                        const float* __restrict__ bias, ActOut out) {
+    pdl_wait();
+    pdl_trigger();
     int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     int lane = threadIdx.x & 31;
     if (b >= n) return;
@@ -210,11 +227,10 @@ __global__ void k_norm(int n, const float* __restrict__ x, int d, const float* _
             if (ok) {
                 Digits3 a0 = split_digits(o.x, ginv), a1 = split_digits(o.y, ginv);
                 Digits3 a2 = split_digits(o.z, ginv), a3 = split_digits(o.w, ginv);
-                size_t plane = (size_t)out.cap * out.K;
-                int8_t* base = out.q + (size_t)b * out.K + k;
-                *reinterpret_cast<int*>(base) = pack4(a0.d1, a1.d1, a2.d1, a3.d1);
-                *reinterpret_cast<int*>(base + plane) = pack4(a0.d2, a1.d2, a2.d2, a3.d2);
-                *reinterpret_cast<int*>(base + 2 * plane) = pack4(a0.d3, a1.d3, a2.d3, a3.d3);
+                // four consecutive columns stay inside one 16-byte chunk of the swizzled row
+                *reinterpret_cast<int*>(out.q + dq_off(out.cap_pad, 0, b, k)) = pack4(a0.d1, a1.d1, a2.d1, a3.d1);
+                *reinterpret_cast<int*>(out.q + dq_off(out.cap_pad, 1, b, k)) = pack4(a0.d2, a1.d2, a2.d2, a3.d2);
+                *reinterpret_cast<int*>(out.q + dq_off(out.cap_pad, 2, b, k)) = pack4(a0.d3, a1.d3, a2.d3, a3.d3);
                 if ((lane & 15) == 0) out.e[(size_t)b * (out.K / kGroup) + (k / kGroup)] = gs;
             }
         }
@@ -225,18 +241,54 @@ __global__ void k_norm(int n, const float* __restrict__ x, int d, const float* _
 // GEMV epilogues: called once per (row, stream) with the finished dot product.
 // ------------------------------------------------------------------------------------------
 
+// Each epilogue also has a chunked form, apply<CH>(row, b0, nb, v): the CH streams b0..b0+nb-1
+// of one row at once, with every load issued before any dependent arithmetic, so a thread that
+// owns a row keeps CH memory operations in flight instead of walking the streams one by one.
+
+// Stream metadata of a tile (slot and reset flag per stream), staged once per CTA; only the
+// in_proj epilogue reads it.
+struct TileMeta {
+    const uint32_t* slot;   // [BN] tile-relative
+    const uint32_t* fresh;  // [BN]
+};
+
 struct EpiStore {  // out[b][row] = v
     float* out;
     int ld;
+    __device__ __forceinline__ void stage(int, int, uint32_t*, uint32_t*) const {}
+    template <int CH>
+    __device__ __forceinline__ void apply(int row, int b0, int nb, const float (&v)[CH], TileMeta, int) const {
+        apply<CH>(row, b0, nb, v);
+    }
     __device__ __forceinline__ void operator()(int row, int b, float v) const { out[(size_t)b * ld + row] = v; }
+    template <int CH>
+    __device__ __forceinline__ void apply(int row, int b0, int nb, const float (&v)[CH]) const {
+#pragma unroll
+        for (int i = 0; i < CH; i++)
+            if (i < nb) out[(size_t)(b0 + i) * ld + row] = v[i];
+    }
 };
 
 struct EpiResidual {  // x[b][row] += v (src/infrastructure/mamba/model.rs:716-719)
     float* x;
     int ld;
+    __device__ __forceinline__ void stage(int, int, uint32_t*, uint32_t*) const {}
+    template <int CH>
+    __device__ __forceinline__ void apply(int row, int b0, int nb, const float (&v)[CH], TileMeta, int) const {
+        apply<CH>(row, b0, nb, v);
+    }
     __device__ __forceinline__ void operator()(int row, int b, float v) const {
         float* p = x + (size_t)b * ld + row;
         *p = __fadd_rn(*p, v);
+    }
+    template <int CH>
+    __device__ __forceinline__ void apply(int row, int b0, int nb, const float (&v)[CH]) const {
+        float old[CH];
+#pragma unroll
+        for (int i = 0; i < CH; i++) old[i] = i < nb ? x[(size_t)(b0 + i) * ld + row] : 0.0f;
+#pragma unroll
+        for (int i = 0; i < CH; i++)
+            if (i < nb) x[(size_t)(b0 + i) * ld + row] = __fadd_rn(old[i], v[i]);
     }
 };
 
@@ -252,6 +304,16 @@ struct EpiInProj {
     const float* conv_b;      // [di]
     float* conv_out;          // [stream][di]
     float* z;                 // [stream][di]
+
+    __device__ __forceinline__ float conv_silu(int j, float s0, float s1, float s2, float v) const {
+        float val = __fadd_rn(0.0f, __fmul_rn(s0, conv_t[j]));
+        val = __fadd_rn(val, __fmul_rn(s1, conv_t[di + j]));
+        val = __fadd_rn(val, __fmul_rn(s2, conv_t[2 * di + j]));
+        val = __fadd_rn(val, __fmul_rn(v, conv_t[3 * di + j]));
+        val = __fadd_rn(val, conv_b[j]);
+        return __fmul_rn(val, lane_sigmoid(val));
+    }
+
     __device__ __forceinline__ void operator()(int row, int b, float v) const {
         if (row >= di) {
             z[(size_t)b * di + (row - di)] = v;
@@ -267,15 +329,93 @@ struct EpiInProj {
             s1 = st[di];
             s2 = st[2 * di];
         }
-        float val = __fadd_rn(0.0f, __fmul_rn(s0, conv_t[j]));
-        val = __fadd_rn(val, __fmul_rn(s1, conv_t[di + j]));
-        val = __fadd_rn(val, __fmul_rn(s2, conv_t[2 * di + j]));
-        val = __fadd_rn(val, __fmul_rn(v, conv_t[3 * di + j]));
-        val = __fadd_rn(val, conv_b[j]);
         st[0] = s1;
         st[di] = s2;
         st[2 * di] = v;
-        conv_out[(size_t)b * di + j] = __fmul_rn(val, lane_sigmoid(val));
+        conv_out[(size_t)b * di + j] = conv_silu(j, s0, s1, s2, v);
+    }
+
+    // stage the slots and reset flags of streams b0..b0+nb-1 into tile-local arrays
+    __device__ __forceinline__ void stage(int b0, int nb, uint32_t* slot_s, uint32_t* fresh_s) const {
+        for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+            uint32_t sl = slots[b0 + i];
+            uint32_t rf = rflag[b0 + i];
+            slot_s[i] = sl;
+            fresh_s[i] = rf;
+        }
+    }
+
+    // chunk of CH streams, tile-relative index t0 = b0 - tile start, metadata from the staged arrays
+    template <int CH>
+    __device__ __forceinline__ void apply(int row, int b0, int nb, const float (&v)[CH], TileMeta meta,
+                                          int t0) const {
+        if (row >= di) {
+#pragma unroll
+            for (int i = 0; i < CH; i++)
+                if (i < nb) z[(size_t)(b0 + i) * di + (row - di)] = v[i];
+            return;
+        }
+        const int j = row;
+        float* st[CH];
+        bool live[CH], rd[CH];
+#pragma unroll
+        for (int i = 0; i < CH; i++) {
+            uint32_t slot = i < nb ? meta.slot[t0 + i] : 0xffffffffu;
+            live[i] = slot < (uint32_t)cap;
+            rd[i] = live[i] && meta.fresh[t0 + i] == 0;
+            st[i] = conv_state + (((size_t)layer * cap + (live[i] ? slot : 0)) * 3) * di + j;
+        }
+        float s0[CH], s1[CH], s2[CH];
+#pragma unroll
+        for (int i = 0; i < CH; i++) {
+            s0[i] = rd[i] ? st[i][0] : 0.0f;
+            s1[i] = rd[i] ? st[i][di] : 0.0f;
+            s2[i] = rd[i] ? st[i][2 * di] : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < CH; i++) {
+            if (!live[i]) continue;
+            st[i][0] = s1[i];
+            st[i][di] = s2[i];
+            st[i][2 * di] = v[i];
+            conv_out[(size_t)(b0 + i) * di + j] = conv_silu(j, s0[i], s1[i], s2[i], v[i]);
+        }
+    }
+
+    template <int CH>
+    __device__ __forceinline__ void apply(int row, int b0, int nb, const float (&v)[CH]) const {
+        if (row >= di) {
+#pragma unroll
+            for (int i = 0; i < CH; i++)
+                if (i < nb) z[(size_t)(b0 + i) * di + (row - di)] = v[i];
+            return;
+        }
+        const int j = row;
+        float* st[CH];
+        bool live[CH], fresh[CH];
+#pragma unroll
+        for (int i = 0; i < CH; i++) {
+            uint32_t slot = i < nb ? slots[b0 + i] : 0xffffffffu;
+            live[i] = slot < (uint32_t)cap;
+            fresh[i] = live[i] && rflag[b0 + i] != 0;
+            st[i] = conv_state + (((size_t)layer * cap + (live[i] ? slot : 0)) * 3) * di + j;
+        }
+        float s0[CH], s1[CH], s2[CH];
+#pragma unroll
+        for (int i = 0; i < CH; i++) {
+            bool rd = live[i] && !fresh[i];
+            s0[i] = rd ? st[i][0] : 0.0f;
+            s1[i] = rd ? st[i][di] : 0.0f;
+            s2[i] = rd ? st[i][2 * di] : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < CH; i++) {
+            if (!live[i]) continue;
+            st[i][0] = s1[i];
+            st[i][di] = s2[i];
+            st[i][2 * di] = v[i];
+            conv_out[(size_t)(b0 + i) * di + j] = conv_silu(j, s0[i], s1[i], s2[i], v[i]);
+        }
     }
 };
 
@@ -286,9 +426,11 @@ struct EpiInProj {
 // Grid: x = stream tiles (fastest, so CTAs reading the same weight rows run together and the
 // rows come from L2 after the first tile), y = row blocks of 8 * RW rows.
 // ------------------------------------------------------------------------------------------
-template <int RW, int NS, class Epi>
+template <int RW, int NS, int NCH, class Epi>
 __global__ void __launch_bounds__(256) k_gemv_f32(int M, int K, const float* __restrict__ W,
                                                   const float* __restrict__ act, int ld_act, int n, Epi epi) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ float4 smem_f4[];
     float* xs = reinterpret_cast<float*>(smem_f4);  // [NS][K]
     int b0 = blockIdx.x * NS;
@@ -308,25 +450,59 @@ __global__ void __launch_bounds__(256) k_gemv_f32(int M, int K, const float* __r
     for (int r = 0; r < RW; r++)
 #pragma unroll
         for (int s = 0; s < NS; s++) acc[r][s] = 0.0f;
-    int nch = (K + 127) >> 7;
-    for (int c = 0; c < nch; c++) {
-        int k = c * 128 + lane * 4;
-        if (k < K) {
-            float4 wv[RW];
+    if constexpr (NCH > 0) {
+        // all weight loads of the row(s) first (NCH x RW independent 16-byte loads per lane)
+        float4 wv[NCH][RW];
+#pragma unroll
+        for (int c = 0; c < NCH; c++) {
+            int k = c * 128 + lane * 4;
 #pragma unroll
             for (int r = 0; r < RW; r++)
-                wv[r] = (r0 + r < M) ? __ldg(reinterpret_cast<const float4*>(W + (size_t)(r0 + r) * K + k))
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                wv[c][r] = (k < K && r0 + r < M)
+                               ? __ldg(reinterpret_cast<const float4*>(W + (size_t)(r0 + r) * K + k))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
 #pragma unroll
-            for (int s = 0; s < NS; s++) {
-                if (s < ns) {
-                    float4 xv = *reinterpret_cast<const float4*>(xs + s * K + k);
+        for (int c = 0; c < NCH; c++) {
+            int k = c * 128 + lane * 4;
+            if (k < K) {
 #pragma unroll
-                    for (int r = 0; r < RW; r++) {
-                        acc[r][s] = __fmaf_rn(wv[r].x, xv.x, acc[r][s]);
-                        acc[r][s] = __fmaf_rn(wv[r].y, xv.y, acc[r][s]);
-                        acc[r][s] = __fmaf_rn(wv[r].z, xv.z, acc[r][s]);
-                        acc[r][s] = __fmaf_rn(wv[r].w, xv.w, acc[r][s]);
+                for (int s = 0; s < NS; s++) {
+                    if (s < ns) {
+                        float4 xv = *reinterpret_cast<const float4*>(xs + s * K + k);
+#pragma unroll
+                        for (int r = 0; r < RW; r++) {
+                            acc[r][s] = __fmaf_rn(wv[c][r].x, xv.x, acc[r][s]);
+                            acc[r][s] = __fmaf_rn(wv[c][r].y, xv.y, acc[r][s]);
+                            acc[r][s] = __fmaf_rn(wv[c][r].z, xv.z, acc[r][s]);
+                            acc[r][s] = __fmaf_rn(wv[c][r].w, xv.w, acc[r][s]);
+                        }
+                    }
+                }
+            }
+        }
+    } else {
+        // rolled chunk loop: the same per-element order, fewer registers
+        int nch = (K + 127) >> 7;
+        for (int c = 0; c < nch; c++) {
+            int k = c * 128 + lane * 4;
+            if (k < K) {
+                float4 wv[RW];
+#pragma unroll
+                for (int r = 0; r < RW; r++)
+                    wv[r] = (r0 + r < M) ? __ldg(reinterpret_cast<const float4*>(W + (size_t)(r0 + r) * K + k))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int s = 0; s < NS; s++) {
+                    if (s < ns) {
+                        float4 xv = *reinterpret_cast<const float4*>(xs + s * K + k);
+#pragma unroll
+                        for (int r = 0; r < RW; r++) {
+                            acc[r][s] = __fmaf_rn(wv[r].x, xv.x, acc[r][s]);
+                            acc[r][s] = __fmaf_rn(wv[r].y, xv.y, acc[r][s]);
+                            acc[r][s] = __fmaf_rn(wv[r].z, xv.z, acc[r][s]);
+                            acc[r][s] = __fmaf_rn(wv[r].w, xv.w, acc[r][s]);
+                        }
                     }
                 }
             }
@@ -355,7 +531,9 @@ __global__ void __launch_bounds__(256) k_gemv_f32(int M, int K, const float* __r
 template <int RW, int NS, int GI, class Epi>
 __global__ void __launch_bounds__(256) k_gemv_q8(int M, int K, const int8_t* __restrict__ Wq,
                                                  const float* __restrict__ Ws, const int8_t* __restrict__ actq,
-                                                 const float* __restrict__ acte, int cap, int n, Epi epi) {
+                                                 const float* __restrict__ acte, int cap_pad, int n, Epi epi) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ float4 smem_f4[];
     int8_t* dq = reinterpret_cast<int8_t*>(smem_f4);                  // [NS][3][K]
     float* de = reinterpret_cast<float*>(dq + (size_t)NS * 3 * K);    // [NS][G]
@@ -363,11 +541,10 @@ __global__ void __launch_bounds__(256) k_gemv_q8(int M, int K, const int8_t* __r
     int b0 = blockIdx.x * NS;
     int ns = min(NS, n - b0);
     int K16 = K >> 4;
-    size_t plane = (size_t)cap * K;
     for (int i = threadIdx.x; i < ns * 3 * K16; i += blockDim.x) {
         int s = i / (3 * K16), rem = i - s * 3 * K16, p = rem / K16, k16 = rem - p * K16;
         reinterpret_cast<int4*>(dq)[(s * 3 + p) * K16 + k16] =
-            reinterpret_cast<const int4*>(actq + p * plane + (size_t)(b0 + s) * K)[k16];
+            *reinterpret_cast<const int4*>(actq + dq_off(cap_pad, p, b0 + s, k16 * 16));
     }
     for (int i = threadIdx.x; i < ns * G; i += blockDim.x) {
         int s = i / G, g = i - s * G;
@@ -377,13 +554,14 @@ __global__ void __launch_bounds__(256) k_gemv_q8(int M, int K, const int8_t* __r
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int gs = lane >> 2, qt = lane & 3;
     int r0 = blockIdx.y * (8 * RW) + warp * RW;
+    const int mpad = round_up(M, 128);
 #pragma unroll 1
     for (int r = r0; r < min(r0 + RW, M); r++) {
         int4 wv[GI];
 #pragma unroll
         for (int gi = 0; gi < GI; gi++) {
             int g = gi * 8 + gs;
-            wv[gi] = g < G ? __ldg(reinterpret_cast<const int4*>(Wq + (size_t)r * K + g * kGroup + qt * 16))
+            wv[gi] = g < G ? __ldg(reinterpret_cast<const int4*>(Wq + wq_off(mpad, r, g * kGroup + qt * 16)))
                            : make_int4(0, 0, 0, 0);
         }
 #pragma unroll 1
@@ -426,12 +604,18 @@ __global__ void __launch_bounds__(256) k_gemv_q8(int M, int K, const int8_t* __r
 }
 
 // ------------------------------------------------------------------------------------------
-// Selective scan for one (stream, channel) per thread (scan_block + ssm_recurrence_d16_scalar,
-// src/infrastructure/mamba/model.rs:174-190, src/domain/tensor.rs:1301-1325):
+// Selective scan (scan_block + ssm_recurrence_d16_scalar, src/infrastructure/mamba/model.rs:174-190,
+// src/domain/tensor.rs:1301-1325), per (stream, channel):
 //   dt = softplus(dt_proj[j] . dt_raw + dt_bias[j])     (8-lane dot order of f32_rows)
 //   if |dt| >= 1e-6: s[n] = exp(0 - dt*A[n]) * s[n] + (dt*x) * B[n]   (A = exp(A_log))
 //   y = hsum_ssm(s[l]*C[l] + s[l+8]*C[l+8]) + D[j]*x;  gated = y * (z * sigmoid(z))
-// Grid (d_inner / 256, n), 256 threads; the gated vector leaves as f32 or Q8 digit planes.
+// Four threads share a channel: thread t owns the dot lanes {t, t+4} and the states
+// {t, t+4, t+8, t+12}.  The reference's fixed trees map onto two shuffle levels:
+//   hsum8     ((l0+l4)+(l2+l6)) + ((l1+l5)+(l3+l7)):  pair sums, xor 2, then xor 1
+//   hsum_ssm  ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7)):  pair sums, xor 1, then xor 2
+// so all four threads hold the reference's values.  A block is one 64-channel group of one
+// stream (grid (d_inner/64, n), 256 threads), which is also the quantisation group of the
+// out_proj activation digits.
 // ------------------------------------------------------------------------------------------
 struct ScanArgs {
     int di, dr, xr, cap, layer;
@@ -440,7 +624,7 @@ struct ScanArgs {
     const float* zp;       // [stream][xr] = (dt_raw, B, C)
     const float* conv_out; // [stream][di]
     const float* z;        // [stream][di]
-    const float* dt_w;     // [di][dr]
+    const float* dt_wt;    // [dr][di] (transposed dt_proj weights)
     const float* dt_b;     // [di]
     const float* a_t;      // [16][di]
     const float* dvec;     // [di]
@@ -448,80 +632,84 @@ struct ScanArgs {
 };
 
 __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ float4 smem_f4[];
     float* zs = reinterpret_cast<float*>(smem_f4);  // [xr]
     __shared__ float s_max[8];
-    int b = blockIdx.y;
-    int j = blockIdx.x * blockDim.x + threadIdx.x;
+    const int b = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = lane & 3;
+    const int j = blockIdx.x * 64 + warp * 8 + (lane >> 2);
+    const uint32_t slot = a.slots[b];
+    const bool ok = j < a.di && slot < (uint32_t)a.cap;
+    const bool fresh = a.rflag[b] != 0;
+    float* st = a.ssm + (((size_t)a.layer * a.cap + (ok ? slot : 0)) * kDState) * a.di + j;
+    // the recurrent state first: four coalesced loads in flight while dt is computed
+    float s[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) s[k] = (ok && !fresh) ? st[(size_t)(t + 4 * k) * a.di] : 0.0f;
     const float* zpb = a.zp + (size_t)b * a.xr;
     for (int i = threadIdx.x; i < a.xr; i += blockDim.x) zs[i] = zpb[i];
     __syncthreads();
-    uint32_t slot = a.slots[b];
-    bool ok = j < a.di && slot < (uint32_t)a.cap;
-    float gated = 0.0f;
-    if (ok) {
-        // dt_proj row in dot_avx2_order: 8 lanes over the 8-aligned body, hsum8, tail
-        const float* wr = a.dt_w + (size_t)j * a.dr;
-        float l[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        int body = a.dr & ~7;
-        for (int c = 0; c < body; c += 8) {
-#pragma unroll
-            for (int t = 0; t < 8; t++) l[t] = __fadd_rn(l[t], __fmul_rn(wr[c + t], zs[c + t]));
-        }
-        float s0 = __fadd_rn(l[0], l[4]), s1 = __fadd_rn(l[1], l[5]), s2 = __fadd_rn(l[2], l[6]),
-              s3 = __fadd_rn(l[3], l[7]);
-        float dt = __fadd_rn(__fadd_rn(s0, s2), __fadd_rn(s1, s3));
-        for (int c = body; c < a.dr; c++) dt = __fadd_rn(dt, __fmul_rn(wr[c], zs[c]));
-        dt = softplus(__fadd_rn(dt, a.dt_b[j]));
-
-        const float* B = zs + a.dr;
-        const float* C = zs + a.dr + kDState;
-        float xv = a.conv_out[(size_t)b * a.di + j];
-        float* st = a.ssm + (((size_t)a.layer * a.cap + slot) * kDState) * a.di + j;
-        float s[kDState];
-        bool fresh = a.rflag[b] != 0;
-#pragma unroll
-        for (int n2 = 0; n2 < kDState; n2++) s[n2] = fresh ? 0.0f : st[(size_t)n2 * a.di];
-        bool update = !(fabsf(dt) < 1e-6f);
-        if (update) {
-            float dtx = __fmul_rn(dt, xv);
-#pragma unroll
-            for (int n2 = 0; n2 < kDState; n2++) {
-                float da = lane_expf(__fsub_rn(0.0f, __fmul_rn(dt, a.a_t[(size_t)n2 * a.di + j])));
-                s[n2] = __fadd_rn(__fmul_rn(da, s[n2]), __fmul_rn(dtx, B[n2]));
-            }
-        }
-        if (update || fresh) {
-#pragma unroll
-            for (int n2 = 0; n2 < kDState; n2++) st[(size_t)n2 * a.di] = s[n2];
-        }
-        float ln[8];
-#pragma unroll
-        for (int t = 0; t < 8; t++) ln[t] = __fadd_rn(__fmul_rn(s[t], C[t]), __fmul_rn(s[t + 8], C[t + 8]));
-        float h0 = __fadd_rn(ln[0], ln[4]), h1 = __fadd_rn(ln[1], ln[5]), h2 = __fadd_rn(ln[2], ln[6]),
-              h3 = __fadd_rn(ln[3], ln[7]);
-        float y = __fadd_rn(__fadd_rn(__fadd_rn(h0, h1), __fadd_rn(h2, h3)), __fmul_rn(a.dvec[j], xv));
-        float zv = a.z[(size_t)b * a.di + j];
-        gated = __fmul_rn(y, __fmul_rn(zv, lane_sigmoid(zv)));
+    const int jj = ok ? j : 0;
+    float xv = a.conv_out[(size_t)b * a.di + jj];
+    float zv = a.z[(size_t)b * a.di + jj];
+    // dt_proj row: lanes t and t+4 of the 8-lane dot, then the hsum8 tree across the quad
+    const float* wt = a.dt_wt + jj;
+    float la = 0.0f, lb = 0.0f;
+    const int body = a.dr & ~7;
+    for (int c = 0; c < body; c += 8) {
+        la = __fadd_rn(la, __fmul_rn(wt[(size_t)(c + t) * a.di], zs[c + t]));
+        lb = __fadd_rn(lb, __fmul_rn(wt[(size_t)(c + t + 4) * a.di], zs[c + t + 4]));
     }
+    float pr = __fadd_rn(la, lb);
+    pr = __fadd_rn(pr, __shfl_xor_sync(0xffffffffu, pr, 2));
+    float dt = __fadd_rn(pr, __shfl_xor_sync(0xffffffffu, pr, 1));
+    for (int c = body; c < a.dr; c++) dt = __fadd_rn(dt, __fmul_rn(wt[(size_t)c * a.di], zs[c]));
+    dt = softplus(__fadd_rn(dt, a.dt_b[jj]));
+
+    const float* B = zs + a.dr;
+    const float* C = zs + a.dr + kDState;
+    const bool update = !(fabsf(dt) < 1e-6f);
+    if (update) {
+        float dtx = __fmul_rn(dt, xv);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            int n2 = t + 4 * k;
+            float da = lane_expf(__fsub_rn(0.0f, __fmul_rn(dt, a.a_t[(size_t)n2 * a.di + jj])));
+            s[k] = __fadd_rn(__fmul_rn(da, s[k]), __fmul_rn(dtx, B[n2]));
+        }
+    }
+    if (ok && (update || fresh)) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) st[(size_t)(t + 4 * k) * a.di] = s[k];
+    }
+    // lanes[t] = s[t]C[t] + s[t+8]C[t+8], lanes[t+4] likewise; h_t = lanes[t] + lanes[t+4]
+    float l0 = __fadd_rn(__fmul_rn(s[0], C[t]), __fmul_rn(s[2], C[t + 8]));
+    float l4 = __fadd_rn(__fmul_rn(s[1], C[t + 4]), __fmul_rn(s[3], C[t + 12]));
+    float h = __fadd_rn(l0, l4);
+    h = __fadd_rn(h, __shfl_xor_sync(0xffffffffu, h, 1));
+    h = __fadd_rn(h, __shfl_xor_sync(0xffffffffu, h, 2));
+    float y = __fadd_rn(h, __fmul_rn(a.dvec[jj], xv));
+    float gated = ok ? __fmul_rn(y, __fmul_rn(zv, lane_sigmoid(zv))) : 0.0f;
     if (out.f) {
-        if (ok) out.f[(size_t)b * out.K + j] = gated;
+        if (ok && t == 0) out.f[(size_t)b * out.K + j] = gated;
         return;
     }
-    // digit planes over 64-channel groups: two warps per group
-    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // digit planes over this block's 64 channels
     float m = warp_allmax(fabsf(gated));
     if (lane == 0) s_max[warp] = m;
     __syncthreads();
-    m = fmaxf(s_max[warp & ~1], s_max[warp | 1]);
-    if (!ok) return;
+    m = s_max[0];
+#pragma unroll
+    for (int w = 1; w < 8; w++) m = fmaxf(m, s_max[w]);
+    if (!ok || t != 0) return;
     float ginv, gs = group_scale(m, &ginv);
     Digits3 dg = split_digits(gated, ginv);
-    size_t plane = (size_t)out.cap * out.K;
-    int8_t* base = out.q + (size_t)b * out.K + j;
-    base[0] = (int8_t)dg.d1;
-    base[plane] = (int8_t)dg.d2;
-    base[2 * plane] = (int8_t)dg.d3;
+    out.q[dq_off(out.cap_pad, 0, b, j)] = (int8_t)dg.d1;
+    out.q[dq_off(out.cap_pad, 1, b, j)] = (int8_t)dg.d2;
+    out.q[dq_off(out.cap_pad, 2, b, j)] = (int8_t)dg.d3;
     if ((j & (kGroup - 1)) == 0) out.e[(size_t)b * (out.K / kGroup) + j / kGroup] = gs;
 }
 

@@ -159,16 +159,53 @@ __device__ __forceinline__ Digits3 split_digits(float x, float inv) {
     return {(int)d1, (int)d2, (int)d3};
 }
 
+// Exact int -> float for |a| < 2^22 without the conversion unit: the bits 0x4B400000 + a are
+// the float 1.5 * 2^23 + a (integer spacing there is 1), and subtracting 1.5 * 2^23 is exact.
+__device__ __forceinline__ float small_int_to_float(int a) {
+    return __fsub_rn(__int_as_float(0x4B400000 + a), 12582912.0f);
+}
+
 // Combine the three exact digit sums of one group: ((a1 + a2 * 2^-7) + a3 * 2^-14).
+// |a_i| <= 64 * 127 * 64 < 2^22, so each conversion is exact.
 __device__ __forceinline__ float digit_value(int a1, int a2, int a3) {
-    float v = __fadd_rn((float)a1, __fmul_rn((float)a2, 0.0078125f));
-    return __fadd_rn(v, __fmul_rn((float)a3, 6.103515625e-05f));
+    float v = __fadd_rn(small_int_to_float(a1), __fmul_rn(small_int_to_float(a2), 0.0078125f));
+    return __fadd_rn(v, __fmul_rn(small_int_to_float(a3), 6.103515625e-05f));
 }
 
 // One step of the sequential group accumulation of a row: acc + v * (w_scale * 2^e).
 __device__ __forceinline__ float group_accumulate(float acc, float v, float w_scale, float a_scale) {
     return __fadd_rn(acc, __fmul_rn(v, __fmul_rn(w_scale, a_scale)));
 }
+
+// ---- Tiled int8 layouts shared by the Q8 producers and consumers ---------------------------
+//
+// Rows of 64 bytes (one quantisation group) are stored in the tensor cores' 64-byte swizzle:
+// 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3).  Both int8 operands are laid out in
+// HBM exactly as a pipeline stage needs them in shared memory, so every stage is one contiguous
+// bulk copy (no per-row TMA requests):
+//   Q8 weights     [group][rows rounded up to 128][64 B]
+//   digit planes   [group][16-stream block][plane][16][64 B]  (streams rounded up to 64)
+// In the digit layout the three planes of any run of 16-stream blocks are contiguous, so one
+// copy brings a tile's B operand and one MMA multiplies all three planes (N = 3 x streams).
+__host__ __device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t byte) {
+    return (((byte >> 4) ^ ((row >> 1) & 3u)) << 4) | (byte & 15u);
+}
+
+__host__ __device__ __forceinline__ size_t wq_off(int rows_pad, int r, int k) {
+    return ((size_t)(k >> 6) * rows_pad + r) * 64 + swz64((uint32_t)r, (uint32_t)(k & 63));
+}
+
+__host__ __device__ __forceinline__ size_t dq_off(int cap_pad, int p, int b, int k) {
+    return ((((size_t)(k >> 6) * (cap_pad >> 4) + (b >> 4)) * 3 + p) * 16 + (b & 15)) * 64 +
+           swz64((uint32_t)b, (uint32_t)(k & 63));
+}
+
+__host__ __device__ __forceinline__ int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+// Programmatic dependent launch: wait for the preceding kernel of the stream (and its memory)
+// before touching anything it wrote, then let the next kernel start its own prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ int pack4(int a, int b, int c, int d) {
     return (a & 0xff) | ((b & 0xff) << 8) | ((c & 0xff) << 16) | ((d & 0xff) << 24);

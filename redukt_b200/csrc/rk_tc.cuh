@@ -2,10 +2,10 @@
 //
 // y[r][b] = sum_g scale[r][g] * 2^e[b][g] * (A1 + A2 * 2^-7 + A3 * 2^-14),
 //   A_i = sum_{c in group g} q[r][c] * digit_i[b][c]   (exact int32)
-// The int8 weights are the A operand (M = 128 rows per tile, K-major, straight from HBM by TMA);
-// the three int8 digit planes of the activations are B operands (N = streams, K-major).  Each
-// pipeline stage carries one 64-column quantisation group: 8 KB of weights + 3 x N x 64 B of
-// digits.  The MMA warp issues, per group, 2 K-steps x 3 planes of tcgen05.mma into three int32
+// The int8 weights are the A operand (M = 128 rows per tile, K-major); the three int8 digit
+// planes of the activations are B operands (N = streams, K-major).  Each pipeline stage carries
+// one 64-column quantisation group: 8 KB of weights + 3 x N x 64 B of digits, brought in by
+// bulk copies (cp.async.bulk) from operands that are stored pre-tiled and pre-swizzled in HBM.  The MMA warp issues, per group, 2 K-steps x 3 planes of tcgen05.mma into three int32
 // TMEM accumulators (double-buffered: group g+1 multiplies while the epilogue reads group g).
 // The epilogue warps read the accumulators with tcgen05.ld (thread = row = TMEM lane) and run
 // the same digit_value/group_accumulate sequence as the CUDA-core kernel, so both paths give the
@@ -16,8 +16,6 @@
 // Every wait is bounded: on timeout the CTA records an error word, stops issuing work, drains
 // the copies it started and frees its TMEM before returning.
 #pragma once
-#include <cuda.h>
-
 #include "rk_kernels.cuh"
 
 namespace rk {
@@ -25,28 +23,36 @@ namespace tc {
 
 constexpr int kBM = 128;      // rows per tile = TMEM lanes
 constexpr int kBK = 64;       // bytes of K per stage = one quantisation group
-constexpr int kStages = 4;
+template <int BN>
+constexpr int stages_for() { return BN == 16 ? 12 : 8; }  // deep enough to cover a ~2 us TMA round trip
 constexpr int kThreads = 192;
 constexpr int kAutoMinStreams = 4;   // below this the CUDA-core kernel is used
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any legitimate wait
+// Wait bound in SM clock cycles (about 2 s at the B200's 1.9 GHz boost clock, longer when the
+// clock is lower): far beyond any legitimate wait.  clock64 is a cheap per-SM counter.
+constexpr long long kWaitLimitCycles = 4000000000ll;
 
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
+template <int BN>
+struct TileCfg {
+    static constexpr int kBufs = BN == 16 ? 4 : 2;          // TMEM accumulator sets in flight
+    static constexpr int kColsUsed = kBufs * 3 * BN;
+    static constexpr uint32_t kCols = kColsUsed <= 128 ? 128u : (kColsUsed <= 256 ? 256u : 512u);
+};
 
 template <int BN>
 struct alignas(1024) Smem {
+    static constexpr int kStages = stages_for<BN>();
     int8_t a[kStages][kBM * kBK];         // 8 KB per stage, 1024-aligned (64B-swizzle atoms)
-    int8_t b[kStages][3][BN * kBK];       // digit planes
+    int8_t b[kStages][3 * BN * kBK];      // digit planes: [16-stream block][plane][16 rows][64 B]
     uint64_t full[kStages];
     uint64_t empty[kStages];
-    uint64_t tfull[2];
-    uint64_t tempty[2];
+    uint32_t slot[BN];                    // stream metadata of the tile (in_proj epilogue)
+    uint32_t fresh[BN];
+    uint64_t tfull[TileCfg<BN>::kBufs];
+    uint64_t tempty[TileCfg<BN>::kBufs];
     uint32_t tmem_base;
     int abort;
     float ae[BN * 32];                    // 2^e of the tile's streams for up to 32 groups
+    float ws[32 * kBM];                   // weight scales of the tile's rows, [group][row]
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -81,29 +87,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait; returns false (and raises the CTA abort flag) when the limit is reached or
 // another role of the CTA has aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-    uint64_t t0 = globaltimer_ns();
-    for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (uint32_t i = 1;; i++) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (*abort) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            *abort = 1;
-            return false;
+        if ((i & 255) == 0) {
+            if (*abort) return false;
+            if (clock64() - t0 > kWaitLimitCycles) {
+                *abort = 1;
+                return false;
+            }
         }
     }
 }
 
 // Bounded wait that ignores the abort flag (used to drain work already in flight).
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
-    uint64_t t0 = globaltimer_ns();
-    while (!mbar_try_wait(bar, parity) && globaltimer_ns() - t0 < kWaitLimitNs) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity) && clock64() - t0 < kWaitLimitCycles) {
     }
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
+// One contiguous bulk copy global -> shared (16-byte aligned, size a multiple of 16), completing
+// on `bar` with complete_tx.  The operands are stored pre-tiled in HBM (rk_math.cuh), so a whole
+// pipeline stage is one request instead of one request per 64-byte row.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
 }
 
 // Shared-memory matrix descriptor, K-major operand in the 64-byte swizzle layout:
@@ -120,9 +131,10 @@ __device__ __forceinline__ uint64_t sw64_desc(const void* p) {
 }
 
 // Instruction descriptor: D = s32, A = B = s8, both K-major, N x 128.
-template <int BN>
+template <int N>
 __device__ __forceinline__ uint32_t idesc_i8() {
-    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+    static_assert(N % 16 == 0 && N >= 16 && N <= 256, "M=128 needs N in 16..256, multiple of 16");
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
@@ -152,54 +164,105 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 
 template <int BN>
 __host__ __device__ constexpr uint32_t tmem_cols() {
-    return (2 * 3 * BN) <= 128 ? 128u : ((2 * 3 * BN) <= 256 ? 256u : 512u);
+    return TileCfg<BN>::kCols;
 }
 
 // Dynamic shared memory for a launch: enough for the tile, and enough that no more CTAs become
-// resident on one SM than its 512 TMEM columns can serve at once.
+// resident on one SM than its 512 TMEM columns can serve at once (at most 227 KB).
 template <int BN>
 constexpr size_t launch_smem() {
     constexpr size_t need = sizeof(Smem<BN>) + 1024;
     constexpr size_t per_sm = 512 / tmem_cols<BN>();
     constexpr size_t floor_bytes = (size_t)233472 / (per_sm + 1) + 1024;
-    return need > floor_bytes ? need : floor_bytes;
+    constexpr size_t want = need > floor_bytes ? need : floor_bytes;
+    static_assert(need <= 232448, "tile does not fit in shared memory");
+    return want > 232448 ? 232448 : want;
 }
 
 // One (128-row, BN-stream) output tile over all K groups of one Q8 projection.
 template <int BN, class Epi>
 __global__ void __launch_bounds__(kThreads, 1)
-k_proj_q8_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_act, int M, int K,
-             int cap, int n, const float* __restrict__ w_scale, const float* __restrict__ act_e, uint32_t* err,
-             Epi epi) {
+k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M, int K, int cap_pad, int n,
+             const float* __restrict__ w_scale, const float* __restrict__ act_e, uint32_t* err, Epi epi) {
     extern __shared__ uint8_t smem_raw[];
     Smem<BN>& S = *reinterpret_cast<Smem<BN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int kBufs = TileCfg<BN>::kBufs;
+    constexpr int kStages = Smem<BN>::kStages;
+    constexpr uint32_t kCols = TileCfg<BN>::kCols;
+    constexpr uint32_t kStageBytes = kBM * kBK + 3 * BN * kBK;
     const int G = K / kBK;
     const int n0 = blockIdx.x * BN;
     const int m0 = blockIdx.y * kBM;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    constexpr uint32_t kCols = tmem_cols<BN>();
+    const int npre = G < kStages ? G : kStages;
+    const int m_pad = round_up(M, kBM);
+    const int8_t* wtile = wq + (size_t)m0 * 64;  // row m0 of group 0 in the tiled layout
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) {
             mbar_init(&S.full[s], 1);
             mbar_init(&S.empty[s], 1);
         }
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < kBufs; i++) {
             mbar_init(&S.tfull[i], 1);
             mbar_init(&S.tempty[i], 128);
         }
         S.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        // weights are never written by the step: stream the first stages before the preceding
+        // kernel has finished
+        for (int g = 0; g < npre; g++) {
+            mbar_expect_tx(&S.full[g], kStageBytes);
+            bulk_load(S.a[g], wtile + (size_t)g * m_pad * 64, kBM * kBK, &S.full[g]);
+        }
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S.tmem_base)),
                      "r"(kCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    for (int i = threadIdx.x; i < BN * G; i += blockDim.x) {
-        int b = i / G, g = i - b * G;
-        S.ae[b * 32 + g] = (n0 + b < n) ? act_e[(size_t)(n0 + b) * G + g] : 0.0f;
+    {
+        // weight scales of the tile: every load issued before any store (no dependent chain)
+        constexpr int kMaxPer = (kBM * 32 + kThreads - 1) / kThreads;
+        float tmp[kMaxPer];
+        const int cnt = kBM * G;
+        const int rows_ok = (M - m0) * G;
+#pragma unroll
+        for (int k = 0; k < kMaxPer; k++) {
+            int i = threadIdx.x + k * kThreads;
+            tmp[k] = (i < cnt && i < rows_ok) ? __ldg(w_scale + (size_t)m0 * G + i) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < kMaxPer; k++) {
+            int i = threadIdx.x + k * kThreads;
+            if (i < cnt) {
+                int r = i / G, g = i - r * G;
+                S.ws[g * kBM + r] = tmp[k];
+            }
+        }
     }
+    pdl_wait();
+    pdl_trigger();
+    {
+        constexpr int kMaxPer = (BN * 32 + kThreads - 1) / kThreads;
+        float tmp[kMaxPer];
+        const int cnt = BN * G;
+#pragma unroll
+        for (int k = 0; k < kMaxPer; k++) {
+            int i = threadIdx.x + k * kThreads;
+            int b = i / G;
+            tmp[k] = (i < cnt && n0 + b < n) ? act_e[(size_t)n0 * G + i] : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < kMaxPer; k++) {
+            int i = threadIdx.x + k * kThreads;
+            if (i < cnt) {
+                int b = i / G, g = i - b * G;
+                S.ae[b * 32 + g] = tmp[k];
+            }
+        }
+    }
+    epi.stage(n0, min(BN, n - n0), S.slot, S.fresh);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -208,91 +271,143 @@ k_proj_q8_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ C
 
     if (warp == 0) {
         if (lane == 0) {
-            constexpr uint32_t kStageBytes = kBM * kBK + 3 * BN * kBK;
             int issued = 0;
             for (int g = 0; g < G; g++) {
                 int s = g % kStages;
                 uint32_t ph = (g / kStages) & 1;
-                if (!mbar_wait(&S.empty[s], ph ^ 1, abort)) break;
-                mbar_expect_tx(&S.full[s], kStageBytes);
-                tma_load_2d(S.a[s], &tm_w, g * kBK, m0, &S.full[s]);
-#pragma unroll
-                for (int p = 0; p < 3; p++) tma_load_2d(S.b[s][p], &tm_act, g * kBK, p * cap + n0, &S.full[s]);
+                if (g >= npre) {
+                    if (!mbar_wait(&S.empty[s], ph ^ 1, abort)) break;
+                    mbar_expect_tx(&S.full[s], kStageBytes);
+                    bulk_load(S.a[s], wtile + (size_t)g * m_pad * 64, kBM * kBK, &S.full[s]);
+                }
+                bulk_load(S.b[s], dq + ((size_t)g * (cap_pad >> 4) + (n0 >> 4)) * 3 * 16 * 64, 3 * BN * kBK, &S.full[s]);
                 issued = g + 1;
             }
             if (*abort) {  // drain the copies this CTA started before its shared memory goes away
-                for (int g = (issued > kStages ? issued - kStages : 0); g < issued; g++)
-                    mbar_drain(&S.full[g % kStages], (g / kStages) & 1);
+                int from = issued > kStages ? issued - kStages : 0;
+                int to = issued > npre ? issued : npre;  // the prefetched weight stages count too
+                for (int g = from; g < to; g++) mbar_drain(&S.full[g % kStages], (g / kStages) & 1);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = idesc_i8<BN>();
+            const uint32_t idesc = idesc_i8<3 * BN>();
             int last = -1;
             for (int g = 0; g < G; g++) {
                 int s = g % kStages;
                 uint32_t ph = (g / kStages) & 1;
-                int buf = g & 1;
-                uint32_t bph = (g >> 1) & 1;
+                int buf = g % kBufs;
+                uint32_t bph = (g / kBufs) & 1;
                 if (!mbar_wait(&S.full[s], ph, abort)) break;
                 if (!mbar_wait(&S.tempty[buf], bph ^ 1, abort)) break;
                 tc_fence_after();
+                // one MMA per K-step: the three digit planes are stacked along N, so accumulator
+                // column (16-stream block u, plane p, stream j) = 48u + 16p + j
                 uint32_t dbase = tmem + (uint32_t)(buf * 3 * BN);
 #pragma unroll
-                for (int p = 0; p < 3; p++) {
-#pragma unroll
-                    for (int ks = 0; ks < 2; ks++) {
-                        uint64_t ad = sw64_desc(S.a[s] + ks * 32);
-                        uint64_t bd = sw64_desc(S.b[s][p] + ks * 32);
-                        mma_i8(dbase + (uint32_t)(p * BN), ad, bd, idesc, (uint32_t)ks);
-                    }
-                }
+                for (int ks = 0; ks < 2; ks++)
+                    mma_i8(dbase, sw64_desc(S.a[s] + ks * 32), sw64_desc(S.b[s] + ks * 32), idesc, (uint32_t)ks);
                 mma_commit(&S.empty[s]);
                 mma_commit(&S.tfull[buf]);
                 last = g;
             }
             // the accumulators must be written before TMEM is released, also on abort
-            if (last >= 0) mbar_drain(&S.tfull[last & 1], (last >> 1) & 1);
+            if (last >= 0) mbar_drain(&S.tfull[last % kBufs], (last / kBufs) & 1);
         }
         __syncwarp();
     } else {
         // epilogue: thread owns one output row (TMEM lane) and BN running sums
         const int quad = warp & 3;
-        const int row = m0 + quad * 32 + lane;
+        const int rl = quad * 32 + lane;
+        const int row = m0 + rl;
         const bool row_ok = row < M;
         const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
         float acc[BN];
 #pragma unroll
         for (int b = 0; b < BN; b++) acc[b] = 0.0f;
-        for (int g = 0; g < G; g++) {
-            int buf = g & 1;
-            uint32_t bph = (g >> 1) & 1;
-            // warp-uniform decision: tcgen05.ld below needs the whole warp converged
-            bool ok = __all_sync(0xffffffffu, mbar_wait(&S.tfull[buf], bph, abort));
-            if (!ok) break;
-            tc_fence_after();
-            float wsg = row_ok ? __ldg(w_scale + (size_t)row * G + g) : 0.0f;
-            uint32_t base = tmem + lane_off + (uint32_t)(buf * 3 * BN);
+        if constexpr (BN > 32) {
+            // wide tiles: one group at a time (the double buffer would not fit in registers)
+            for (int g = 0; g < G; g++) {
+                const int buf = g % kBufs;
+                bool ok = __all_sync(0xffffffffu, mbar_wait(&S.tfull[buf], (g / kBufs) & 1, abort));
+                if (!ok) break;
+                tc_fence_after();
+                const float wsg = S.ws[g * kBM + rl];
+                const uint32_t base = tmem + lane_off + (uint32_t)(buf * 3 * BN);
 #pragma unroll
-            for (int c = 0; c < BN / 16; c++) {
-                int a1[16], a2[16], a3[16];
-                tmem_ld16(base + (uint32_t)(c * 16), a1);
-                tmem_ld16(base + (uint32_t)(BN + c * 16), a2);
-                tmem_ld16(base + (uint32_t)(2 * BN + c * 16), a3);
+                for (int c = 0; c < BN / 16; c++) {
+                    int a1[16], a2[16], a3[16];
+                    tmem_ld16(base + (uint32_t)(c * 48), a1);
+                    tmem_ld16(base + (uint32_t)(c * 48 + 16), a2);
+                    tmem_ld16(base + (uint32_t)(c * 48 + 32), a3);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        int b = c * 16 + j;
+                        acc[b] = group_accumulate(acc[b], digit_value(a1[j], a2[j], a3[j]), wsg, S.ae[b * 32 + g]);
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(&S.tempty[buf]);
+            }
+        } else {
+        // software pipeline: the accumulators of group g+1 are loaded from TMEM while group g is
+            // combined (tcgen05.ld is asynchronous until tcgen05.wait::ld)
+            int cur[3][BN], nxt[3][BN];
+            bool have = __all_sync(0xffffffffu, mbar_wait(&S.tfull[0], 0, abort));
+            if (have) {
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < BN / 16; c++)
+#pragma unroll
+                    for (int p = 0; p < 3; p++)
+                        tmem_ld16(tmem + lane_off + (uint32_t)(c * 48 + p * 16), *reinterpret_cast<int(*)[16]>(&cur[p][c * 16]));
                 tmem_wait_ld();
+            }
+            for (int g = 0; have && g < G; g++) {
+                const int buf = g % kBufs;
+                bool more = false;
+                if (g + 1 < G) {
+                    const int nb = (g + 1) % kBufs;
+                    more = __all_sync(0xffffffffu, mbar_wait(&S.tfull[nb], ((g + 1) / kBufs) & 1, abort));
+                    if (more) {
+                        tc_fence_after();
+                        const uint32_t base = tmem + lane_off + (uint32_t)(nb * 3 * BN);
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    int b = c * 16 + j;
-                    acc[b] = group_accumulate(acc[b], digit_value(a1[j], a2[j], a3[j]), wsg, S.ae[b * 32 + g]);
+                        for (int c = 0; c < BN / 16; c++)
+#pragma unroll
+                            for (int p = 0; p < 3; p++)
+                                tmem_ld16(base + (uint32_t)(c * 48 + p * 16), *reinterpret_cast<int(*)[16]>(&nxt[p][c * 16]));
+                    }
+                }
+                const float wsg = S.ws[g * kBM + rl];
+#pragma unroll
+                for (int b = 0; b < BN; b++)
+                    acc[b] = group_accumulate(acc[b], digit_value(cur[0][b], cur[1][b], cur[2][b]), wsg, S.ae[b * 32 + g]);
+                tc_fence_before();
+                mbar_arrive(&S.tempty[buf]);
+                if (g + 1 < G) {
+                    if (!more) {
+                        have = false;
+                        break;
+                    }
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int p = 0; p < 3; p++)
+#pragma unroll
+                        for (int b = 0; b < BN; b++) cur[p][b] = nxt[p][b];
                 }
             }
-            tc_fence_before();
-            mbar_arrive(&S.tempty[buf]);
         }
         if (!*abort && row_ok) {
 #pragma unroll
-            for (int b = 0; b < BN; b++)
-                if (n0 + b < n) epi(row, n0 + b, acc[b]);
+            for (int c = 0; c < BN / 8; c++) {
+                float v[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++) v[i] = acc[c * 8 + i];
+                int b0 = n0 + c * 8;
+                if (b0 < n) epi.template apply<8>(row, b0, min(8, n - b0), v, TileMeta{S.slot, S.fresh}, c * 8);
+            }
         }
     }
     tc_fence_before();
