@@ -138,6 +138,22 @@ int32_t redukt_b200_kernel_times(int32_t enable, double* ms, uint32_t* launches,
  * n slots and overwrites its scratch and the state of slots 0..n-1. */
 int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* ms_per_launch);
 
+/* Softmax of n_rows rows of vocab logits, device memory in and out, with no allocation.
+ * No counterpart in the reference: redukt's plugin ABI returns logits and the host does the
+ * softmax.  This entry point is for callers that must not allocate device memory while they
+ * run: code recording a CUDA graph (cudaMalloc cannot be captured), hosts that run on a fixed
+ * device-memory budget or a caching allocator and forbid allocation on the decode path.
+ * Its per-row scratch lives in a fixed array inside the library (256 KiB on every GPU that
+ * loads it, held until the process exits), so it handles at most 1024 rows of at most 65536
+ * logits; larger requests return INVALID_ARGUMENT.  Results are the same as the probability pass
+ * of redukt_backend_forward_batch_probs.  Work is enqueued on cuda_stream (a cudaStream_t; NULL =
+ * the legacy default stream) and not synchronised.  The first call on a device looks up the
+ * array's address on that device; make that first call before any stream capture.  All calls
+ * share the one array: calls whose work overlaps on the GPU (other streams, other threads)
+ * race and must be serialised by the caller.  Needs no model loaded. */
+int32_t redukt_b200_softmax_noalloc(const float* d_logits, uint32_t n_rows, uint32_t vocab, float* d_probs,
+                                    void* cuda_stream);
+
 /* Last error message of this library (empty string when none). */
 const char* redukt_b200_last_error(void);
 

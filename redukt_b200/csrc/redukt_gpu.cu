@@ -12,6 +12,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <new>
 #include <set>
 #include <string>
@@ -805,6 +806,23 @@ std::string rbin_path(const uint8_t* weights_path) {
     return p;
 }
 
+// ------------------------------------------------------------------------------------------
+// Probability pass without allocation (redukt_b200_softmax_noalloc).
+//
+// The pass needs scratch for one (max, sum) partial per 2048-logit tile of each row.  Here that
+// scratch is a fixed array in the library's own device memory, so the entry point never calls
+// cudaMalloc.  The array exists once per GPU that loads the library, for the life of the process.
+// ------------------------------------------------------------------------------------------
+constexpr uint32_t kNoAllocMaxRows = 1024;
+constexpr uint32_t kNoAllocMaxVocab = 65536;
+constexpr uint32_t kNoAllocMaxParts = kNoAllocMaxVocab / kSoftmaxTile;  // 32 tiles of 2048 logits
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocMaxRows * kNoAllocMaxParts * 2];
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {};  // device address of g_noalloc_scratch, per device
+
 }  // namespace
 
 // ==========================================================================================
@@ -1154,6 +1172,48 @@ int32_t redukt_b200_set_option(const char* key, int64_t value) {
         return BACKEND_OK;
     }
     return BACKEND_INVALID_ARGUMENT;
+}
+
+// See include/redukt_gpu.h.  The first call on a device looks up the scratch array's device
+// address on that device (cudaGetSymbolAddress, with that device current) and caches it.
+int32_t redukt_b200_softmax_noalloc(const float* d_logits, uint32_t n_rows, uint32_t vocab, float* d_probs,
+                                    void* cuda_stream) {
+    if (!d_logits || !d_probs) return BACKEND_INVALID_ARGUMENT;
+    if (n_rows == 0) return BACKEND_OK;
+    if (n_rows > kNoAllocMaxRows || vocab == 0 || vocab > kNoAllocMaxVocab) {
+        set_err("softmax_noalloc: %u rows x %u logits exceeds the fixed scratch (at most %u rows of at most %u logits)",
+                n_rows, vocab, kNoAllocMaxRows, kNoAllocMaxVocab);
+        return BACKEND_INVALID_ARGUMENT;
+    }
+    int dev = -1;
+    CK(cudaGetDevice(&dev), BACKEND_FORWARD_FAILED);
+    if (dev < 0 || dev >= kNoAllocMaxDevices) {
+        set_err("softmax_noalloc: device ordinal %d is out of range", dev);
+        return BACKEND_INVALID_ARGUMENT;
+    }
+    float* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void* addr = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+            if (e != cudaSuccess || !addr) {
+                set_err("softmax_noalloc: cudaGetSymbolAddress failed on device %d (%s)", dev, cudaGetErrorString(e));
+                return BACKEND_FORWARD_FAILED;
+            }
+            g_noalloc_ptr[dev] = static_cast<float*>(addr);
+        }
+        scratch = g_noalloc_ptr[dev];
+    }
+    // every (row, tile) partial is written by the first kernel before the second reads it, so
+    // nothing left in the array by an earlier call is ever read
+    const int parts = (int)((vocab + kSoftmaxTile - 1) / kSoftmaxTile);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(cuda_stream);
+    k_softmax_partial<<<dim3(parts, n_rows), 256, 0, st>>>(d_logits, (int)vocab, scratch, parts);
+    k_softmax_final<<<dim3(std::max(1, std::min(64, (int)vocab / 1024)), n_rows), 256, 0, st>>>(
+        d_logits, (int)vocab, scratch, parts, d_probs);
+    CK(cudaGetLastError(), BACKEND_FORWARD_FAILED);
+    return BACKEND_OK;
 }
 
 const char* redukt_b200_last_error(void) { return g_err; }

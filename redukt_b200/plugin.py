@@ -33,7 +33,7 @@ V2_SYMBOLS = ("redukt_backend_abi_version", "redukt_backend_batch_init", "redukt
 EXT_SYMBOLS = ("redukt_backend_set_reset_every", "redukt_backend_forward_batch_probs",
                "redukt_b200_forward_batch_device", "redukt_b200_device_error", "redukt_b200_get_state",
                "redukt_b200_get_q8", "redukt_b200_info", "redukt_b200_set_option", "redukt_b200_kernel_times",
-               "redukt_b200_time_kernel", "redukt_b200_last_error")
+               "redukt_b200_time_kernel", "redukt_b200_softmax_noalloc", "redukt_b200_last_error")
 KERNEL_CLASSES = ("embed", "norm", "in_proj", "x_proj", "scan", "out_proj", "head", "softmax")
 
 
@@ -134,7 +134,15 @@ class PluginLibrary:
             L.redukt_b200_kernel_times.restype = i32
             L.redukt_b200_time_kernel.argtypes = [i32, u32, u32, ctypes.POINTER(ctypes.c_float)]
             L.redukt_b200_time_kernel.restype = i32
+            L.redukt_b200_softmax_noalloc.argtypes = [vp, u32, u32, vp, vp]
+            L.redukt_b200_softmax_noalloc.restype = i32
             L.redukt_b200_last_error.argtypes, L.redukt_b200_last_error.restype = [], ctypes.c_char_p
+
+    def softmax_noalloc(self, d_logits: int, n_rows: int, vocab: int, d_probs: int, stream: int = 0) -> BackendResult:
+        """Row softmax of device logits into device probabilities without any allocation
+        (redukt_b200_softmax_noalloc); raw device addresses, stream 0 = legacy default stream."""
+        return BackendResult.from_code(self.lib.redukt_b200_softmax_noalloc(d_logits, n_rows, vocab, d_probs,
+                                                                            stream or None))
 
     def last_error(self) -> str:
         if not self.has_ext:
