@@ -496,7 +496,7 @@ void project_tc_bn(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st)
     size_t smem = tc::launch_smem<BN>();
     allow_smem(k, smem);
     dim3 grid((n + BN - 1) / BN, (m.rows + tc::kBM - 1) / tc::kBM);
-    launch(k, grid, dim3(tc::kThreads), smem, st, (const int8_t*)m.q, (const int8_t*)p.act_q, m.rows, m.cols,
+    launch(k, grid, dim3(tc::TileCfg<BN>::kThreads), smem, st, (const int8_t*)m.q, (const int8_t*)p.act_q, m.rows, m.cols,
            p.cap_pad, n, (const float*)m.s, (const float*)p.act_e, G.d_err, epi);
 }
 
@@ -512,6 +512,13 @@ void project(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st) {
     } else {
         gemv_q8(m, p.act_q, p.act_e, p.cap_pad, n, epi, st);
     }
+}
+
+// Four threads per channel while the batch is small (latency), one when it is large (no repeated
+// per-channel work); both give the same bits.
+void launch_scan(const ScanArgs& sc, const ActOut& ao, int n, cudaStream_t st) {
+    if (n <= 64) launch(k_scan<4>, dim3(G.di / 64, n), dim3(256), G.xr * sizeof(float), st, sc, ao);
+    else launch(k_scan<1>, dim3((G.di + 255) / 256, n), dim3(256), G.xr * sizeof(float), st, sc, ao);
 }
 
 void launch_norm(const Pool& p, int n, const float* w, const float* b, int K_out, cudaStream_t st) {
@@ -653,7 +660,7 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
             ActOut ao{p.act_f, p.act_q, p.act_e, p.cap_pad, G.di};
             if (G.profile != kF32) ao.f = nullptr;
             else ao.q = nullptr;
-            launch(k_scan, dim3(G.di / 64, n), dim3(256), G.xr * sizeof(float), st, sc, ao);
+            launch_scan(sc, ao, n, st);
         }
         {
             KScope k(kKOutProj, st);
@@ -1096,7 +1103,7 @@ int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* m
                     ActOut ao{p.act_f, p.act_q, p.act_e, p.cap_pad, G.di};
                     if (G.profile != kF32) ao.f = nullptr;
                     else ao.q = nullptr;
-                    launch(k_scan, dim3(G.di / 64, nn), dim3(256), G.xr * sizeof(float), st, sc, ao);
+                    launch_scan(sc, ao, nn, st);
                 }
                 if (cls == kKOutProj) project(L.out_proj, p, nn, EpiResidual{p.x, G.d}, st);
                 launches++;

@@ -631,41 +631,60 @@ struct ScanArgs {
     float* ssm;            // [layer][slot][16][di]
 };
 
+// One thread per channel (large batches: no repeated work) or four (small batches: shorter
+// dependency chains per thread).  Both evaluate the same trees in the same order.
+template <int TPC>
 __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
     pdl_wait();
     pdl_trigger();
     extern __shared__ float4 smem_f4[];
     float* zs = reinterpret_cast<float*>(smem_f4);  // [xr]
     __shared__ float s_max[8];
+    constexpr int kCh = 256 / TPC;           // channels per block
+    constexpr int kSt = kDState / TPC;       // states per thread
     const int b = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = lane & 3;
-    const int j = blockIdx.x * 64 + warp * 8 + (lane >> 2);
+    const int t = TPC == 1 ? 0 : (lane & 3);
+    const int jl = TPC == 1 ? threadIdx.x : warp * 8 + (lane >> 2);
+    const int j = blockIdx.x * kCh + jl;
     const uint32_t slot = a.slots[b];
     const bool ok = j < a.di && slot < (uint32_t)a.cap;
     const bool fresh = a.rflag[b] != 0;
     float* st = a.ssm + (((size_t)a.layer * a.cap + (ok ? slot : 0)) * kDState) * a.di + j;
-    // the recurrent state first: four coalesced loads in flight while dt is computed
-    float s[4];
+    // the recurrent state first: coalesced loads in flight while dt is computed
+    float s[kSt];
 #pragma unroll
-    for (int k = 0; k < 4; k++) s[k] = (ok && !fresh) ? st[(size_t)(t + 4 * k) * a.di] : 0.0f;
+    for (int k = 0; k < kSt; k++) s[k] = (ok && !fresh) ? st[(size_t)(t + TPC * k) * a.di] : 0.0f;
     const float* zpb = a.zp + (size_t)b * a.xr;
     for (int i = threadIdx.x; i < a.xr; i += blockDim.x) zs[i] = zpb[i];
     __syncthreads();
     const int jj = ok ? j : 0;
-    float xv = a.conv_out[(size_t)b * a.di + jj];
-    float zv = a.z[(size_t)b * a.di + jj];
-    // dt_proj row: lanes t and t+4 of the 8-lane dot, then the hsum8 tree across the quad
+    const float xv = a.conv_out[(size_t)b * a.di + jj];
+    const float zv = a.z[(size_t)b * a.di + jj];
+    // dt_proj row, 8-lane dot order: lane l accumulates columns c + l of the 8-aligned body
     const float* wt = a.dt_wt + jj;
-    float la = 0.0f, lb = 0.0f;
     const int body = a.dr & ~7;
-    for (int c = 0; c < body; c += 8) {
-        la = __fadd_rn(la, __fmul_rn(wt[(size_t)(c + t) * a.di], zs[c + t]));
-        lb = __fadd_rn(lb, __fmul_rn(wt[(size_t)(c + t + 4) * a.di], zs[c + t + 4]));
+    float dt;
+    if constexpr (TPC == 1) {
+        float l[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int c = 0; c < body; c += 8) {
+#pragma unroll
+            for (int q = 0; q < 8; q++) l[q] = __fadd_rn(l[q], __fmul_rn(wt[(size_t)(c + q) * a.di], zs[c + q]));
+        }
+        // hsum8: ((l0+l4)+(l2+l6)) + ((l1+l5)+(l3+l7))
+        dt = __fadd_rn(__fadd_rn(__fadd_rn(l[0], l[4]), __fadd_rn(l[2], l[6])),
+                       __fadd_rn(__fadd_rn(l[1], l[5]), __fadd_rn(l[3], l[7])));
+    } else {
+        // this thread holds lanes t and t+4; the quad finishes hsum8 with xor 2 then xor 1
+        float la = 0.0f, lb = 0.0f;
+        for (int c = 0; c < body; c += 8) {
+            la = __fadd_rn(la, __fmul_rn(wt[(size_t)(c + t) * a.di], zs[c + t]));
+            lb = __fadd_rn(lb, __fmul_rn(wt[(size_t)(c + t + 4) * a.di], zs[c + t + 4]));
+        }
+        float pr = __fadd_rn(la, lb);
+        pr = __fadd_rn(pr, __shfl_xor_sync(0xffffffffu, pr, 2));
+        dt = __fadd_rn(pr, __shfl_xor_sync(0xffffffffu, pr, 1));
     }
-    float pr = __fadd_rn(la, lb);
-    pr = __fadd_rn(pr, __shfl_xor_sync(0xffffffffu, pr, 2));
-    float dt = __fadd_rn(pr, __shfl_xor_sync(0xffffffffu, pr, 1));
     for (int c = body; c < a.dr; c++) dt = __fadd_rn(dt, __fmul_rn(wt[(size_t)c * a.di], zs[c]));
     dt = softplus(__fadd_rn(dt, a.dt_b[jj]));
 
@@ -673,37 +692,50 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
     const float* C = zs + a.dr + kDState;
     const bool update = !(fabsf(dt) < 1e-6f);
     if (update) {
-        float dtx = __fmul_rn(dt, xv);
+        const float dtx = __fmul_rn(dt, xv);
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            int n2 = t + 4 * k;
-            float da = lane_expf(__fsub_rn(0.0f, __fmul_rn(dt, a.a_t[(size_t)n2 * a.di + jj])));
+        for (int k = 0; k < kSt; k++) {
+            const int n2 = t + TPC * k;
+            const float da = lane_expf(__fsub_rn(0.0f, __fmul_rn(dt, a.a_t[(size_t)n2 * a.di + jj])));
             s[k] = __fadd_rn(__fmul_rn(da, s[k]), __fmul_rn(dtx, B[n2]));
         }
     }
     if (ok && (update || fresh)) {
 #pragma unroll
-        for (int k = 0; k < 4; k++) st[(size_t)(t + 4 * k) * a.di] = s[k];
+        for (int k = 0; k < kSt; k++) st[(size_t)(t + TPC * k) * a.di] = s[k];
     }
-    // lanes[t] = s[t]C[t] + s[t+8]C[t+8], lanes[t+4] likewise; h_t = lanes[t] + lanes[t+4]
-    float l0 = __fadd_rn(__fmul_rn(s[0], C[t]), __fmul_rn(s[2], C[t + 8]));
-    float l4 = __fadd_rn(__fmul_rn(s[1], C[t + 4]), __fmul_rn(s[3], C[t + 12]));
-    float h = __fadd_rn(l0, l4);
-    h = __fadd_rn(h, __shfl_xor_sync(0xffffffffu, h, 1));
-    h = __fadd_rn(h, __shfl_xor_sync(0xffffffffu, h, 2));
-    float y = __fadd_rn(h, __fmul_rn(a.dvec[jj], xv));
-    float gated = ok ? __fmul_rn(y, __fmul_rn(zv, lane_sigmoid(zv))) : 0.0f;
+    // y = hsum_ssm(lanes) + D x, lanes[l] = s[l] C[l] + s[l+8] C[l+8],
+    // hsum_ssm = ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7))
+    float h;
+    if constexpr (TPC == 1) {
+        float ln[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) ln[q] = __fadd_rn(__fmul_rn(s[q], C[q]), __fmul_rn(s[q + 8], C[q + 8]));
+        h = __fadd_rn(__fadd_rn(__fadd_rn(ln[0], ln[4]), __fadd_rn(ln[1], ln[5])),
+                      __fadd_rn(__fadd_rn(ln[2], ln[6]), __fadd_rn(ln[3], ln[7])));
+    } else {
+        // states t, t+4, t+8, t+12 here: lanes t and t+4, then xor 1 and xor 2 across the quad
+        const float l0 = __fadd_rn(__fmul_rn(s[0], C[t]), __fmul_rn(s[2], C[t + 8]));
+        const float l4 = __fadd_rn(__fmul_rn(s[1], C[t + 4]), __fmul_rn(s[3], C[t + 12]));
+        h = __fadd_rn(l0, l4);
+        h = __fadd_rn(h, __shfl_xor_sync(0xffffffffu, h, 1));
+        h = __fadd_rn(h, __shfl_xor_sync(0xffffffffu, h, 2));
+    }
+    const float y = __fadd_rn(h, __fmul_rn(a.dvec[jj], xv));
+    const float gated = ok ? __fmul_rn(y, __fmul_rn(zv, lane_sigmoid(zv))) : 0.0f;
     if (out.f) {
         if (ok && t == 0) out.f[(size_t)b * out.K + j] = gated;
         return;
     }
-    // digit planes over this block's 64 channels
+    // digit planes over 64-channel groups: 64 / (32 / TPC) warps per group
+    constexpr int kWarpsPerGroup = 64 * TPC / 32;
     float m = warp_allmax(fabsf(gated));
     if (lane == 0) s_max[warp] = m;
     __syncthreads();
-    m = s_max[0];
+    const int w0 = (warp / kWarpsPerGroup) * kWarpsPerGroup;
+    m = s_max[w0];
 #pragma unroll
-    for (int w = 1; w < 8; w++) m = fmaxf(m, s_max[w]);
+    for (int w = 1; w < kWarpsPerGroup; w++) m = fmaxf(m, s_max[w0 + w]);
     if (!ok || t != 0) return;
     float ginv, gs = group_scale(m, &ginv);
     Digits3 dg = split_digits(gated, ginv);

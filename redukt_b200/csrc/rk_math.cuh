@@ -167,9 +167,11 @@ __device__ __forceinline__ float small_int_to_float(int a) {
 
 // Combine the three exact digit sums of one group: ((a1 + a2 * 2^-7) + a3 * 2^-14).
 // |a_i| <= 64 * 127 * 64 < 2^22, so each conversion is exact.
+// a2 * 2^-7 and a3 * 2^-14 are exact, so each fused multiply-add rounds exactly once, like the
+// separate add it replaces.
 __device__ __forceinline__ float digit_value(int a1, int a2, int a3) {
-    float v = __fadd_rn(small_int_to_float(a1), __fmul_rn(small_int_to_float(a2), 0.0078125f));
-    return __fadd_rn(v, __fmul_rn(small_int_to_float(a3), 6.103515625e-05f));
+    float v = __fmaf_rn(small_int_to_float(a2), 0.0078125f, small_int_to_float(a1));
+    return __fmaf_rn(small_int_to_float(a3), 6.103515625e-05f, v);
 }
 
 // One step of the sequential group accumulation of a row: acc + v * (w_scale * 2^e).

@@ -11,8 +11,9 @@
 // the same digit_value/group_accumulate sequence as the CUDA-core kernel, so both paths give the
 // same bits.  No TMA multicast (this code runs on every GPU of a multi-GPU job).
 //
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer,
-// warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4) .. +31).
+// Warp roles: warp 0 = copy producer, warp 1 = TMEM owner + MMA issuer, then one or two
+// epilogue warpgroups (warp w reads TMEM lanes 32*(w%4) .. +31; with two warpgroups each owns
+// half of the tile's streams).
 // Every wait is bounded: on timeout the CTA records an error word, stops issuing work, drains
 // the copies it started and frees its TMEM before returning.
 #pragma once
@@ -25,7 +26,7 @@ constexpr int kBM = 128;      // rows per tile = TMEM lanes
 constexpr int kBK = 64;       // bytes of K per stage = one quantisation group
 template <int BN>
 constexpr int stages_for() { return BN == 16 ? 12 : 8; }  // deep enough to cover a ~2 us TMA round trip
-constexpr int kThreads = 192;
+
 constexpr int kAutoMinStreams = 4;   // below this the CUDA-core kernel is used
 // Wait bound in SM clock cycles (about 2 s at the B200's 1.9 GHz boost clock, longer when the
 // clock is lower): far beyond any legitimate wait.  clock64 is a cheap per-SM counter.
@@ -36,6 +37,9 @@ struct TileCfg {
     static constexpr int kBufs = BN == 16 ? 4 : 2;          // TMEM accumulator sets in flight
     static constexpr int kColsUsed = kBufs * 3 * BN;
     static constexpr uint32_t kCols = kColsUsed <= 128 ? 128u : (kColsUsed <= 256 ? 256u : 512u);
+    static constexpr int kEG = BN >= 32 ? 2 : 1;              // epilogue warpgroups
+    static constexpr int kSPT = BN / kEG;                    // streams per epilogue thread
+    static constexpr int kThreads = 64 + 128 * kEG;          // producer + MMA warp + epilogue
 };
 
 template <int BN>
@@ -181,12 +185,15 @@ constexpr size_t launch_smem() {
 
 // One (128-row, BN-stream) output tile over all K groups of one Q8 projection.
 template <int BN, class Epi>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(TileCfg<BN>::kThreads, 1)
 k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M, int K, int cap_pad, int n,
              const float* __restrict__ w_scale, const float* __restrict__ act_e, uint32_t* err, Epi epi) {
     extern __shared__ uint8_t smem_raw[];
     Smem<BN>& S = *reinterpret_cast<Smem<BN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr int kBufs = TileCfg<BN>::kBufs;
+    constexpr int kEG = TileCfg<BN>::kEG;
+    constexpr int kSPT = TileCfg<BN>::kSPT;
+    constexpr int kThreads = TileCfg<BN>::kThreads;
     constexpr int kStages = Smem<BN>::kStages;
     constexpr uint32_t kCols = TileCfg<BN>::kCols;
     constexpr uint32_t kStageBytes = kBM * kBK + 3 * BN * kBK;
@@ -205,7 +212,7 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
         }
         for (int i = 0; i < kBufs; i++) {
             mbar_init(&S.tfull[i], 1);
-            mbar_init(&S.tempty[i], 128);
+            mbar_init(&S.tempty[i], 128 * kEG);
         }
         S.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -316,17 +323,21 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
         }
         __syncwarp();
     } else {
-        // epilogue: thread owns one output row (TMEM lane) and BN running sums
+        // epilogue: thread owns one output row (TMEM lane) and kSPT running sums
+        const int e = warp - 2;
         const int quad = warp & 3;
+        const int half = e >> 2;                  // which kSPT streams of the tile
+        const int u0 = half * (kSPT / 16);        // first 16-stream block
         const int rl = quad * 32 + lane;
         const int row = m0 + rl;
         const bool row_ok = row < M;
         const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-        float acc[BN];
+        float acc[kSPT];
 #pragma unroll
-        for (int b = 0; b < BN; b++) acc[b] = 0.0f;
-        if constexpr (BN > 32) {
-            // wide tiles: one group at a time (the double buffer would not fit in registers)
+        for (int b = 0; b < kSPT; b++) acc[b] = 0.0f;
+        // TMEM column of (stream block u, digit plane p, stream j of the block) = 48u + 16p + j
+        if constexpr (kSPT > 16) {
+            // one group at a time (a double buffer would not fit in registers)
             for (int g = 0; g < G; g++) {
                 const int buf = g % kBufs;
                 bool ok = __all_sync(0xffffffffu, mbar_wait(&S.tfull[buf], (g / kBufs) & 1, abort));
@@ -335,33 +346,32 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
                 const float wsg = S.ws[g * kBM + rl];
                 const uint32_t base = tmem + lane_off + (uint32_t)(buf * 3 * BN);
 #pragma unroll
-                for (int c = 0; c < BN / 16; c++) {
+                for (int c = 0; c < kSPT / 16; c++) {
                     int a1[16], a2[16], a3[16];
-                    tmem_ld16(base + (uint32_t)(c * 48), a1);
-                    tmem_ld16(base + (uint32_t)(c * 48 + 16), a2);
-                    tmem_ld16(base + (uint32_t)(c * 48 + 32), a3);
+                    tmem_ld16(base + (uint32_t)((u0 + c) * 48), a1);
+                    tmem_ld16(base + (uint32_t)((u0 + c) * 48 + 16), a2);
+                    tmem_ld16(base + (uint32_t)((u0 + c) * 48 + 32), a3);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        int b = c * 16 + j;
-                        acc[b] = group_accumulate(acc[b], digit_value(a1[j], a2[j], a3[j]), wsg, S.ae[b * 32 + g]);
+                    for (int q = 0; q < 16; q++) {
+                        const int b = c * 16 + q;
+                        acc[b] = group_accumulate(acc[b], digit_value(a1[q], a2[q], a3[q]), wsg,
+                                                  S.ae[(half * kSPT + b) * 32 + g]);
                     }
                 }
                 tc_fence_before();
                 mbar_arrive(&S.tempty[buf]);
             }
         } else {
-        // software pipeline: the accumulators of group g+1 are loaded from TMEM while group g is
-            // combined (tcgen05.ld is asynchronous until tcgen05.wait::ld)
-            int cur[3][BN], nxt[3][BN];
+            // software pipeline: group g+1 is read from TMEM while group g is combined
+            // (tcgen05.ld is asynchronous until tcgen05.wait::ld)
+            int cur[3][16], nxt[3][16];
+            const uint32_t ucol = (uint32_t)(u0 * 48);
             bool have = __all_sync(0xffffffffu, mbar_wait(&S.tfull[0], 0, abort));
             if (have) {
                 tc_fence_after();
 #pragma unroll
-                for (int c = 0; c < BN / 16; c++)
-#pragma unroll
-                    for (int p = 0; p < 3; p++)
-                        tmem_ld16(tmem + lane_off + (uint32_t)(c * 48 + p * 16), *reinterpret_cast<int(*)[16]>(&cur[p][c * 16]));
+                for (int p = 0; p < 3; p++) tmem_ld16(tmem + lane_off + ucol + (uint32_t)(p * 16), cur[p]);
                 tmem_wait_ld();
             }
             for (int g = 0; have && g < G; g++) {
@@ -372,18 +382,16 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
                     more = __all_sync(0xffffffffu, mbar_wait(&S.tfull[nb], ((g + 1) / kBufs) & 1, abort));
                     if (more) {
                         tc_fence_after();
-                        const uint32_t base = tmem + lane_off + (uint32_t)(nb * 3 * BN);
+                        const uint32_t base = tmem + lane_off + (uint32_t)(nb * 3 * BN) + ucol;
 #pragma unroll
-                        for (int c = 0; c < BN / 16; c++)
-#pragma unroll
-                            for (int p = 0; p < 3; p++)
-                                tmem_ld16(base + (uint32_t)(c * 48 + p * 16), *reinterpret_cast<int(*)[16]>(&nxt[p][c * 16]));
+                        for (int p = 0; p < 3; p++) tmem_ld16(base + (uint32_t)(p * 16), nxt[p]);
                     }
                 }
                 const float wsg = S.ws[g * kBM + rl];
 #pragma unroll
-                for (int b = 0; b < BN; b++)
-                    acc[b] = group_accumulate(acc[b], digit_value(cur[0][b], cur[1][b], cur[2][b]), wsg, S.ae[b * 32 + g]);
+                for (int b = 0; b < 16; b++)
+                    acc[b] = group_accumulate(acc[b], digit_value(cur[0][b], cur[1][b], cur[2][b]), wsg,
+                                              S.ae[(half * kSPT + b) * 32 + g]);
                 tc_fence_before();
                 mbar_arrive(&S.tempty[buf]);
                 if (g + 1 < G) {
@@ -395,18 +403,19 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
 #pragma unroll
                     for (int p = 0; p < 3; p++)
 #pragma unroll
-                        for (int b = 0; b < BN; b++) cur[p][b] = nxt[p][b];
+                        for (int b = 0; b < 16; b++) cur[p][b] = nxt[p][b];
                 }
             }
         }
         if (!*abort && row_ok) {
 #pragma unroll
-            for (int c = 0; c < BN / 8; c++) {
-                float v[8];
+            for (int c = 0; c < kSPT / 16; c++) {
+                float v[16];
 #pragma unroll
-                for (int i = 0; i < 8; i++) v[i] = acc[c * 8 + i];
-                int b0 = n0 + c * 8;
-                if (b0 < n) epi.template apply<8>(row, b0, min(8, n - b0), v, TileMeta{S.slot, S.fresh}, c * 8);
+                for (int i = 0; i < 16; i++) v[i] = acc[c * 16 + i];
+                const int tb = half * kSPT + c * 16;  // tile-relative first stream
+                const int b0 = n0 + tb;
+                if (b0 < n) epi.template apply<16>(row, b0, min(16, n - b0), v, TileMeta{S.slot, S.fresh}, tb);
             }
         }
     }
