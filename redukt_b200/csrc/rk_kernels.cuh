@@ -255,7 +255,7 @@ struct TileMeta {
 struct EpiStore {  // out[b][row] = v
     float* out;
     int ld;
-    __device__ __forceinline__ void stage(int, int, uint32_t*, uint32_t*) const {}
+    __device__ __forceinline__ void stage(int, int, uint32_t*, uint32_t*, int, int) const {}
     template <int CH>
     __device__ __forceinline__ void apply(int row, int b0, int nb, const float (&v)[CH], TileMeta, int) const {
         apply<CH>(row, b0, nb, v);
@@ -272,7 +272,7 @@ struct EpiStore {  // out[b][row] = v
 struct EpiResidual {  // x[b][row] += v (src/infrastructure/mamba/model.rs:716-719)
     float* x;
     int ld;
-    __device__ __forceinline__ void stage(int, int, uint32_t*, uint32_t*) const {}
+    __device__ __forceinline__ void stage(int, int, uint32_t*, uint32_t*, int, int) const {}
     template <int CH>
     __device__ __forceinline__ void apply(int row, int b0, int nb, const float (&v)[CH], TileMeta, int) const {
         apply<CH>(row, b0, nb, v);
@@ -336,8 +336,10 @@ struct EpiInProj {
     }
 
     // stage the slots and reset flags of streams b0..b0+nb-1 into tile-local arrays
-    __device__ __forceinline__ void stage(int b0, int nb, uint32_t* slot_s, uint32_t* fresh_s) const {
-        for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+    // (thread `tid` of `nthreads` cooperating threads)
+    __device__ __forceinline__ void stage(int b0, int nb, uint32_t* slot_s, uint32_t* fresh_s, int tid,
+                                          int nthreads) const {
+        for (int i = tid; i < nb; i += nthreads) {
             uint32_t sl = slots[b0 + i];
             uint32_t rf = rflag[b0 + i];
             slot_s[i] = sl;

@@ -228,48 +228,8 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
                      "r"(kCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    {
-        // weight scales of the tile: every load issued before any store (no dependent chain)
-        constexpr int kMaxPer = (kBM * 32 + kThreads - 1) / kThreads;
-        float tmp[kMaxPer];
-        const int cnt = kBM * G;
-        const int rows_ok = (M - m0) * G;
-#pragma unroll
-        for (int k = 0; k < kMaxPer; k++) {
-            int i = threadIdx.x + k * kThreads;
-            tmp[k] = (i < cnt && i < rows_ok) ? __ldg(w_scale + (size_t)m0 * G + i) : 0.0f;
-        }
-#pragma unroll
-        for (int k = 0; k < kMaxPer; k++) {
-            int i = threadIdx.x + k * kThreads;
-            if (i < cnt) {
-                int r = i / G, g = i - r * G;
-                S.ws[g * kBM + r] = tmp[k];
-            }
-        }
-    }
-    pdl_wait();
-    pdl_trigger();
-    {
-        constexpr int kMaxPer = (BN * 32 + kThreads - 1) / kThreads;
-        float tmp[kMaxPer];
-        const int cnt = BN * G;
-#pragma unroll
-        for (int k = 0; k < kMaxPer; k++) {
-            int i = threadIdx.x + k * kThreads;
-            int b = i / G;
-            tmp[k] = (i < cnt && n0 + b < n) ? act_e[(size_t)n0 * G + i] : 0.0f;
-        }
-#pragma unroll
-        for (int k = 0; k < kMaxPer; k++) {
-            int i = threadIdx.x + k * kThreads;
-            if (i < cnt) {
-                int b = i / G, g = i - b * G;
-                S.ae[b * 32 + g] = tmp[k];
-            }
-        }
-    }
-    epi.stage(n0, min(BN, n - n0), S.slot, S.fresh);
+    // Only barrier initialisation and the TMEM allocation gate the producer and MMA warps; the
+    // epilogue warps stage their scales and stream metadata below while the first stages land.
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -278,6 +238,8 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
 
     if (warp == 0) {
         if (lane == 0) {
+            pdl_wait();  // the activation digits come from the preceding kernel
+            pdl_trigger();
             int issued = 0;
             for (int g = 0; g < G; g++) {
                 int s = g % kStages;
@@ -332,6 +294,48 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
         const int row = m0 + rl;
         const bool row_ok = row < M;
         const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+        {
+            // stage the tile's weight scales (never written by the step: before the dependency
+            // wait), then the activation scales and stream metadata, each as one batch of loads
+            const int et = threadIdx.x - 64;  // 0 .. 128 * kEG - 1
+            constexpr int kET = 128 * kEG;
+            constexpr int kWsPer = (kBM * 32 + kET - 1) / kET;
+            float tw[kWsPer];
+            const int wcnt = kBM * G, wok = (M - m0) * G;
+#pragma unroll
+            for (int k = 0; k < kWsPer; k++) {
+                int i = et + k * kET;
+                tw[k] = (i < wcnt && i < wok) ? __ldg(w_scale + (size_t)m0 * G + i) : 0.0f;
+            }
+            pdl_wait();
+            pdl_trigger();
+            constexpr int kAePer = (BN * 32 + kET - 1) / kET;
+            float ta[kAePer];
+            const int acnt = BN * G;
+#pragma unroll
+            for (int k = 0; k < kAePer; k++) {
+                int i = et + k * kET;
+                ta[k] = (i < acnt && n0 + i / G < n) ? act_e[(size_t)n0 * G + i] : 0.0f;
+            }
+            epi.stage(n0, min(BN, n - n0), S.slot, S.fresh, et, kET);
+#pragma unroll
+            for (int k = 0; k < kWsPer; k++) {
+                int i = et + k * kET;
+                if (i < wcnt) {
+                    int r = i / G, g = i - r * G;
+                    S.ws[g * kBM + r] = tw[k];
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kAePer; k++) {
+                int i = et + k * kET;
+                if (i < acnt) {
+                    int b = i / G, g = i - b * G;
+                    S.ae[b * 32 + g] = ta[k];
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(kET) : "memory");  // epilogue warps only
+        }
         float acc[kSPT];
 #pragma unroll
         for (int b = 0; b < kSPT; b++) acc[b] = 0.0f;
