@@ -33,6 +33,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 from redukt_b200 import rbin  # noqa: E402
+from redukt_b200.shard import max_over_ranks as shard_max  # noqa: E402
 from redukt_b200.workload import ZIPF_SEED_BASE, zipf_tokens  # noqa: E402
 
 WINDOW = 2700          # tokens per stream window (configs[0-1])
@@ -193,11 +194,7 @@ def run_b200(args, rank, world, local, dist):
             dist.barrier()
 
     def max_over_ranks(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return shard_max(x, dist, dev)
 
     from redukt_b200.plugin import PluginBackend
     f32_path, q8_path = model_paths(rank, world, barrier)
@@ -399,6 +396,20 @@ def run_reference(args, rank, world):
             "e2e": {"value": round(v, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_profile_case(n: int, quant: str = "q8") -> None:
+    """Small case for ncu captures: two eager (graph-free) steps of n streams through the C ABI."""
+    from redukt_b200.plugin import PluginBackend
+    f32_path, q8_path = model_paths(0, 1, lambda: None)
+    b = PluginBackend(q8_path if quant == "q8" else f32_path)
+    b.set_option("graphs", 0)
+    b.batch_init(n)
+    toks = zipf_tokens(n, 2, vocab=b.vocab_size)
+    for t in range(2):
+        b.forward_batch(list(range(n)), toks[:, t])
+    b.close()
+    print(json.dumps({"profile_case": n, "quant": quant, "steps": 2}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -409,7 +420,13 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--profile-case", type=int, default=0,
+                    help="run two eager steps of N streams and exit (small case for ncu captures)")
+    ap.add_argument("--profile-quant", default="q8", choices=["q8", "f32"])
     args = ap.parse_args()
+    if args.profile_case:
+        run_profile_case(args.profile_case, args.profile_quant)
+        return
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -9,7 +9,8 @@
 // TMEM accumulators (double-buffered: group g+1 multiplies while the epilogue reads group g).
 // The epilogue warps read the accumulators with tcgen05.ld (thread = row = TMEM lane) and run
 // the same digit_value/group_accumulate sequence as the CUDA-core kernel, so both paths give the
-// same bits.  No TMA multicast (this code runs on every GPU of a multi-GPU job).
+// same bits.  Every operand copy is a plain bulk copy into this CTA's own shared memory, so the
+// kernel runs unchanged on every GPU of a multi-GPU job.
 //
 // Warp roles: warp 0 = copy producer, warp 1 = TMEM owner + MMA issuer, then one or two
 // epilogue warpgroups (warp w reads TMEM lanes 32*(w%4) .. +31; with two warpgroups each owns
