@@ -48,7 +48,12 @@ typedef struct {
 
 /* Loads `weights_path` (a *.rbin file, or a directory holding model.rbin: mamba_cuda.cu:664-671)
  * onto device `device_id` and allocates the private single-stream state.  WEIGHTS_NOT_FOUND for
- * a missing/invalid file, INIT_FAILED for a CUDA failure.  Replaces mamba_cuda.cu:675-708. */
+ * a missing/invalid file, INIT_FAILED for a CUDA failure.  Replaces mamba_cuda.cu:675-708.
+ * Two model kinds: a Mamba .rbin (version 1/2, the reference plugin's format) or an RWKV-7 .rbin
+ * (version 3 with flag bit 4, this engine's model-kind extension; W8A8 like the reference's
+ * default RWKV-7 quantisation, src/infrastructure/rwkv7/model.rs:245).  Every entry point below
+ * serves both kinds unless its comment says otherwise; BackendInfo.name says which is loaded
+ * ("b200-mamba-*" or "b200-rwkv7-w8a8"). */
 BackendResult redukt_backend_init(const uint8_t* weights_path, int32_t device_id, BackendInfo* info_out);
 
 /* One step of the v1 stream; writes vocab_size logits.  Replaces mamba_cuda.cu:710-715. */
@@ -112,12 +117,21 @@ int32_t redukt_b200_device_error(uint32_t* out_word);
 int32_t redukt_b200_get_state(uint32_t slot, float* conv, float* ssm);
 
 /* Copies one quantised matrix as the engine holds it: which = 0 embedding, 1 head, 2 in_proj,
- * 3 out_proj (layer).  q [rows][cols] int8, scales [rows][cols/64] f32 (per-row scales repeated). */
+ * 3 out_proj (layer).  q [rows][cols] int8, scales [rows][cols/64] f32 (per-row scales repeated).
+ * RWKV-7: which = 0 receptance, 1 key, 2 value, 3 output, 4 FFN key, 5 FFN value (layer), 6 head;
+ * scales [rows] (Q8Tensor::from_f32, src/domain/tensor.rs:113-135). */
 int32_t redukt_b200_get_q8(int32_t which, uint32_t layer, int8_t* q, float* scales);
+
+/* RWKV-7 only: one slot's recurrent state in the reference layout (Rwkv7State,
+ * src/infrastructure/rwkv7/model.rs:113-120): x_att [n_layer][d], wkv [n_layer][n_head][64][64],
+ * x_ffn [n_layer][d], v_first [d].  Any pointer may be NULL.  slot = UINT32_MAX reads the v1 state.
+ * INVALID_ARGUMENT when a Mamba model is loaded (use redukt_b200_get_state). */
+int32_t redukt_b200_rwkv_get_state(uint32_t slot, float* x_att, float* wkv, float* x_ffn, float* v_first);
 
 /* Model and engine facts: out[0..12] = vocab, d_model, d_inner, d_state, d_conv, dt_rank, n_layer,
  * flags, profile (0 F32, 1 Q8-g64, 2 Q8 per-row), pool capacity, reset_every, projection path,
- * kernel launches of the last enqueued step. */
+ * kernel launches of the last enqueued step.  RWKV-7: words 2..5 are d_ffn, n_head, head size (64)
+ * and the sum of the four LoRA ranks, and profile is 3 (W8A8). */
 int32_t redukt_b200_info(uint32_t* out, uint32_t n);
 
 /* Engine switches for tests and benchmarks:
@@ -129,13 +143,15 @@ int32_t redukt_b200_set_option(const char* key, int64_t value);
 /* Per-kernel-class device time: returns the CUDA-event time (ms) and launch count accumulated per
  * class since the previous call (0 embed, 1 norm, 2 in_proj, 3 x_proj, 4 scan, 5 out_proj, 6 head,
  * 7 softmax), then turns event bracketing on (enable != 0) or off.  While on, steps run without
- * CUDA graphs so each launch can be bracketed.  Synchronises the device. */
+ * CUDA graphs so each launch can be bracketed.  Synchronises the device.  RWKV-7 classes: 1 the
+ * LayerNorm/shift/quantise kernels, 2 the r/k/v projections, 3 the LoRA down-projections, 4 the WKV
+ * head update and its quantisation, 5 the output and FFN projections, 6 head, 7 softmax. */
 int32_t redukt_b200_kernel_times(int32_t enable, double* ms, uint32_t* launches, uint32_t n_classes);
 
 /* Device time of one kernel class in isolation, in ms per launch: the class's launches of one
  * step for n streams (every layer; the embedding and head once) replayed as a CUDA graph after an
  * L2 flush, `reps` times.  cls as in redukt_b200_kernel_times (0-6).  Needs a batch pool of at least
- * n slots and overwrites its scratch and the state of slots 0..n-1. */
+ * n slots and overwrites its scratch and the state of slots 0..n-1.  Mamba only. */
 int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* ms_per_launch);
 
 /* Softmax of n_rows rows of vocab logits, device memory in and out, with no allocation.

@@ -50,6 +50,8 @@
 #include <unistd.h>
 
 #define ORC_API __attribute__((visibility("default")))
+#define ORC_INTERNAL __attribute__((visibility("hidden")))
+#include "oracle_internal.h"
 
 /* ------------------------------------------------------------------------------------
  * Portable transcendentals (tensor.rs:757-915)
@@ -121,9 +123,9 @@ ORC_API float orc_lnf(float x) {
 }
 
 /* tensor.rs:869-879: one lane of fast_exp_ps (a NaN lane is clamped to EXP_LO). */
-static inline float lane_expf(float x) { return orc_expf(isnan(x) ? -87.3365447505531f : x); }
+ORC_INTERNAL float lane_expf(float x) { return orc_expf(isnan(x) ? -87.3365447505531f : x); }
 ORC_API float orc_lane_sigmoidf(float x) { return 1.0f / (1.0f + lane_expf(0.0f - x)); }
-static inline float portable_sigmoidf(float x) { return 1.0f / (1.0f + orc_expf(-x)); }
+ORC_INTERNAL float portable_sigmoidf(float x) { return 1.0f / (1.0f + orc_expf(-x)); }
 static inline float portable_silu(float x) { return x * portable_sigmoidf(x); }
 ORC_API float orc_softplus(float x) { return x > 20.0f ? x : orc_lnf(1.0f + orc_expf(x)); }
 
@@ -151,7 +153,7 @@ static void rms_norm_into(float* x, const float* w, size_t n, float eps) {
 }
 
 /* tensor.rs:1390-1398 (Rust's f32 Sum folds sequentially). */
-static void layer_norm_into(float* out, const float* x, const float* w, const float* b, size_t n, float eps) {
+ORC_INTERNAL void layer_norm_into(float* out, const float* x, const float* w, const float* b, size_t n, float eps) {
     float sum = 0.0f;
     for (size_t i = 0; i < n; i++) sum += x[i];
     float mean = sum / (float)n;
@@ -169,7 +171,6 @@ static void layer_norm_into(float* out, const float* x, const float* w, const fl
  * thread count.
  * ---------------------------------------------------------------------------------- */
 
-typedef void (*par_fn)(void* ctx, long begin, long end);
 
 static struct {
     pthread_mutex_t mu;
@@ -232,7 +233,7 @@ static void pool_start(void) {
 }
 
 /* Runs fn over [0, n) split into one contiguous range per thread; serial when small. */
-static void par_for(long n, long work, par_fn fn, void* ctx) {
+ORC_INTERNAL void par_for(long n, long work, par_fn fn, void* ctx) {
     if (n <= 0) return;
     pool_start();
     if (g_pool.nthreads == 1 || work < 65536 || n < 2) { fn(ctx, 0, n); return; }
@@ -324,7 +325,7 @@ __attribute__((target("avx2"))) static float group_dot_avx2(const int8_t* q, con
 #endif
 
 static int g_use_avx2 = -1; /* -1 = detect */
-static int use_avx2(void) {
+ORC_INTERNAL int use_avx2(void) {
 #if defined(__x86_64__)
     if (g_use_avx2 < 0) {
         const char* e = getenv("REDUKT_NO_SIMD");
@@ -338,7 +339,7 @@ static int use_avx2(void) {
 
 ORC_API void orc_set_simd(int on) { g_use_avx2 = on ? 1 : 0; }
 
-static inline float dot_ref(const float* w, const float* v, size_t n) {
+ORC_INTERNAL float dot_ref(const float* w, const float* v, size_t n) {
 #if defined(__x86_64__)
     if (use_avx2()) return dot_ref_avx2(w, v, n);
 #endif

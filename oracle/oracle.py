@@ -1,4 +1,4 @@
-"""ctypes view of the CPU oracle (mamba_oracle.c) -- TEST INFRASTRUCTURE ONLY.
+"""ctypes view of the CPU oracle (mamba_oracle.c; RWKV-7 in rwkv7.py) -- TEST INFRASTRUCTURE ONLY.
 
 Only tests/, `__graft_entry__.smoke()` and bench.py's CPU-baseline leg import this module, and
 only as the checker or the timed CPU baseline.  The product path (redukt_b200) never does.
@@ -29,8 +29,9 @@ def build(ref: bool = False) -> None:
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
-        src = os.path.join(HERE, "mamba_oracle.c")
-        if not os.path.exists(LIB_PATH) or (os.path.exists(src) and os.path.getmtime(src) > os.path.getmtime(LIB_PATH)):
+        srcs = [os.path.join(HERE, f) for f in ("mamba_oracle.c", "rwkv7_oracle.c", "oracle_internal.h")]
+        if not os.path.exists(LIB_PATH) or any(
+                os.path.exists(s) and os.path.getmtime(s) > os.path.getmtime(LIB_PATH) for s in srcs):
             build(ref=False)
         L = ctypes.CDLL(LIB_PATH)
         f32, u32, i32, vp = ctypes.c_float, ctypes.c_uint32, ctypes.c_int, ctypes.c_void_p

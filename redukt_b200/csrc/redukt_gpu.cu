@@ -20,6 +20,7 @@
 
 #include "../../include/redukt_gpu.h"
 #include "rk_kernels.cuh"
+#include "rk_rwkv7.cuh"
 #include "rk_tc.cuh"
 
 namespace {
@@ -124,6 +125,7 @@ struct Model {
     int proj_path = 0;     // 0 auto, 1 CUDA cores, 2 tensor cores
     bool use_graphs = true;
     bool use_pdl = true;   // programmatic dependent launch between the step's kernels
+    bool rwkv = false;     // an RWKV-7 model is loaded (rwkv7_engine.cuh) instead of Mamba
     bool ready = false;
 };
 
@@ -199,10 +201,16 @@ bool pool_alloc(Pool* p, uint32_t cap) {
 }
 
 void clear_dev_graphs();
+namespace rwe {
+void clear_graphs();
+void release();
+}  // namespace rwe
 
 void free_model() {
     if (G.stream) cudaStreamSynchronize(G.stream);
     clear_dev_graphs();
+    rwe::clear_graphs();
+    rwe::release();
     pool_free(&G.v1);
     pool_free(&G.batch);
     for (void* a : G.allocs) cudaFree(a);
@@ -813,6 +821,8 @@ std::string rbin_path(const uint8_t* weights_path) {
     return p;
 }
 
+#include "rwkv7_engine.cuh"
+
 // ------------------------------------------------------------------------------------------
 // Probability pass without allocation (redukt_b200_softmax_noalloc).
 //
@@ -857,12 +867,14 @@ BackendResult redukt_backend_init(const uint8_t* weights_path, int32_t device_id
         free_model();
         return BACKEND_INIT_FAILED;
     }
-    int rc = load_weights(path.c_str());
+    const int kind = rwe::peek_kind(path.c_str());
+    G.rwkv = kind == 1;
+    int rc = G.rwkv ? rwe::load_weights(path.c_str()) : load_weights(path.c_str());
     if (rc != BACKEND_OK) {
         free_model();
         return (BackendResult)rc;
     }
-    if (!dalloc(&G.d_err, 1) || !pool_alloc(&G.v1, 1)) {
+    if (!dalloc(&G.d_err, 1) || !(G.rwkv ? rwe::pool_alloc(&rwe::M.v1, 1) : pool_alloc(&G.v1, 1))) {
         set_err("device allocation failed");
         free_model();
         return BACKEND_INIT_FAILED;
@@ -875,7 +887,8 @@ BackendResult redukt_backend_init(const uint8_t* weights_path, int32_t device_id
     info_out->ffi_version = BACKEND_FFI_VERSION;
     info_out->vocab_size = (uint32_t)G.V;
     info_out->hidden_dim = (uint32_t)G.d;
-    const char* name = G.profile == kF32 ? "b200-mamba-f32" : (G.profile == kQ8 ? "b200-mamba-q8" : "b200-mamba-q8row");
+    const char* name = G.rwkv ? "b200-rwkv7-w8a8"
+                              : (G.profile == kF32 ? "b200-mamba-f32" : (G.profile == kQ8 ? "b200-mamba-q8" : "b200-mamba-q8row"));
     memcpy(info_out->name, name, strlen(name));
     return BACKEND_OK;
 }
@@ -883,14 +896,16 @@ BackendResult redukt_backend_init(const uint8_t* weights_path, int32_t device_id
 BackendResult redukt_backend_forward(uint32_t token, float* out_logits, uint32_t vocab_size) {
     if (!G.ready || !out_logits || vocab_size != (uint32_t)G.V) return BACKEND_FORWARD_FAILED;
     uint32_t slot = 0;
-    int rc = pool_forward(G.v1, 1, &slot, &token, out_logits, false);
+    int rc = G.rwkv ? rwe::pool_forward(rwe::M.v1, 1, &slot, &token, out_logits, false)
+                    : pool_forward(G.v1, 1, &slot, &token, out_logits, false);
     return rc == BACKEND_OK ? BACKEND_OK : BACKEND_FORWARD_FAILED;
 }
 
 void redukt_backend_reset_state(void) {
     if (!G.ready) return;
     uint32_t slot = 0;
-    if (pool_reset(G.v1, &slot, 1) != BACKEND_OK) fprintf(stderr, "[redukt-b200] reset_state failed\n");
+    int rc = G.rwkv ? rwe::pool_reset(rwe::M.v1, &slot, 1) : pool_reset(G.v1, &slot, 1);
+    if (rc != BACKEND_OK) fprintf(stderr, "[redukt-b200] reset_state failed\n");
 }
 
 void redukt_backend_free(void) { free_model(); }
@@ -902,28 +917,33 @@ int32_t redukt_backend_batch_init(uint32_t max_streams) {
     if (max_streams > kMaxStreams) return BACKEND_INVALID_ARGUMENT;
     CK(cudaStreamSynchronize(G.stream), BACKEND_INIT_FAILED);
     clear_dev_graphs();
+    rwe::clear_graphs();
     pool_free(&G.batch);
+    rwe::pool_free(&rwe::M.batch);
     if (max_streams == 0) return BACKEND_OK;
-    if (!pool_alloc(&G.batch, max_streams)) {
+    if (!(G.rwkv ? rwe::pool_alloc(&rwe::M.batch, max_streams) : pool_alloc(&G.batch, max_streams))) {
         set_err("batch pool of %u streams: device allocation failed", max_streams);
         return BACKEND_INIT_FAILED;
     }
     return BACKEND_OK;
 }
 
+static uint32_t batch_cap() { return G.rwkv ? rwe::M.batch.cap : G.batch.cap; }
+
 int32_t redukt_backend_batch_reset(const uint32_t* slots, uint32_t n_slots) {
-    if (!G.ready || G.batch.cap == 0) return BACKEND_INIT_FAILED;
-    if (slots && n_slots > G.batch.cap) return BACKEND_INVALID_ARGUMENT;
-    return pool_reset(G.batch, slots, n_slots);
+    if (!G.ready || batch_cap() == 0) return BACKEND_INIT_FAILED;
+    if (slots && n_slots > batch_cap()) return BACKEND_INVALID_ARGUMENT;
+    return G.rwkv ? rwe::pool_reset(rwe::M.batch, slots, n_slots) : pool_reset(G.batch, slots, n_slots);
 }
 
 static int32_t forward_batch_impl(uint32_t n, const uint32_t* slots, const uint32_t* tokens, float* out,
                                   uint32_t vocab, bool probs) {
-    if (!G.ready || G.batch.cap == 0) return BACKEND_INIT_FAILED;
-    if (vocab != (uint32_t)G.V || n > G.batch.cap) return BACKEND_INVALID_ARGUMENT;
+    if (!G.ready || batch_cap() == 0) return BACKEND_INIT_FAILED;
+    if (vocab != (uint32_t)G.V || n > batch_cap()) return BACKEND_INVALID_ARGUMENT;
     if (n == 0) return BACKEND_OK;
     if (!slots || !tokens || !out) return BACKEND_INVALID_ARGUMENT;
-    return pool_forward(G.batch, n, slots, tokens, out, probs);
+    return G.rwkv ? rwe::pool_forward(rwe::M.batch, n, slots, tokens, out, probs)
+                  : pool_forward(G.batch, n, slots, tokens, out, probs);
 }
 
 int32_t redukt_backend_forward_batch(uint32_t n_streams, const uint32_t* slots, const uint32_t* tokens,
@@ -945,11 +965,12 @@ int32_t redukt_backend_set_reset_every(uint32_t every) {
 
 int32_t redukt_b200_forward_batch_device(uint32_t n, const uint32_t* d_slots, const uint32_t* d_tokens, float* d_out,
                                          uint32_t vocab, int32_t probs, void* cuda_stream) {
-    if (!G.ready || G.batch.cap == 0) return BACKEND_INIT_FAILED;
-    if (vocab != (uint32_t)G.V || n > G.batch.cap) return BACKEND_INVALID_ARGUMENT;
+    if (!G.ready || batch_cap() == 0) return BACKEND_INIT_FAILED;
+    if (vocab != (uint32_t)G.V || n > batch_cap()) return BACKEND_INVALID_ARGUMENT;
     if (n == 0) return BACKEND_OK;
     if (!d_slots || !d_tokens || !d_out) return BACKEND_INVALID_ARGUMENT;
     cudaStream_t st = cuda_stream ? reinterpret_cast<cudaStream_t>(cuda_stream) : G.stream;
+    if (G.rwkv) return rwe::forward_device(n, d_slots, d_tokens, d_out, probs != 0, st);
     DevKey k{graph_key((int)n, probs != 0), d_slots, d_tokens, d_out};
     if (!G.use_graphs || g_kt.on || !g_dev_eager.count(k)) {
         int rc = enqueue_step(G.batch, (int)n, d_slots, d_tokens, d_out, probs != 0, st);
@@ -1009,6 +1030,7 @@ int32_t redukt_b200_device_error(uint32_t* out_word) {
 
 int32_t redukt_b200_get_state(uint32_t slot, float* conv, float* ssm) {
     if (!G.ready) return BACKEND_INIT_FAILED;
+    if (G.rwkv) return BACKEND_INVALID_ARGUMENT;
     Pool* p = &G.batch;
     if (slot == 0xffffffffu) {
         p = &G.v1;
@@ -1035,8 +1057,15 @@ int32_t redukt_b200_get_state(uint32_t slot, float* conv, float* ssm) {
     return BACKEND_OK;
 }
 
+int32_t redukt_b200_rwkv_get_state(uint32_t slot, float* x_att, float* wkv, float* x_ffn, float* v_first) {
+    if (!G.ready) return BACKEND_INIT_FAILED;
+    if (!G.rwkv) return BACKEND_INVALID_ARGUMENT;
+    return rwe::get_state(slot, x_att, wkv, x_ffn, v_first);
+}
+
 int32_t redukt_b200_get_q8(int32_t which, uint32_t layer, int8_t* q, float* scales) {
     if (!G.ready) return BACKEND_INIT_FAILED;
+    if (G.rwkv) return rwe::get_q8(which, layer, q, scales);
     if (G.profile == kF32) return BACKEND_INVALID_ARGUMENT;
     const Mat* m = nullptr;
     if (which == 0) m = &G.emb;
@@ -1064,7 +1093,11 @@ int32_t redukt_b200_get_q8(int32_t which, uint32_t layer, int8_t* q, float* scal
 // slots 0..n-1; each replay follows an L2 flush (a 256 MiB memset) so weights come from HBM as
 // in a real step.  Overwrites the pool's scratch and the state of slots 0..n-1.
 int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* ms_per_launch) {
-    if (!G.ready || G.batch.cap == 0) return BACKEND_INIT_FAILED;
+    if (!G.ready || batch_cap() == 0) return BACKEND_INIT_FAILED;
+    if (G.rwkv) {
+        set_err("time_kernel: per-class timing is implemented for the Mamba engine only");
+        return BACKEND_INVALID_ARGUMENT;
+    }
     if (n == 0 || n > G.batch.cap || !ms_per_launch || cls < 0 || cls >= (int)kKSoftmax) return BACKEND_INVALID_ARGUMENT;
     Pool& p = G.batch;
     std::vector<uint32_t> idx(n);
@@ -1154,6 +1187,13 @@ int32_t redukt_b200_info(uint32_t* out, uint32_t n) {
     uint32_t v[13] = {(uint32_t)G.V, (uint32_t)G.d, (uint32_t)G.di, G.h.ds, G.h.dc, (uint32_t)G.dr, (uint32_t)G.nl,
                       G.h.flags, (uint32_t)G.profile, G.batch.cap, G.reset_every, (uint32_t)G.proj_path,
                       (uint32_t)g_launches_per_step};
+    if (G.rwkv) {  // RWKV-7: words 2..5 are d_ffn, n_head, head size, sum of LoRA ranks; profile 3 = W8A8
+        const rwe::Model& m = rwe::M;
+        uint32_t w[13] = {(uint32_t)m.V, (uint32_t)m.D, (uint32_t)m.F, (uint32_t)m.H, 64u, (uint32_t)m.R,
+                          (uint32_t)m.L, m.flags, 3u, m.batch.cap, G.reset_every, (uint32_t)G.proj_path,
+                          (uint32_t)g_launches_per_step};
+        for (int i = 0; i < 13; i++) v[i] = w[i];
+    }
     for (uint32_t i = 0; i < n && i < 13; i++) out[i] = v[i];
     return BACKEND_OK;
 }
@@ -1176,6 +1216,7 @@ int32_t redukt_b200_set_option(const char* key, int64_t value) {
             p->graphs.clear();
         }
         clear_dev_graphs();
+        rwe::clear_graphs();
         return BACKEND_OK;
     }
     return BACKEND_INVALID_ARGUMENT;

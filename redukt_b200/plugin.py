@@ -33,7 +33,8 @@ V2_SYMBOLS = ("redukt_backend_abi_version", "redukt_backend_batch_init", "redukt
 EXT_SYMBOLS = ("redukt_backend_set_reset_every", "redukt_backend_forward_batch_probs",
                "redukt_b200_forward_batch_device", "redukt_b200_device_error", "redukt_b200_get_state",
                "redukt_b200_get_q8", "redukt_b200_info", "redukt_b200_set_option", "redukt_b200_kernel_times",
-               "redukt_b200_time_kernel", "redukt_b200_softmax_noalloc", "redukt_b200_last_error")
+               "redukt_b200_time_kernel", "redukt_b200_softmax_noalloc", "redukt_b200_rwkv_get_state",
+               "redukt_b200_last_error")
 KERNEL_CLASSES = ("embed", "norm", "in_proj", "x_proj", "scan", "out_proj", "head", "softmax")
 
 
@@ -135,6 +136,8 @@ class PluginLibrary:
             L.redukt_b200_time_kernel.argtypes = [i32, u32, u32, ctypes.POINTER(ctypes.c_float)]
             L.redukt_b200_time_kernel.restype = i32
             L.redukt_b200_softmax_noalloc.argtypes = [vp, u32, u32, vp, vp]
+            L.redukt_b200_rwkv_get_state.argtypes = [u32, f32p, f32p, f32p, f32p]
+            L.redukt_b200_rwkv_get_state.restype = i32
             L.redukt_b200_softmax_noalloc.restype = i32
             L.redukt_b200_last_error.argtypes, L.redukt_b200_last_error.restype = [], ctypes.c_char_p
 
@@ -167,6 +170,7 @@ class PluginBackend:
         self.info = info
         self.vocab_size = info.vocab_size
         self.hidden_dim = info.hidden_dim
+        self.is_rwkv = info.name_str().startswith("b200-rwkv7")
         self.max_streams = 0
         self._closed = False
 
@@ -294,6 +298,31 @@ class PluginBackend:
                 "pool", "reset_every", "proj_path", "launches_per_step")
         return dict(zip(keys, (int(x) for x in w)))
 
+    def rwkv_info(self) -> dict:
+        """Dimensions of a loaded RWKV-7 model (redukt_b200_info words in RWKV-7 order)."""
+        w = np.zeros(13, np.uint32)
+        code = BackendResult.from_code(self.lib.redukt_b200_info(_u32p(w), 13))
+        if code != BackendResult.OK:
+            raise PluginError("redukt_b200_info", code, self.libobj.last_error())
+        keys = ("vocab", "d_model", "d_ffn", "n_head", "head_size", "lora_sum", "n_layer", "flags", "profile",
+                "pool", "reset_every", "proj_path", "launches_per_step")
+        return dict(zip(keys, (int(x) for x in w)))
+
+    def rwkv_state(self, slot: int):
+        """(x_prev_att [L, D], wkv [L, H, N, N], x_prev_ffn [L, D], v_first [D]) of an RWKV-7 slot
+        (slot=-1: the v1 stream), in the reference's layout (`Rwkv7State`)."""
+        i = self.rwkv_info()
+        L, D, H, N = i["n_layer"], i["d_model"], i["n_head"], i["head_size"]
+        xa = np.empty((L, D), np.float32)
+        wkv = np.empty((L, H, N, N), np.float32)
+        xf = np.empty((L, D), np.float32)
+        vf = np.empty(D, np.float32)
+        code = BackendResult.from_code(self.lib.redukt_b200_rwkv_get_state(slot & 0xFFFFFFFF, _f32p(xa), _f32p(wkv),
+                                                                           _f32p(xf), _f32p(vf)))
+        if code != BackendResult.OK:
+            raise PluginError("redukt_b200_rwkv_get_state", code, self.libobj.last_error())
+        return xa, wkv, xf, vf
+
     def get_state(self, slot: int):
         """(conv [L, di, dc-1], ssm [L, di, ds]) of a batch slot (slot=-1: the v1 stream)."""
         i = self.info_words()
@@ -304,7 +333,20 @@ class PluginBackend:
             raise PluginError("redukt_b200_get_state", code, self.libobj.last_error())
         return conv, ssm
 
+    RWKV_Q8 = ("receptance", "key", "value", "output", "ffn_key", "ffn_value", "head")
+
     def get_q8(self, which: str, layer: int = 0):
+        if self.is_rwkv:
+            i = self.rwkv_info()
+            d, f, v = i["d_model"], i["d_ffn"], i["vocab"]
+            rows, cols = {"ffn_key": (f, d), "ffn_value": (d, f), "head": (v, d)}.get(which, (d, d))
+            q = np.empty((rows, cols), np.int8)
+            s = np.empty(rows, np.float32)
+            code = BackendResult.from_code(self.lib.redukt_b200_get_q8(self.RWKV_Q8.index(which), layer, q.ctypes.data,
+                                                                       _f32p(s)))
+            if code != BackendResult.OK:
+                raise PluginError("redukt_b200_get_q8", code, self.libobj.last_error())
+            return q, s
         i = self.info_words()
         code_w = {"emb": 0, "head": 1, "in_proj": 2, "out_proj": 3}[which]
         rows, cols = {"emb": (i["vocab"], i["d_model"]), "head": (i["vocab"], i["d_model"]),

@@ -52,6 +52,23 @@ def mamba130m_rbin(model_dir):
     return rbin.ensure_model(os.path.join(model_dir, "mamba130m.rbin"), rbin.MAMBA_130M, kind="gaussian")
 
 
+_SHARED_BACKEND = {}
+
+
+def shared_backend(path: str):
+    """The plugin is a process-global singleton: every GPU test module goes through this one cache,
+    so a module never holds a handle to a model another module has replaced."""
+    from redukt_b200.plugin import PluginBackend
+    b = _SHARED_BACKEND.get("b")
+    if b is not None and _SHARED_BACKEND.get("path") == path and not b._closed:
+        return b
+    if b is not None and not b._closed:
+        b.close()
+    b = PluginBackend(path)
+    _SHARED_BACKEND.update(b=b, path=path)
+    return b
+
+
 def q8(path: str, per_row: bool = False) -> str:
     flags = rbin.FLAG_Q8 | (rbin.FLAG_Q8_PER_ROW if per_row else 0)
     suffix = ".q8row.rbin" if per_row else ".q8.rbin"

@@ -9,7 +9,7 @@ Tolerance against the oracle: max |delta log p| <= 1e-3 nats per token (the engi
 import numpy as np
 import pytest
 
-from conftest import max_dlogp, q8
+from conftest import max_dlogp, q8, shared_backend
 from oracle import oracle as O
 from redukt_b200.plugin import BackendResult, PluginBackend
 from redukt_b200.workload import zipf_tokens
@@ -18,19 +18,9 @@ pytestmark = pytest.mark.gpu
 
 TOL_NATS = 1e-3
 
-_BACKEND = {}
-
-
 def backend(path):
     """The plugin is a process-global singleton: re-init only when the model changes."""
-    b = _BACKEND.get("b")
-    if b is not None and _BACKEND.get("path") == path:
-        return b
-    if b is not None:
-        b.close()
-    b = PluginBackend(path)
-    _BACKEND.update(b=b, path=path)
-    return b
+    return shared_backend(path)
 
 
 def oracle_model(path, profile):
