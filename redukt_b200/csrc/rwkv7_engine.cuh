@@ -13,7 +13,8 @@
 //   v_first        [cap][D]
 //   since          [cap]
 // Weights: LayerNorm / mix / bias vectors f32; the four LoRA down-projections concatenated into
-// one [R][D] matrix and the four up-projections into [D][R] (R = sum of the ranks); the W8A8
+// one [R][D] matrix and the four up-projections into a head-major [H][R][64] (R = sum of the
+// ranks); the W8A8
 // matrices as per-row-quantised int8 in the tiled layout of the tensor-core projection.
 
 namespace rwe {
@@ -39,7 +40,7 @@ struct Layer {
     float *w0 = nullptr, *a0 = nullptr, *v0 = nullptr, *k_k = nullptr, *k_a = nullptr, *r_k = nullptr;
     float *lnx_w = nullptr, *lnx_b = nullptr, *ffn_xk = nullptr;
     float* w1cat = nullptr;  // [R][D]
-    float* w2cat = nullptr;  // [D][R]
+    float* w2cat = nullptr;  // [H][R][64] (head-major, k_rw_put_up)
     W8 r, k, v, o, fk, fv;
 };
 
@@ -131,11 +132,12 @@ bool load_w8(Reader& r, W8* m, int rows, int cols) {
     return ok;
 }
 
-// A LoRA up-projection [D][len] into columns [off, off + len) of the layer's [D][R] matrix.
+// A LoRA up-projection [D][len] into columns [off, off + len) of the layer's head-major [H][R][64]
+// up-projection matrix.
 bool load_up(Reader& r, float* w2cat, int len, int off) {
     const size_t count = (size_t)M.D * len;
     if (!r.read_to(g_tmp, count)) return false;
-    k_rw_put_cols<<<(unsigned)((count + 255) / 256), 256>>>(g_tmp, M.D, len, M.R, off, w2cat);
+    k_rw_put_up<<<(unsigned)((count + 255) / 256), 256>>>(g_tmp, M.D, len, M.R, off, w2cat);
     return cudaDeviceSynchronize() == cudaSuccess;
 }
 
@@ -176,7 +178,7 @@ int load_weights(const char* path) {
     for (int i = 0; i < 4; i++) {
         M.seg_off[i] = M.R;
         M.seg_len[i] = ranks[i];
-        M.tiles_before[i + 1] = M.tiles_before[i] + (ranks[i] + 31) / 32;
+        M.tiles_before[i + 1] = M.tiles_before[i] + (ranks[i] + kLoraRows - 1) / kLoraRows;
         M.R += ranks[i];
     }
     // Engine limits: head size 64, d and d_ffn multiples of 64 (int8 K slices), every LoRA rank
@@ -302,10 +304,12 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
     const RwStep sa{n, (int)p.cap, p.cap_pad, M.V, d_slots, d_tokens, p.rflag, p.since, G.reset_every, G.d_err};
     const int D = M.D, F = M.F;
     const size_t cap = p.cap;
-    const size_t ln_smem = 6 * (size_t)D * sizeof(float);
+    const size_t ln_smem = (size_t)D * sizeof(float);
+    const dim3 ln_block(D / 4), q_grid(n);
     const size_t wkv_sm = wkv_smem(M.R);
     allow_smem(k_rw_ln_mix, ln_smem);
     allow_smem(k_rw_wkv, wkv_sm);
+    allow_smem(k_rw_lora1, lora1_smem());
     int launches = 0;
     for (int li = 0; li < M.L; li++) {
         const Layer& Y = M.layers[li];
@@ -316,7 +320,7 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
             KScope k(kKNorm, st);
             LnMixArgs la{D, kLnTime, li == 0 ? M.emb : nullptr, p.x, Y.ln1_w, Y.ln1_b, x_att, Y.mix6,
                          p.aq0, p.aq1, p.aq2, p.as, p.lora_in};
-            launch(k_rw_ln_mix, dim3(n), dim3(256), ln_smem, st, sa, la);
+            launch(k_rw_ln_mix, dim3(n), ln_block, ln_smem, st, sa, la);
         }
         {
             KScope k(kKInProj, st);
@@ -341,7 +345,8 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
             a1.xin = p.lora_in;
             a1.w1cat = Y.w1cat;
             a1.h1 = p.h1;
-            launch(k_rw_lora1, dim3(M.tiles_before[4], (n + 15) / 16), dim3(256), 0, st, sa, a1);
+            launch(k_rw_lora1, dim3(M.tiles_before[4], (n + kLoraStreams - 1) / kLoraStreams), dim3(256), lora1_smem(),
+                   st, sa, a1);
         }
         {
             KScope k(kKScan, st);
@@ -370,7 +375,7 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
             wk.v_first = p.v_first;
             wk.gated = p.gated;
             launch(k_rw_wkv, dim3(M.H, (n + kWkvSB - 1) / kWkvSB), dim3(kHS * kWkvSB), wkv_sm, st, sa, wk);
-            launch(k_rw_quant, dim3(n), dim3(256), 0, st, sa, (const float*)p.gated, D, p.aq0, p.as);
+            launch(k_rw_quant, q_grid, dim3(256), 0, st, sa, (const float*)p.gated, D, p.aq0, p.as);
         }
         {
             KScope k(kKOutProj, st);
@@ -382,14 +387,14 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
             KScope k(kKNorm, st);
             LnMixArgs lc{D, kLnChannel, nullptr, p.x, Y.ln2_w, Y.ln2_b, x_ffn, Y.ffn_xk,
                          p.aq0, nullptr, nullptr, p.as, nullptr};
-            launch(k_rw_ln_mix, dim3(n), dim3(256), ln_smem, st, sa, lc);
+            launch(k_rw_ln_mix, dim3(n), ln_block, ln_smem, st, sa, lc);
         }
         {
             KScope k(kKOutProj, st);
             W8Args wa = w8args(D, n, p);
             wa.job[0] = job(Y.fk, p.aq0, p.as, p.ffn, F, kW8ReluSq);
             project(wa, 1, st);
-            launch(k_rw_quant, dim3(n), dim3(256), 0, st, sa, (const float*)p.ffn, F, p.aq0, p.as);
+            launch(k_rw_quant, q_grid, dim3(256), 0, st, sa, (const float*)p.ffn, F, p.aq0, p.as);
             W8Args wv = w8args(F, n, p);
             wv.job[0] = job(Y.fv, p.aq0, p.as, p.x, D, kW8Add);
             project(wv, 1, st);
@@ -400,7 +405,7 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
         KScope k(kKNorm, st);
         LnMixArgs lf{D, kLnFinal, nullptr, p.x, M.ln_out_w, M.ln_out_b, nullptr, nullptr,
                      p.aq0, nullptr, nullptr, p.as, nullptr};
-        launch(k_rw_ln_mix, dim3(n), dim3(256), ln_smem, st, sa, lf);
+        launch(k_rw_ln_mix, dim3(n), ln_block, ln_smem, st, sa, lf);
     }
     float* lo = probs ? p.logits : d_out;
     {
