@@ -9,8 +9,8 @@ by one token.  Weights are seeded random (no checkpoint is available); tokens ar
   e2e    the same through the plugin C ABI with host buffers: H2D of slots/tokens and D2H of the
          logits inside the timed region
 Extra keys: per-kernel CUDA-event times, the roofline of the dominant kernel, the batch sweep
-(1/128/1024 streams, Q8 and F32) at N=1, and the CPU baseline (the reference CPU path restated in
-C, oracle/, timed on this host's cores).
+(1/128/1024 streams, Q8 and F32) at N=1 plus RWKV-7 0.1B W8A8 at 1/32/256 streams,
+and the CPU baseline (the reference CPU path restated in C, oracle/, timed on this host's cores).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 Multi-GPU: launch under torch.distributed.run; each rank owns its own windows (weak scaling, no
@@ -33,6 +33,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 from redukt_b200 import rbin  # noqa: E402
+from redukt_b200 import rwkv7_rbin  # noqa: E402
 from redukt_b200.shard import max_over_ranks as shard_max  # noqa: E402
 from redukt_b200.workload import ZIPF_SEED_BASE, zipf_tokens  # noqa: E402
 
@@ -41,6 +42,7 @@ STREAMS = 32           # lockstep streams per GPU
 L2_BYTES = 126 * 2**20
 METRIC = "Mamba-130M decode tok/s (Q8, 32 lockstep streams per GPU)"
 SWEEP_N = (1, 128, 1024)
+RWKV_N = (1, 32, 256)  # configs[3] is 256 lockstep streams of uniform byte tokens
 
 
 # ---------------------------------------------------------------------------------------------
@@ -58,6 +60,17 @@ def dims_bytes(dims: rbin.MambaDims, profile: str):
     weights = L * layer + mat(V, d) + d * 4
     emb_row = (d + (d // 64) * 4) if q8 else d * 4
     per_stream = 2 * dims.state_bytes() + V * 4 + emb_row
+    return weights, per_stream
+
+
+def rwkv7_bytes(d: rwkv7_rbin.Rwkv7Dims):
+    """RWKV-7 W8A8 step: (weight bytes read once per step, compulsory bytes per stream)."""
+    D, F, V, R = d.d_model, d.d_ffn, d.vocab, d.lora_w + d.lora_a + d.lora_v + d.lora_g
+    w8 = lambda rows, cols: rows * cols + rows * 4  # int8 + one f32 scale per row
+    layer = 4 * w8(D, D) + w8(F, D) + w8(D, F) + 2 * R * D * 4 + 19 * D * 4
+    weights = d.n_layer * layer + w8(V, D) + 2 * D * 4
+    state = d.state_floats() * 4
+    per_stream = 2 * state + V * 4 + D * 4  # state read + write, logits, embedding row
     return weights, per_stream
 
 
@@ -347,6 +360,52 @@ def sweep(b, f32_path, q8_path, dims, args, dev, peaks):
             out[f"{prof}_n{n}"] = {"tok_s": round(n / ms * 1e3, 1), "ms_per_step": round(ms, 4), "steps": K,
                                    "hbm_frac": round(by / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)}
             del o, toks
+    b.close()
+    out.update(sweep_rwkv7(args, dev, peaks))
+    return out
+
+
+def sweep_rwkv7(args, dev, peaks):
+    """RWKV-7 0.1B (W8A8, the reference's default quantisation) decode tok/s at 256
+    lockstep streams of uniform byte tokens (and at 1 and 32), device-resident inputs."""
+    import torch
+    from redukt_b200.plugin import PluginBackend
+    cache = os.environ.get("REDUKT_B200_MODEL_CACHE", os.path.join(tempfile.gettempdir(), "redukt_b200_models"))
+    path = rwkv7_rbin.ensure_model(os.path.join(cache, "rwkv7_0_1b.rbin"), rwkv7_rbin.RWKV7_0_1B)
+    dims = rwkv7_rbin.RWKV7_0_1B
+    wb, ps = rwkv7_bytes(dims)
+    b = PluginBackend(path, device_id=dev.index)
+    out = {}
+    for n in RWKV_N:
+        b.batch_init(n)
+        toks = torch.from_numpy(rwkv7_rbin.byte_tokens(n, 64).T.copy().astype(np.int32)).to(dev)
+        slots = torch.arange(n, dtype=torch.int32, device=dev)
+        tok = torch.empty(n, dtype=torch.int32, device=dev)
+        o = torch.empty((n, b.vocab_size), dtype=torch.float32, device=dev)
+        sh = torch.cuda.current_stream(dev).cuda_stream
+        assert sh != 0, "the sweep must run on a non-default stream"
+
+        def step(i):
+            tok.copy_(toks[i % 64])
+            b.forward_batch_device(n, slots.data_ptr(), tok.data_ptr(), o.data_ptr(), stream=sh)
+        for i in range(max(3, args.warmup)):
+            step(i)
+        torch.cuda.synchronize()
+        K = max(5, min(args.steps, int(4000 / max(1, n)) + 5))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(torch.cuda.current_stream(dev))
+        for i in range(K):
+            step(i)
+        e1.record(torch.cuda.current_stream(dev))
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / K
+        by = wb + n * ps
+        out[f"rwkv7_w8a8_n{n}"] = {"tok_s": round(n / ms * 1e3, 1), "ms_per_step": round(ms, 4), "steps": K,
+                                   "hbm_frac": round(by / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+                                   "bytes_per_step": by}
+        if b.device_error():
+            raise RuntimeError("RWKV-7 sweep: device error word set")
+        del o, toks
     b.close()
     return out
 
