@@ -96,6 +96,9 @@ struct Pool {
     float* zp = nullptr;         // [cap][xr]
     float* logits = nullptr;     // [cap][V]
     float* red = nullptr;        // [cap][softmax partial slots] (max, sum) pairs
+    float* part = nullptr;       // split-K split sums [tiles][S][128][16] (Q8, up to 64 streams)
+    size_t part_cap = 0;         // floats in `part`
+    uint32_t* counter = nullptr; // split-K tile counters
     uint32_t* rflag = nullptr;   // [cap]
     uint32_t* d_slots = nullptr;
     uint32_t* d_tokens = nullptr;
@@ -159,7 +162,7 @@ void pool_free(Pool* p) {
     p->graphs.clear();
     p->eager_done.clear();
     void* bufs[] = {p->conv, p->ssm, p->since, p->x, p->act_f, p->act_q, p->act_e, p->conv_out, p->z,
-                    p->zp, p->logits, p->red, p->rflag, p->d_slots, p->d_tokens};
+                    p->zp, p->logits, p->red, p->part, p->counter, p->rflag, p->d_slots, p->d_tokens};
     for (void* b : bufs) cudaFree(b);
     if (p->h_slots) cudaFreeHost(p->h_slots);
     if (p->h_tokens) cudaFreeHost(p->h_tokens);
@@ -168,6 +171,15 @@ void pool_free(Pool* p) {
 }
 
 constexpr int kSoftmaxTile = 2048;  // logits per partial (max, sum) of the probability pass
+constexpr int kSplitMaxTiles = 1024;    // split-K tile counters
+constexpr int kSplitMaxN = 64;          // split launches use the 16-stream tile (n <= 64)
+int g_split_target = 148;               // split when a launch has fewer tiles than this
+
+size_t split_part_floats(int rows, int groups, int n) {
+    const size_t tiles = (size_t)((rows + tc::kBM - 1) / tc::kBM) * ((n + 15) / 16);
+    return tiles * q8_splits(groups) * tc::kBM * 16;
+}
+
 
 bool pool_alloc(Pool* p, uint32_t cap) {
     *p = Pool();
@@ -184,6 +196,11 @@ bool pool_alloc(Pool* p, uint32_t cap) {
         else {
             p->cap_pad = round_up((int)cap, 64);
             ok = dalloc(&p->act_q, 3 * (size_t)p->cap_pad * di) && dalloc(&p->act_e, n * (di / kGroup));
+            // split-K scratch for the layer projections (the head's many tiles never split)
+            const int nn = (int)std::min<size_t>(n, kSplitMaxN);
+            p->part_cap = std::max(split_part_floats(2 * (int)di, (int)d / kGroup, nn),
+                                   split_part_floats((int)d, (int)di / kGroup, nn));
+            ok = ok && dalloc(&p->part, p->part_cap, false) && dalloc(&p->counter, kSplitMaxTiles);
         }
     }
     if (ok) ok = cudaHostAlloc(reinterpret_cast<void**>(&p->h_slots), n * sizeof(uint32_t), cudaHostAllocDefault) ==
@@ -498,14 +515,27 @@ bool use_tc(int n) {
     return n >= tc::kAutoMinStreams;
 }
 
+// Split-K of a tensor-core projection: when a small batch leaves fewer (row, stream) tiles than
+// g_split_target, each tile runs its q8_splits(G) accumulation splits in parallel CTAs.  The
+// accumulation order is the same either way (q8_splits), so this is purely a latency choice.
+int split_for(int tiles, int rows, int groups, int n, size_t part_cap) {
+    if (n > kSplitMaxN || tiles >= g_split_target || tiles > kSplitMaxTiles) return 1;
+    const int S = q8_splits(groups);
+    if (S <= 1 || split_part_floats(rows, groups, n) > part_cap) return 1;
+    return S;
+}
+
 template <int BN, class Epi>
 void project_tc_bn(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st) {
     auto k = tc::k_proj_q8_tc<BN, Epi>;
     size_t smem = tc::launch_smem<BN>();
     allow_smem(k, smem);
-    dim3 grid((n + BN - 1) / BN, (m.rows + tc::kBM - 1) / tc::kBM);
+    const int gx = (n + BN - 1) / BN, gy = (m.rows + tc::kBM - 1) / tc::kBM;
+    tc::SplitK sk{1, p.part, p.counter};
+    if (BN == 16 && p.part) sk.splits = split_for(gx * gy, m.rows, m.cols / kGroup, n, p.part_cap);
+    dim3 grid(gx, gy, sk.splits);
     launch(k, grid, dim3(tc::TileCfg<BN>::kThreads), smem, st, (const int8_t*)m.q, (const int8_t*)p.act_q, m.rows, m.cols,
-           p.cap_pad, n, (const float*)m.s, (const float*)p.act_e, G.d_err, epi);
+           p.cap_pad, n, (const float*)m.s, (const float*)p.act_e, G.d_err, epi, sk);
 }
 
 template <class Epi>
@@ -786,6 +816,7 @@ int pool_forward(Pool& p, uint32_t n, const uint32_t* slots, const uint32_t* tok
     if (*p.h_err) {
         set_err("device error word 0x%x (2 = a tensor-core pipeline wait timed out)", *p.h_err);
         cudaMemset(G.d_err, 0, sizeof(uint32_t));
+        if (p.counter) cudaMemset(p.counter, 0, kSplitMaxTiles * sizeof(uint32_t));  // an aborted tile keeps its count
         return BACKEND_FORWARD_FAILED;
     }
     return BACKEND_OK;
@@ -1207,6 +1238,16 @@ int32_t redukt_b200_set_option(const char* key, int64_t value) {
     }
     if (!strcmp(key, "graphs")) {
         G.use_graphs = value != 0;
+        return BACKEND_OK;
+    }
+    if (!strcmp(key, "split_target")) {
+        if (value < 0 || value > 4096) return BACKEND_INVALID_ARGUMENT;
+        g_split_target = (int)value;
+        for (Pool* p : {&G.v1, &G.batch}) {  // captured graphs hold the old grids
+            for (auto& kv : p->graphs) cudaGraphExecDestroy(kv.second);
+            p->graphs.clear();
+        }
+        clear_dev_graphs();
         return BACKEND_OK;
     }
     if (!strcmp(key, "pdl")) {

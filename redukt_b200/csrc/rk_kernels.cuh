@@ -528,20 +528,21 @@ __global__ void __launch_bounds__(256) k_gemv_f32(int M, int K, const float* __r
 // group are exact int32, reduced across the 4 quarter lanes with integer shuffles; the row then
 // accumulates its groups sequentially, g = 0..G-1, with group_accumulate().  The tensor-core
 // kernel produces the same integers and runs the same combine, hence the same bits.
-// Smem: digit planes of the NS-stream tile [NS][3][K] and group scales [NS][G].
+// Smem: digit planes of the NSB-stream tile [NSB][3][K] and group scales [NSB][G].
 // ------------------------------------------------------------------------------------------
-template <int RW, int NS, int GI, class Epi>
+template <int RW, int NSB, int GI, class Epi>
 __global__ void __launch_bounds__(256) k_gemv_q8(int M, int K, const int8_t* __restrict__ Wq,
                                                  const float* __restrict__ Ws, const int8_t* __restrict__ actq,
                                                  const float* __restrict__ acte, int cap_pad, int n, Epi epi) {
     pdl_wait();
     pdl_trigger();
     extern __shared__ float4 smem_f4[];
-    int8_t* dq = reinterpret_cast<int8_t*>(smem_f4);                  // [NS][3][K]
-    float* de = reinterpret_cast<float*>(dq + (size_t)NS * 3 * K);    // [NS][G]
+    int8_t* dq = reinterpret_cast<int8_t*>(smem_f4);                  // [NSB][3][K]
+    float* de = reinterpret_cast<float*>(dq + (size_t)NSB * 3 * K);   // [NSB][G]
     const int G = K / kGroup;
-    int b0 = blockIdx.x * NS;
-    int ns = min(NS, n - b0);
+    const int NS = q8_splits(G);
+    int b0 = blockIdx.x * NSB;
+    int ns = min(NSB, n - b0);
     int K16 = K >> 4;
     for (int i = threadIdx.x; i < ns * 3 * K16; i += blockDim.x) {
         int s = i / (3 * K16), rem = i - s * 3 * K16, p = rem / K16, k16 = rem - p * K16;
@@ -590,17 +591,28 @@ __global__ void __launch_bounds__(256) k_gemv_q8(int M, int K, const int8_t* __r
                 a3 += __shfl_xor_sync(0xffffffffu, a3, 1); a3 += __shfl_xor_sync(0xffffffffu, a3, 2);
                 val[gi] = digit_value(a1, a2, a3);
             }
-            float acc = 0.0f;
+            // the split order of every Q8 projection path (q8_splits): groups accumulated in order
+            // within each split, split sums added in split order
+            float acc = 0.0f, tot = 0.0f;
+            int sp = 0, send = (G * 1) / NS;
 #pragma unroll
             for (int gi = 0; gi < GI; gi++) {
 #pragma unroll
                 for (int t = 0; t < 8; t++) {
                     int g = gi * 8 + t;
                     float v = __shfl_sync(0xffffffffu, val[gi], t * 4);
-                    if (g < G) acc = group_accumulate(acc, v, __ldg(Ws + (size_t)r * G + g), de[s * G + g]);
+                    if (g < G) {
+                        acc = group_accumulate(acc, v, __ldg(Ws + (size_t)r * G + g), de[s * G + g]);
+                        if (g + 1 == send) {
+                            tot = sp == 0 ? acc : __fadd_rn(tot, acc);
+                            acc = 0.0f;
+                            sp++;
+                            send = (G * (sp + 1)) / NS;
+                        }
+                    }
                 }
             }
-            if (lane == (s & 31)) epi(r, b0 + s, acc);
+            if (lane == (s & 31)) epi(r, b0 + s, tot);
         }
     }
 }

@@ -174,6 +174,13 @@ __device__ __forceinline__ float digit_value(int a1, int a2, int a3) {
     return __fmaf_rn(small_int_to_float(a3), 6.103515625e-05f, v);
 }
 
+// Accumulation order of a Q8 projection row (every path): the G groups are cut into
+// S = max(1, G / 3) consecutive splits (split s = groups [G s / S, G (s+1) / S)); each split's
+// groups are accumulated in order from 0 (group_accumulate), and the split sums are added in split
+// order.  S depends only on the matrix shape, so every kernel and batch size gives the same bits,
+// and a tensor-core launch may run the splits in parallel CTAs.
+__host__ __device__ __forceinline__ int q8_splits(int G) { return G >= 6 ? G / 3 : 1; }
+
 // One step of the sequential group accumulation of a row: acc + v * (w_scale * 2^e).
 __device__ __forceinline__ float group_accumulate(float acc, float v, float w_scale, float a_scale) {
     return __fadd_rn(acc, __fmul_rn(v, __fmul_rn(w_scale, a_scale)));

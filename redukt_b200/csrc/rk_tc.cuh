@@ -54,6 +54,8 @@ struct alignas(1024) Smem {
     uint32_t fresh[BN];
     uint64_t tfull[TileCfg<BN>::kBufs];
     uint64_t tempty[TileCfg<BN>::kBufs];
+    uint64_t gather;                      // split-K: the last CTA's copy of the tile's partial sums
+    int last;                             // split-K: this CTA combines the tile
     uint32_t tmem_base;
     int abort;
     float ae[BN * 32];                    // 2^e of the tile's streams for up to 32 groups
@@ -184,11 +186,20 @@ constexpr size_t launch_smem() {
     return want > 232448 ? 232448 : want;
 }
 
-// One (128-row, BN-stream) output tile over all K groups of one Q8 projection.
+// Split-K launch: with splits == S, CTA z of a tile runs only split z and stores its 128 x BN sums to
+// `part`; the tile's last CTA to finish (an atomic counter per tile) copies the tile's S blocks into
+// shared memory and adds them in split order.  With splits == 1 one CTA runs all splits.
+struct SplitK {
+    int splits;          // 1 or q8_splits(G)
+    float* part;         // [tiles][S][128][BN] split sums
+    uint32_t* counter;   // [tiles], zero between launches (the last CTA of a tile resets its entry)
+};
+
+// One (128-row, BN-stream) output tile over all K groups (or one split) of one Q8 projection.
 template <int BN, class Epi>
 __global__ void __launch_bounds__(TileCfg<BN>::kThreads, 1)
 k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M, int K, int cap_pad, int n,
-             const float* __restrict__ w_scale, const float* __restrict__ act_e, uint32_t* err, Epi epi) {
+             const float* __restrict__ w_scale, const float* __restrict__ act_e, uint32_t* err, Epi epi, SplitK sk) {
     extern __shared__ uint8_t smem_raw[];
     Smem<BN>& S = *reinterpret_cast<Smem<BN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr int kBufs = TileCfg<BN>::kBufs;
@@ -198,13 +209,18 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
     constexpr int kStages = Smem<BN>::kStages;
     constexpr uint32_t kCols = TileCfg<BN>::kCols;
     constexpr uint32_t kStageBytes = kBM * kBK + 3 * BN * kBK;
-    const int G = K / kBK;
+    const int G = K / kBK;                          // groups of a row
+    const int NS = q8_splits(G);                     // splits of the accumulation order
+    const bool split = BN == 16 && sk.splits > 1;    // this launch: one CTA per split (narrow tiles only)
+    const int zs = split ? (int)blockIdx.z : 0;
+    const int gb = split ? (G * zs) / NS : 0;        // this CTA's groups [gb, gb + GL)
+    const int GL = split ? (G * (zs + 1)) / NS - gb : G;
     const int n0 = blockIdx.x * BN;
     const int m0 = blockIdx.y * kBM;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int npre = G < kStages ? G : kStages;
+    const int npre = GL < kStages ? GL : kStages;
     const int m_pad = round_up(M, kBM);
-    const int8_t* wtile = wq + (size_t)m0 * 64;  // row m0 of group 0 in the tiled layout
+    const int8_t* wtile = wq + ((size_t)gb * m_pad + m0) * 64;  // row m0 of group gb in the tiled layout
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) {
@@ -215,7 +231,9 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
             mbar_init(&S.tfull[i], 1);
             mbar_init(&S.tempty[i], 128 * kEG);
         }
+        mbar_init(&S.gather, 1);
         S.abort = 0;
+        S.last = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         // weights are never written by the step: stream the first stages before the preceding
         // kernel has finished
@@ -242,7 +260,7 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
             pdl_wait();  // the activation digits come from the preceding kernel
             pdl_trigger();
             int issued = 0;
-            for (int g = 0; g < G; g++) {
+            for (int g = 0; g < GL; g++) {
                 int s = g % kStages;
                 uint32_t ph = (g / kStages) & 1;
                 if (g >= npre) {
@@ -250,7 +268,8 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
                     mbar_expect_tx(&S.full[s], kStageBytes);
                     bulk_load(S.a[s], wtile + (size_t)g * m_pad * 64, kBM * kBK, &S.full[s]);
                 }
-                bulk_load(S.b[s], dq + ((size_t)g * (cap_pad >> 4) + (n0 >> 4)) * 3 * 16 * 64, 3 * BN * kBK, &S.full[s]);
+                bulk_load(S.b[s], dq + ((size_t)(gb + g) * (cap_pad >> 4) + (n0 >> 4)) * 3 * 16 * 64, 3 * BN * kBK,
+                          &S.full[s]);
                 issued = g + 1;
             }
             if (*abort) {  // drain the copies this CTA started before its shared memory goes away
@@ -263,7 +282,7 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
         if (lane == 0) {
             const uint32_t idesc = idesc_i8<3 * BN>();
             int last = -1;
-            for (int g = 0; g < G; g++) {
+            for (int g = 0; g < GL; g++) {
                 int s = g % kStages;
                 uint32_t ph = (g / kStages) & 1;
                 int buf = g % kBufs;
@@ -337,15 +356,29 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
             }
             asm volatile("bar.sync 1, %0;" ::"r"(kET) : "memory");  // epilogue warps only
         }
-        float acc[kSPT];
+        float acc[kSPT], tot[kSPT];  // running sum of the current split; sum of the finished splits
 #pragma unroll
-        for (int b = 0; b < kSPT; b++) acc[b] = 0.0f;
+        for (int b = 0; b < kSPT; b++) acc[b] = tot[b] = 0.0f;
+        // after group g: close the split if g is its last group (whole-row CTA: add it to tot;
+        // split launch: this CTA's only split, kept in acc for the store below)
+        int sp = 0, send = G / NS;  // current split and its end group
+        auto split_end = [&](int g) {
+            if (split || g + 1 != send) return;
+#pragma unroll
+            for (int b = 0; b < kSPT; b++) {
+                tot[b] = sp == 0 ? acc[b] : __fadd_rn(tot[b], acc[b]);
+                acc[b] = 0.0f;
+            }
+            sp++;
+            send = (G * (sp + 1)) / NS;
+        };
         // TMEM column of (stream block u, digit plane p, stream j of the block) = 48u + 16p + j
         if constexpr (kSPT > 16) {
             // one group at a time (a double buffer would not fit in registers)
-            for (int g = 0; g < G; g++) {
-                const int buf = g % kBufs;
-                bool ok = __all_sync(0xffffffffu, mbar_wait(&S.tfull[buf], (g / kBufs) & 1, abort));
+            for (int gl = 0; gl < GL; gl++) {
+                const int g = gb + gl;
+                const int buf = gl % kBufs;
+                bool ok = __all_sync(0xffffffffu, mbar_wait(&S.tfull[buf], (gl / kBufs) & 1, abort));
                 if (!ok) break;
                 tc_fence_after();
                 const float wsg = S.ws[g * kBM + rl];
@@ -366,6 +399,7 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
                 }
                 tc_fence_before();
                 mbar_arrive(&S.tempty[buf]);
+                split_end(g);
             }
         } else {
             // software pipeline: group g+1 is read from TMEM while group g is combined
@@ -379,12 +413,13 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
                 for (int p = 0; p < 3; p++) tmem_ld16(tmem + lane_off + ucol + (uint32_t)(p * 16), cur[p]);
                 tmem_wait_ld();
             }
-            for (int g = 0; have && g < G; g++) {
-                const int buf = g % kBufs;
+            for (int gl = 0; have && gl < GL; gl++) {
+                const int g = gb + gl;
+                const int buf = gl % kBufs;
                 bool more = false;
-                if (g + 1 < G) {
-                    const int nb = (g + 1) % kBufs;
-                    more = __all_sync(0xffffffffu, mbar_wait(&S.tfull[nb], ((g + 1) / kBufs) & 1, abort));
+                if (gl + 1 < GL) {
+                    const int nb = (gl + 1) % kBufs;
+                    more = __all_sync(0xffffffffu, mbar_wait(&S.tfull[nb], ((gl + 1) / kBufs) & 1, abort));
                     if (more) {
                         tc_fence_after();
                         const uint32_t base = tmem + lane_off + (uint32_t)(nb * 3 * BN) + ucol;
@@ -399,7 +434,8 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
                                               S.ae[(half * kSPT + b) * 32 + g]);
                 tc_fence_before();
                 mbar_arrive(&S.tempty[buf]);
-                if (g + 1 < G) {
+                split_end(g);
+                if (gl + 1 < GL) {
                     if (!more) {
                         have = false;
                         break;
@@ -412,7 +448,53 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
                 }
             }
         }
-        if (!*abort && row_ok) {
+        bool emit = true;
+        if constexpr (BN == 16) {
+            static_assert(Smem<BN>::kStages * kBM * kBK >= 12 * kBM * BN * (int)sizeof(float),
+                          "the stage buffers hold the gathered sums of up to 12 splits");
+            if (split) {
+                // publish this split's sums, then the tile's last CTA adds all splits in order
+                constexpr int kET = 128 * kEG;
+                const uint32_t tile = blockIdx.y * gridDim.x + blockIdx.x;
+                float* blk = sk.part + (size_t)tile * NS * (kBM * BN);
+                float4* mine = reinterpret_cast<float4*>(blk + ((size_t)zs * kBM + rl) * BN);
+#pragma unroll
+                for (int q = 0; q < BN / 4; q++) mine[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+                __threadfence();
+                asm volatile("bar.sync 1, %0;" ::"r"(kET) : "memory");
+                if (threadIdx.x == 64 && !*abort) {
+                    const uint32_t old = atomicAdd(&sk.counter[tile], 1u);
+                    if (old == (uint32_t)NS - 1) {
+                        sk.counter[tile] = 0u;  // ready for the next launch
+                        __threadfence();
+                        // other CTAs' generic-proxy writes, read below by the bulk-copy (async) proxy
+                        asm volatile("fence.proxy.async.global;" ::: "memory");
+                        const uint32_t bytes = (uint32_t)(NS * kBM * BN * sizeof(float));
+                        mbar_expect_tx(&S.gather, bytes);
+                        bulk_load(&S.a[0][0], blk, bytes, &S.gather);
+                        S.last = 1;
+                    }
+                }
+                asm volatile("bar.sync 1, %0;" ::"r"(kET) : "memory");
+                emit = S.last != 0;
+                if (emit) {
+                    emit = __all_sync(0xffffffffu, mbar_wait(&S.gather, 0, abort));
+                    const float* P = reinterpret_cast<const float*>(&S.a[0][0]);
+#pragma unroll
+                    for (int b = 0; b < kSPT; b++) acc[b] = P[rl * BN + b];
+                    for (int sp = 1; sp < NS; sp++)
+#pragma unroll
+                        for (int b = 0; b < kSPT; b++) acc[b] = __fadd_rn(acc[b], P[((size_t)sp * kBM + rl) * BN + b]);
+                }
+            } else {
+#pragma unroll
+                for (int b = 0; b < kSPT; b++) acc[b] = tot[b];
+            }
+        } else {
+#pragma unroll
+            for (int b = 0; b < kSPT; b++) acc[b] = tot[b];
+        }
+        if (emit && !*abort && row_ok) {
 #pragma unroll
             for (int c = 0; c < kSPT / 16; c++) {
                 float v[16];
@@ -424,6 +506,7 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
             }
         }
     }
+    if (threadIdx.x == 64 && S.last) mbar_drain(&S.gather, 0);  // a gather copy never outlives the CTA
     tc_fence_before();
     __syncthreads();
     if (*abort && threadIdx.x == 0) atomicOr(err, 2u);
