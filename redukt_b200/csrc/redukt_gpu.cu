@@ -90,7 +90,7 @@ struct Pool {
     float* act_f = nullptr;      // [cap][di] f32 activations (F32 profile)
     int8_t* act_q = nullptr;     // tiled digit planes [di/64][3][cap_pad][64] (Q8)
     int cap_pad = 0;             // cap rounded up to 64
-    float* act_e = nullptr;      // [cap][di/64]
+    float* act_e = nullptr;      // [cap][kEStride]
     float* conv_out = nullptr;   // [cap][di]
     float* z = nullptr;          // [cap][di]
     float* zp = nullptr;         // [cap][xr]
@@ -173,7 +173,7 @@ void pool_free(Pool* p) {
 constexpr int kSoftmaxTile = 2048;  // logits per partial (max, sum) of the probability pass
 constexpr int kSplitMaxTiles = 1024;    // split-K tile counters
 constexpr int kSplitMaxN = 64;          // split launches use the 16-stream tile (n <= 64)
-int g_split_target = 148;               // split when a launch has fewer tiles than this
+int g_split_target = 148;               // CTAs a split launch may use (one wave on 148 SMs)
 
 size_t split_part_floats(int rows, int groups, int n) {
     const size_t tiles = (size_t)((rows + tc::kBM - 1) / tc::kBM) * ((n + 15) / 16);
@@ -195,7 +195,7 @@ bool pool_alloc(Pool* p, uint32_t cap) {
         if (G.profile == kF32) ok = dalloc(&p->act_f, n * di);
         else {
             p->cap_pad = round_up((int)cap, 64);
-            ok = dalloc(&p->act_q, 3 * (size_t)p->cap_pad * di) && dalloc(&p->act_e, n * (di / kGroup));
+            ok = dalloc(&p->act_q, 3 * (size_t)p->cap_pad * di) && dalloc(&p->act_e, n * kEStride);
             // split-K scratch for the layer projections (the head's many tiles never split)
             const int nn = (int)std::min<size_t>(n, kSplitMaxN);
             p->part_cap = std::max(split_part_floats(2 * (int)di, (int)d / kGroup, nn),
@@ -518,10 +518,14 @@ bool use_tc(int n) {
 // Split-K of a tensor-core projection: when a small batch leaves fewer (row, stream) tiles than
 // g_split_target, each tile runs its q8_splits(G) accumulation splits in parallel CTAs.  The
 // accumulation order is the same either way (q8_splits), so this is purely a latency choice.
+// Split only while the split launch still fits one wave: the tile kernel runs one CTA per SM
+// (registers and the TMEM guard), so tiles x S must stay within g_split_target (the SM count).
 int split_for(int tiles, int rows, int groups, int n, size_t part_cap) {
-    if (n > kSplitMaxN || tiles >= g_split_target || tiles > kSplitMaxTiles) return 1;
+    if (n > kSplitMaxN || tiles > kSplitMaxTiles) return 1;
     const int S = q8_splits(groups);
-    if (S <= 1 || split_part_floats(rows, groups, n) > part_cap) return 1;
+    if (S <= 1 || S > tc::kMaxGatherSplits || (long)tiles * S > g_split_target ||
+        split_part_floats(rows, groups, n) > part_cap)
+        return 1;
     return S;
 }
 
@@ -681,6 +685,7 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
         {
             KScope k(kKNorm, st);
             launch_norm(p, n, L.norm_w, L.norm_b, G.d, st);
+            launches++;
         }
         {
             KScope k(kKInProj, st);
@@ -704,18 +709,19 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
             KScope k(kKOutProj, st);
             project(L.out_proj, p, n, EpiResidual{p.x, G.d}, st);
         }
-        launches += 5;
+        launches += 4;
     }
     {
         KScope k(kKNorm, st);
         launch_norm(p, n, G.norm_f_w, G.norm_f_b, G.d, st);
+        launches++;
     }
     float* lo = probs ? p.logits : d_out;
     {
         KScope k(kKHead, st);
         project(G.head, p, n, EpiStore{lo, G.V}, st);
     }
-    launches += 2;
+    launches += 1;
     if (probs) {
         KScope k(kKSoftmax, st);
         int parts = (G.V + kSoftmaxTile - 1) / kSoftmaxTile;

@@ -141,28 +141,24 @@ __global__ void k_embed(StepArgs a, const float* __restrict__ emb_f, const int8_
 struct ActOut {
     float* f;       // [cap][K] f32, or nullptr
     int8_t* q;      // tiled digit planes [K/64][3][cap_pad][64], or nullptr
-    float* e;       // [cap][K/64] group scales 2^e
+    float* e;       // [cap][kEStride] group scales 2^e
     int cap_pad;    // streams per plane, rounded up to 64
     int K;
 };
 
-// Norm of one stream per warp (layer_norm_step, src/infrastructure/mamba/model.rs:193-200).
+// Norm of one stream by one warp (layer_norm_step, src/infrastructure/mamba/model.rs:193-200).
 // Lane l owns columns 128c + 4l .. 128c + 4l + 3; sums are sequential per lane, then a butterfly.
 // RMSNorm: x * (1 / sqrt(sum(x^2)/d + eps)) * w; LayerNorm: (x - mean) * inv_std * w + b.
 template <int NC>  // NC = d / 128 rounded up; d <= 128 * NC
-__global__ void k_norm(int n, const float* __restrict__ x, int d, const float* __restrict__ w,
-                       const float* __restrict__ bias, ActOut out) {
-    pdl_wait();
-    pdl_trigger();
-    int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    int lane = threadIdx.x & 31;
-    if (b >= n) return;
+__device__ __forceinline__ void norm_row_warp(int b, const float* __restrict__ x, int d, const float* __restrict__ w,
+                                              const float* __restrict__ bias, const ActOut& out, int lane) {
     const float* xb = x + (size_t)b * d;
     float4 v[NC];
 #pragma unroll
     for (int c = 0; c < NC; c++) {
         int k = c * 128 + lane * 4;
-        v[c] = k < d ? *reinterpret_cast<const float4*>(xb + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k < d) v[c] = *reinterpret_cast<const float4*>(xb + k);
     }
     float mean = 0.0f, inv;
     if (bias) {
@@ -231,10 +227,21 @@ __global__ void k_norm(int n, const float* __restrict__ x, int d, const float* _
                 *reinterpret_cast<int*>(out.q + dq_off(out.cap_pad, 0, b, k)) = pack4(a0.d1, a1.d1, a2.d1, a3.d1);
                 *reinterpret_cast<int*>(out.q + dq_off(out.cap_pad, 1, b, k)) = pack4(a0.d2, a1.d2, a2.d2, a3.d2);
                 *reinterpret_cast<int*>(out.q + dq_off(out.cap_pad, 2, b, k)) = pack4(a0.d3, a1.d3, a2.d3, a3.d3);
-                if ((lane & 15) == 0) out.e[(size_t)b * (out.K / kGroup) + (k / kGroup)] = gs;
+                if ((lane & 15) == 0) out.e[(size_t)b * kEStride + (k / kGroup)] = gs;
             }
         }
     }
+}
+
+// One stream per warp.
+template <int NC>
+__global__ void k_norm(int n, const float* __restrict__ x, int d, const float* __restrict__ w,
+                       const float* __restrict__ bias, ActOut out) {
+    pdl_wait();
+    pdl_trigger();
+    int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (b >= n) return;
+    norm_row_warp<NC>(b, x, d, w, bias, out, threadIdx.x & 31);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -551,7 +558,7 @@ __global__ void __launch_bounds__(256) k_gemv_q8(int M, int K, const int8_t* __r
     }
     for (int i = threadIdx.x; i < ns * G; i += blockDim.x) {
         int s = i / G, g = i - s * G;
-        de[s * G + g] = acte[(size_t)(b0 + s) * G + g];
+        de[s * G + g] = acte[(size_t)(b0 + s) * kEStride + g];
     }
     __syncthreads();
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -756,7 +763,7 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
     out.q[dq_off(out.cap_pad, 0, b, j)] = (int8_t)dg.d1;
     out.q[dq_off(out.cap_pad, 1, b, j)] = (int8_t)dg.d2;
     out.q[dq_off(out.cap_pad, 2, b, j)] = (int8_t)dg.d3;
-    if ((j & (kGroup - 1)) == 0) out.e[(size_t)b * (out.K / kGroup) + j / kGroup] = gs;
+    if ((j & (kGroup - 1)) == 0) out.e[(size_t)b * kEStride + j / kGroup] = gs;
 }
 
 // Zero the conv and SSM state of the listed slots in every layer, and their reset counters.

@@ -211,6 +211,11 @@ __host__ __device__ __forceinline__ size_t dq_off(int cap_pad, int p, int b, int
 
 __host__ __device__ __forceinline__ int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
+// Per-stream group exponents 2^e of the digit planes: [stream][kEStride], whatever the vector
+// length, so writers of different vectors (the norm: d/64 groups, the scan: d_inner/64) never touch
+// another stream's entries.  Every Q8 projection has at most 32 groups.
+constexpr int kEStride = 32;
+
 // Programmatic dependent launch: wait for the preceding kernel of the stream (and its memory)
 // before touching anything it wrote, then let the next kernel start its own prologue.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

@@ -26,9 +26,9 @@ namespace tc {
 constexpr int kBM = 128;      // rows per tile = TMEM lanes
 constexpr int kBK = 64;       // bytes of K per stage = one quantisation group
 template <int BN>
-constexpr int stages_for() { return BN == 16 ? 12 : 8; }  // deep enough to cover a ~2 us TMA round trip
+constexpr int stages_for() { return BN == 16 ? 12 : 8; }  // deep enough to cover a ~2 us copy round trip
 
-constexpr int kAutoMinStreams = 4;   // below this the CUDA-core kernel is used
+constexpr int kAutoMinStreams = 1;   // the tensor-core kernel serves every batch size (CUDA cores when forced)
 // Wait bound in SM clock cycles (about 2 s at the B200's 1.9 GHz boost clock, longer when the
 // clock is lower): far beyond any legitimate wait.  clock64 is a cheap per-SM counter.
 constexpr long long kWaitLimitCycles = 4000000000ll;
@@ -38,9 +38,10 @@ struct TileCfg {
     static constexpr int kBufs = BN == 16 ? 4 : 2;          // TMEM accumulator sets in flight
     static constexpr int kColsUsed = kBufs * 3 * BN;
     static constexpr uint32_t kCols = kColsUsed <= 128 ? 128u : (kColsUsed <= 256 ? 256u : 512u);
-    static constexpr int kEG = BN >= 32 ? 2 : 1;              // epilogue warpgroups
+    static constexpr int kEG = 2;                            // epilogue warpgroups (each owns BN/2 streams)
     static constexpr int kSPT = BN / kEG;                    // streams per epilogue thread
     static constexpr int kThreads = 64 + 128 * kEG;          // producer + MMA warp + epilogue
+    static constexpr int kMinBlocks = BN == 16 ? 2 : 1;      // CTAs per SM the registers must allow
 };
 
 template <int BN>
@@ -165,6 +166,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&r)[16]) {
         : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, int (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+
+// kSPT (8 or 16) consecutive accumulator columns of this thread's TMEM lane
+template <int N>
+__device__ __forceinline__ void tmem_ld_n(uint32_t taddr, int (&r)[N]) {
+    if constexpr (N == 16) tmem_ld16(taddr, r);
+    else tmem_ld8(taddr, r);
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -186,6 +200,8 @@ constexpr size_t launch_smem() {
     return want > 232448 ? 232448 : want;
 }
 
+constexpr int kMaxGatherSplits = 8;  // split launches gather at most this many split blocks
+
 // Split-K launch: with splits == S, CTA z of a tile runs only split z and stores its 128 x BN sums to
 // `part`; the tile's last CTA to finish (an atomic counter per tile) copies the tile's S blocks into
 // shared memory and adds them in split order.  With splits == 1 one CTA runs all splits.
@@ -197,7 +213,7 @@ struct SplitK {
 
 // One (128-row, BN-stream) output tile over all K groups (or one split) of one Q8 projection.
 template <int BN, class Epi>
-__global__ void __launch_bounds__(TileCfg<BN>::kThreads, 1)
+__global__ void __launch_bounds__(TileCfg<BN>::kThreads, TileCfg<BN>::kMinBlocks)
 k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M, int K, int cap_pad, int n,
              const float* __restrict__ w_scale, const float* __restrict__ act_e, uint32_t* err, Epi epi, SplitK sk) {
     extern __shared__ uint8_t smem_raw[];
@@ -309,7 +325,8 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
         const int e = warp - 2;
         const int quad = warp & 3;
         const int half = e >> 2;                  // which kSPT streams of the tile
-        const int u0 = half * (kSPT / 16);        // first 16-stream block
+        const int u0 = (half * kSPT) / 16;        // first 16-stream block
+        const int j0 = (half * kSPT) % 16;        // first stream inside it (kSPT = 8)
         const int rl = quad * 32 + lane;
         const int row = m0 + rl;
         const bool row_ok = row < M;
@@ -335,7 +352,7 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
 #pragma unroll
             for (int k = 0; k < kAePer; k++) {
                 int i = et + k * kET;
-                ta[k] = (i < acnt && n0 + i / G < n) ? act_e[(size_t)n0 * G + i] : 0.0f;
+                ta[k] = (i < acnt && n0 + i / G < n) ? act_e[(size_t)(n0 + i / G) * kEStride + i % G] : 0.0f;
             }
             epi.stage(n0, min(BN, n - n0), S.slot, S.fresh, et, kET);
 #pragma unroll
@@ -404,13 +421,13 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
         } else {
             // software pipeline: group g+1 is read from TMEM while group g is combined
             // (tcgen05.ld is asynchronous until tcgen05.wait::ld)
-            int cur[3][16], nxt[3][16];
-            const uint32_t ucol = (uint32_t)(u0 * 48);
+            int cur[3][kSPT], nxt[3][kSPT];
+            const uint32_t ucol = (uint32_t)(u0 * 48 + j0);
             bool have = __all_sync(0xffffffffu, mbar_wait(&S.tfull[0], 0, abort));
             if (have) {
                 tc_fence_after();
 #pragma unroll
-                for (int p = 0; p < 3; p++) tmem_ld16(tmem + lane_off + ucol + (uint32_t)(p * 16), cur[p]);
+                for (int p = 0; p < 3; p++) tmem_ld_n<kSPT>(tmem + lane_off + ucol + (uint32_t)(p * 16), cur[p]);
                 tmem_wait_ld();
             }
             for (int gl = 0; have && gl < GL; gl++) {
@@ -424,12 +441,12 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
                         tc_fence_after();
                         const uint32_t base = tmem + lane_off + (uint32_t)(nb * 3 * BN) + ucol;
 #pragma unroll
-                        for (int p = 0; p < 3; p++) tmem_ld16(base + (uint32_t)(p * 16), nxt[p]);
+                        for (int p = 0; p < 3; p++) tmem_ld_n<kSPT>(base + (uint32_t)(p * 16), nxt[p]);
                     }
                 }
                 const float wsg = S.ws[g * kBM + rl];
 #pragma unroll
-                for (int b = 0; b < 16; b++)
+                for (int b = 0; b < kSPT; b++)
                     acc[b] = group_accumulate(acc[b], digit_value(cur[0][b], cur[1][b], cur[2][b]), wsg,
                                               S.ae[(half * kSPT + b) * 32 + g]);
                 tc_fence_before();
@@ -444,22 +461,22 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
 #pragma unroll
                     for (int p = 0; p < 3; p++)
 #pragma unroll
-                        for (int b = 0; b < 16; b++) cur[p][b] = nxt[p][b];
+                        for (int b = 0; b < kSPT; b++) cur[p][b] = nxt[p][b];
                 }
             }
         }
         bool emit = true;
         if constexpr (BN == 16) {
-            static_assert(Smem<BN>::kStages * kBM * kBK >= 12 * kBM * BN * (int)sizeof(float),
-                          "the stage buffers hold the gathered sums of up to 12 splits");
+            static_assert(sizeof(Smem<BN>::a) + sizeof(Smem<BN>::b) >= (size_t)kMaxGatherSplits * kBM * BN * sizeof(float),
+                          "the stage buffers hold the gathered sums of kMaxGatherSplits splits");
             if (split) {
                 // publish this split's sums, then the tile's last CTA adds all splits in order
                 constexpr int kET = 128 * kEG;
                 const uint32_t tile = blockIdx.y * gridDim.x + blockIdx.x;
                 float* blk = sk.part + (size_t)tile * NS * (kBM * BN);
-                float4* mine = reinterpret_cast<float4*>(blk + ((size_t)zs * kBM + rl) * BN);
+                float4* mine = reinterpret_cast<float4*>(blk + ((size_t)zs * kBM + rl) * BN + half * kSPT);
 #pragma unroll
-                for (int q = 0; q < BN / 4; q++) mine[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+                for (int q = 0; q < kSPT / 4; q++) mine[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
                 __threadfence();
                 asm volatile("bar.sync 1, %0;" ::"r"(kET) : "memory");
                 if (threadIdx.x == 64 && !*abort) {
@@ -481,10 +498,11 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
                     emit = __all_sync(0xffffffffu, mbar_wait(&S.gather, 0, abort));
                     const float* P = reinterpret_cast<const float*>(&S.a[0][0]);
 #pragma unroll
-                    for (int b = 0; b < kSPT; b++) acc[b] = P[rl * BN + b];
+                    for (int b = 0; b < kSPT; b++) acc[b] = P[rl * BN + half * kSPT + b];
                     for (int sp = 1; sp < NS; sp++)
 #pragma unroll
-                        for (int b = 0; b < kSPT; b++) acc[b] = __fadd_rn(acc[b], P[((size_t)sp * kBM + rl) * BN + b]);
+                        for (int b = 0; b < kSPT; b++)
+                            acc[b] = __fadd_rn(acc[b], P[((size_t)sp * kBM + rl) * BN + half * kSPT + b]);
                 }
             } else {
 #pragma unroll
@@ -495,14 +513,15 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
             for (int b = 0; b < kSPT; b++) acc[b] = tot[b];
         }
         if (emit && !*abort && row_ok) {
+            constexpr int kCH = kSPT < 16 ? kSPT : 16;  // streams per epilogue call
 #pragma unroll
-            for (int c = 0; c < kSPT / 16; c++) {
-                float v[16];
+            for (int c = 0; c < kSPT / kCH; c++) {
+                float v[kCH];
 #pragma unroll
-                for (int i = 0; i < 16; i++) v[i] = acc[c * 16 + i];
-                const int tb = half * kSPT + c * 16;  // tile-relative first stream
+                for (int i = 0; i < kCH; i++) v[i] = acc[c * kCH + i];
+                const int tb = half * kSPT + c * kCH;  // tile-relative first stream
                 const int b0 = n0 + tb;
-                if (b0 < n) epi.template apply<16>(row, b0, min(16, n - b0), v, TileMeta{S.slot, S.fresh}, tb);
+                if (b0 < n) epi.template apply<kCH>(row, b0, min(kCH, n - b0), v, TileMeta{S.slot, S.fresh}, tb);
             }
         }
     }
