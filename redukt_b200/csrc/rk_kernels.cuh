@@ -438,30 +438,15 @@ struct EpiInProj {
 template <int RW, int NS, int NCH, class Epi>
 __global__ void __launch_bounds__(256) k_gemv_f32(int M, int K, const float* __restrict__ W,
                                                   const float* __restrict__ act, int ld_act, int n, Epi epi) {
-    pdl_wait();
-    pdl_trigger();
     extern __shared__ float4 smem_f4[];
     float* xs = reinterpret_cast<float*>(smem_f4);  // [NS][K]
-    int b0 = blockIdx.x * NS;
-    int ns = min(NS, n - b0);
-    int K4 = K >> 2;
-    for (int i = threadIdx.x; i < ns * K4; i += blockDim.x) {
-        int s = i / K4, k4 = i - s * K4;
-        reinterpret_cast<float4*>(xs)[s * K4 + k4] =
-            reinterpret_cast<const float4*>(act + (size_t)(b0 + s) * ld_act)[k4];
-    }
-    __syncthreads();
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int r0 = blockIdx.y * (8 * RW) + warp * RW;
-    if (r0 >= M) return;
-    float acc[RW][NS];
-#pragma unroll
-    for (int r = 0; r < RW; r++)
-#pragma unroll
-        for (int s = 0; s < NS; s++) acc[r][s] = 0.0f;
+    // the weights are constant: with unrolled chunks, every weight load of the row(s) is issued
+    // before the dependency wait (NCH x RW independent 16-byte loads per lane)
+    constexpr int kNW = NCH > 0 ? NCH : 1;
+    float4 wv[kNW][RW];
     if constexpr (NCH > 0) {
-        // all weight loads of the row(s) first (NCH x RW independent 16-byte loads per lane)
-        float4 wv[NCH][RW];
 #pragma unroll
         for (int c = 0; c < NCH; c++) {
             int k = c * 128 + lane * 4;
@@ -471,6 +456,25 @@ __global__ void __launch_bounds__(256) k_gemv_f32(int M, int K, const float* __r
                                ? __ldg(reinterpret_cast<const float4*>(W + (size_t)(r0 + r) * K + k))
                                : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+    }
+    pdl_wait();
+    pdl_trigger();
+    int b0 = blockIdx.x * NS;
+    int ns = min(NS, n - b0);
+    int K4 = K >> 2;
+    for (int i = threadIdx.x; i < ns * K4; i += blockDim.x) {
+        int s = i / K4, k4 = i - s * K4;
+        reinterpret_cast<float4*>(xs)[s * K4 + k4] =
+            reinterpret_cast<const float4*>(act + (size_t)(b0 + s) * ld_act)[k4];
+    }
+    __syncthreads();
+    if (r0 >= M) return;
+    float acc[RW][NS];
+#pragma unroll
+    for (int r = 0; r < RW; r++)
+#pragma unroll
+        for (int s = 0; s < NS; s++) acc[r][s] = 0.0f;
+    if constexpr (NCH > 0) {
 #pragma unroll
         for (int c = 0; c < NCH; c++) {
             int k = c * 128 + lane * 4;
@@ -656,8 +660,6 @@ struct ScanArgs {
 // dependency chains per thread).  Both evaluate the same trees in the same order.
 template <int TPC>
 __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
-    pdl_wait();
-    pdl_trigger();
     extern __shared__ float4 smem_f4[];
     float* zs = reinterpret_cast<float*>(smem_f4);  // [xr]
     __shared__ float s_max[8];
@@ -672,19 +674,38 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
     const bool ok = j < a.di && slot < (uint32_t)a.cap;
     const bool fresh = a.rflag[b] != 0;
     float* st = a.ssm + (((size_t)a.layer * a.cap + (ok ? slot : 0)) * kDState) * a.di + j;
-    // the recurrent state first: coalesced loads in flight while dt is computed
+    // Everything except x_proj's (dt_raw, B, C) is read before the dependency wait: the state and
+    // the reset flag come from earlier steps and kernels, conv_out and z from the in_proj two
+    // launches back (complete, since every kernel waits for its predecessor before it lets the
+    // next one start), the weights are constant.
     float s[kSt];
 #pragma unroll
     for (int k = 0; k < kSt; k++) s[k] = (ok && !fresh) ? st[(size_t)(t + TPC * k) * a.di] : 0.0f;
-    const float* zpb = a.zp + (size_t)b * a.xr;
-    for (int i = threadIdx.x; i < a.xr; i += blockDim.x) zs[i] = zpb[i];
-    __syncthreads();
     const int jj = ok ? j : 0;
     const float xv = a.conv_out[(size_t)b * a.di + jj];
     const float zv = a.z[(size_t)b * a.di + jj];
     // dt_proj row, 8-lane dot order: lane l accumulates columns c + l of the 8-aligned body
     const float* wt = a.dt_wt + jj;
     const int body = a.dr & ~7;
+    constexpr int kPre = 8;  // dt_proj columns c + t, c + t + 4 prefetched for dt_rank <= 64 (TPC = 4)
+    float wa[kPre], wb[kPre];
+    if constexpr (TPC != 1) {
+#pragma unroll
+        for (int i = 0; i < kPre; i++) {
+            const int c = 8 * i;
+            wa[i] = c < body ? __ldg(wt + (size_t)(c + t) * a.di) : 0.0f;
+            wb[i] = c < body ? __ldg(wt + (size_t)(c + t + 4) * a.di) : 0.0f;
+        }
+    }
+    float at[kSt];
+#pragma unroll
+    for (int k = 0; k < kSt; k++) at[k] = __ldg(a.a_t + (size_t)(t + TPC * k) * a.di + jj);
+    const float dtb = __ldg(a.dt_b + jj), dv = __ldg(a.dvec + jj);
+    pdl_wait();
+    pdl_trigger();
+    const float* zpb = a.zp + (size_t)b * a.xr;
+    for (int i = threadIdx.x; i < a.xr; i += blockDim.x) zs[i] = zpb[i];
+    __syncthreads();
     float dt;
     if constexpr (TPC == 1) {
         float l[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -698,7 +719,15 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
     } else {
         // this thread holds lanes t and t+4; the quad finishes hsum8 with xor 2 then xor 1
         float la = 0.0f, lb = 0.0f;
-        for (int c = 0; c < body; c += 8) {
+#pragma unroll
+        for (int i = 0; i < kPre; i++) {
+            const int c = 8 * i;
+            if (c < body) {
+                la = __fadd_rn(la, __fmul_rn(wa[i], zs[c + t]));
+                lb = __fadd_rn(lb, __fmul_rn(wb[i], zs[c + t + 4]));
+            }
+        }
+        for (int c = 8 * kPre; c < body; c += 8) {
             la = __fadd_rn(la, __fmul_rn(wt[(size_t)(c + t) * a.di], zs[c + t]));
             lb = __fadd_rn(lb, __fmul_rn(wt[(size_t)(c + t + 4) * a.di], zs[c + t + 4]));
         }
@@ -707,7 +736,7 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
         dt = __fadd_rn(pr, __shfl_xor_sync(0xffffffffu, pr, 1));
     }
     for (int c = body; c < a.dr; c++) dt = __fadd_rn(dt, __fmul_rn(wt[(size_t)c * a.di], zs[c]));
-    dt = softplus(__fadd_rn(dt, a.dt_b[jj]));
+    dt = softplus(__fadd_rn(dt, dtb));
 
     const float* B = zs + a.dr;
     const float* C = zs + a.dr + kDState;
@@ -717,7 +746,7 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
 #pragma unroll
         for (int k = 0; k < kSt; k++) {
             const int n2 = t + TPC * k;
-            const float da = lane_expf(__fsub_rn(0.0f, __fmul_rn(dt, a.a_t[(size_t)n2 * a.di + jj])));
+            const float da = lane_expf(__fsub_rn(0.0f, __fmul_rn(dt, at[k])));
             s[k] = __fadd_rn(__fmul_rn(da, s[k]), __fmul_rn(dtx, B[n2]));
         }
     }
@@ -742,7 +771,7 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
         h = __fadd_rn(h, __shfl_xor_sync(0xffffffffu, h, 1));
         h = __fadd_rn(h, __shfl_xor_sync(0xffffffffu, h, 2));
     }
-    const float y = __fadd_rn(h, __fmul_rn(a.dvec[jj], xv));
+    const float y = __fadd_rn(h, __fmul_rn(dv, xv));
     const float gated = ok ? __fmul_rn(y, __fmul_rn(zv, lane_sigmoid(zv))) : 0.0f;
     if (out.f) {
         if (ok && t == 0) out.f[(size_t)b * out.K + j] = gated;
