@@ -523,10 +523,10 @@ bool use_tc(int n) {
 int split_for(int tiles, int rows, int groups, int n, size_t part_cap) {
     if (n > kSplitMaxN || tiles > kSplitMaxTiles) return 1;
     const int S = q8_splits(groups);
-    if (S <= 1 || S > tc::kMaxGatherSplits || (long)tiles * S > g_split_target ||
-        split_part_floats(rows, groups, n) > part_cap)
-        return 1;
-    return S;
+    if (S <= 1 || S > tc::kMaxGatherSplits || split_part_floats(rows, groups, n) > part_cap) return 1;
+    for (int z = S; z > 1; z--)  // the most CTAs per tile that divide S and keep one wave
+        if (S % z == 0 && (long)tiles * z <= g_split_target) return z;
+    return 1;
 }
 
 template <int BN, class Epi>

@@ -41,7 +41,7 @@ struct TileCfg {
     static constexpr int kEG = 2;                            // epilogue warpgroups (each owns BN/2 streams)
     static constexpr int kSPT = BN / kEG;                    // streams per epilogue thread
     static constexpr int kThreads = 64 + 128 * kEG;          // producer + MMA warp + epilogue
-    static constexpr int kMinBlocks = BN == 16 ? 2 : 1;      // CTAs per SM the registers must allow
+    static constexpr int kMinBlocks = 1;                     // CTAs per SM the registers must allow (shared memory allows one)
 };
 
 template <int BN>
@@ -202,11 +202,12 @@ constexpr size_t launch_smem() {
 
 constexpr int kMaxGatherSplits = 8;  // split launches gather at most this many split blocks
 
-// Split-K launch: with splits == S, CTA z of a tile runs only split z and stores its 128 x BN sums to
-// `part`; the tile's last CTA to finish (an atomic counter per tile) copies the tile's S blocks into
-// shared memory and adds them in split order.  With splits == 1 one CTA runs all splits.
+// Split-K launch: with splits == Z (a divisor of S), CTA z of a tile runs splits [S z / Z, S (z+1) / Z)
+// and stores each one's 128 x BN sums to `part`; the tile's last CTA to finish (an atomic counter per
+// tile) copies the tile's S blocks into shared memory and adds them in split order.  With splits == 1
+// one CTA runs all splits.
 struct SplitK {
-    int splits;          // 1 or q8_splits(G)
+    int splits;          // CTAs per tile: 1 or a divisor of q8_splits(G)
     float* part;         // [tiles][S][128][BN] split sums
     uint32_t* counter;   // [tiles], zero between launches (the last CTA of a tile resets its entry)
 };
@@ -227,10 +228,12 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
     constexpr uint32_t kStageBytes = kBM * kBK + 3 * BN * kBK;
     const int G = K / kBK;                          // groups of a row
     const int NS = q8_splits(G);                     // splits of the accumulation order
-    const bool split = BN == 16 && sk.splits > 1;    // this launch: one CTA per split (narrow tiles only)
+    const bool split = BN == 16 && sk.splits > 1;    // this launch: splits.. CTAs per tile (narrow tiles only)
+    const int nz = split ? sk.splits : 1;            // CTAs per tile; divides NS
     const int zs = split ? (int)blockIdx.z : 0;
-    const int gb = split ? (G * zs) / NS : 0;        // this CTA's groups [gb, gb + GL)
-    const int GL = split ? (G * (zs + 1)) / NS - gb : G;
+    const int s0 = (NS * zs) / nz, s1 = (NS * (zs + 1)) / nz;  // this CTA's splits [s0, s1)
+    const int gb = (G * s0) / NS;                    // and groups [gb, gb + GL)
+    const int GL = (G * s1) / NS - gb;
     const int n0 = blockIdx.x * BN;
     const int m0 = blockIdx.y * kBM;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -378,14 +381,22 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
         for (int b = 0; b < kSPT; b++) acc[b] = tot[b] = 0.0f;
         // after group g: close the split if g is its last group (whole-row CTA: add it to tot;
         // split launch: this CTA's only split, kept in acc for the store below)
-        int sp = 0, send = G / NS;  // current split and its end group
+        int sp = s0, send = (G * (s0 + 1)) / NS;  // current split and its end group
+        const uint32_t tile = blockIdx.y * gridDim.x + blockIdx.x;
+        float* blk = sk.part + (size_t)tile * NS * (kBM * BN);  // split launch: the tile's split sums
         auto split_end = [&](int g) {
-            if (split || g + 1 != send) return;
+            if (g + 1 != send) return;
+            if (split) {  // publish the split's sums for the tile's last CTA
+                float4* mine = reinterpret_cast<float4*>(blk + ((size_t)sp * kBM + rl) * BN + half * kSPT);
 #pragma unroll
-            for (int b = 0; b < kSPT; b++) {
-                tot[b] = sp == 0 ? acc[b] : __fadd_rn(tot[b], acc[b]);
-                acc[b] = 0.0f;
+                for (int q = 0; q < kSPT / 4; q++)
+                    mine[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+            } else {
+#pragma unroll
+                for (int b = 0; b < kSPT; b++) tot[b] = sp == 0 ? acc[b] : __fadd_rn(tot[b], acc[b]);
             }
+#pragma unroll
+            for (int b = 0; b < kSPT; b++) acc[b] = 0.0f;
             sp++;
             send = (G * (sp + 1)) / NS;
         };
@@ -470,18 +481,14 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
             static_assert(sizeof(Smem<BN>::a) + sizeof(Smem<BN>::b) >= (size_t)kMaxGatherSplits * kBM * BN * sizeof(float),
                           "the stage buffers hold the gathered sums of kMaxGatherSplits splits");
             if (split) {
-                // publish this split's sums, then the tile's last CTA adds all splits in order
+                // this CTA's split sums are published (split_end); the tile's last CTA adds all
+                // splits in order
                 constexpr int kET = 128 * kEG;
-                const uint32_t tile = blockIdx.y * gridDim.x + blockIdx.x;
-                float* blk = sk.part + (size_t)tile * NS * (kBM * BN);
-                float4* mine = reinterpret_cast<float4*>(blk + ((size_t)zs * kBM + rl) * BN + half * kSPT);
-#pragma unroll
-                for (int q = 0; q < kSPT / 4; q++) mine[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
                 __threadfence();
                 asm volatile("bar.sync 1, %0;" ::"r"(kET) : "memory");
                 if (threadIdx.x == 64 && !*abort) {
                     const uint32_t old = atomicAdd(&sk.counter[tile], 1u);
-                    if (old == (uint32_t)NS - 1) {
+                    if (old == (uint32_t)nz - 1) {
                         sk.counter[tile] = 0u;  // ready for the next launch
                         __threadfence();
                         // other CTAs' generic-proxy writes, read below by the bulk-copy (async) proxy
