@@ -456,8 +456,21 @@ def run_reference(args, rank, world):
 
 
 def run_profile_case(n: int, quant: str = "q8") -> None:
-    """Small case for ncu captures: two eager (graph-free) steps of n streams through the C ABI."""
+    """Small case for ncu captures: two eager (graph-free) steps of n streams through the C ABI.
+    quant "rwkv7" runs the RWKV-7 0.1B W8A8 model instead of Mamba-130M."""
     from redukt_b200.plugin import PluginBackend
+    if quant == "rwkv7":
+        cache = os.environ.get("REDUKT_B200_MODEL_CACHE", os.path.join(tempfile.gettempdir(), "redukt_b200_models"))
+        path = rwkv7_rbin.ensure_model(os.path.join(cache, "rwkv7_0_1b.rbin"), rwkv7_rbin.RWKV7_0_1B)
+        b = PluginBackend(path)
+        b.set_option("graphs", 0)
+        b.batch_init(n)
+        toks = rwkv7_rbin.byte_tokens(n, 2)
+        for t in range(2):
+            b.forward_batch(list(range(n)), toks[:, t])
+        b.close()
+        print(json.dumps({"profile_case": n, "quant": quant, "steps": 2}))
+        return
     f32_path, q8_path = model_paths(0, 1, lambda: None)
     b = PluginBackend(q8_path if quant == "q8" else f32_path)
     b.set_option("graphs", 0)
@@ -481,7 +494,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--profile-case", type=int, default=0,
                     help="run two eager steps of N streams and exit (small case for ncu captures)")
-    ap.add_argument("--profile-quant", default="q8", choices=["q8", "f32"])
+    ap.add_argument("--profile-quant", default="q8", choices=["q8", "f32", "rwkv7"])
     args = ap.parse_args()
     if args.profile_case:
         run_profile_case(args.profile_case, args.profile_quant)

@@ -149,9 +149,23 @@ struct ActOut {
 // Norm of one stream by one warp (layer_norm_step, src/infrastructure/mamba/model.rs:193-200).
 // Lane l owns columns 128c + 4l .. 128c + 4l + 3; sums are sequential per lane, then a butterfly.
 // RMSNorm: x * (1 / sqrt(sum(x^2)/d + eps)) * w; LayerNorm: (x - mean) * inv_std * w + b.
+// The norm's weight and bias columns of one lane (constant: loaded before the dependency wait).
+template <int NC>
+struct NormWeights {
+    float4 w[NC], b[NC];
+    __device__ __forceinline__ void load(const float* __restrict__ wp, const float* __restrict__ bp, int d, int lane) {
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            int k = c * 128 + lane * 4;
+            w[c] = k < d ? __ldg(reinterpret_cast<const float4*>(wp + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            b[c] = (bp && k < d) ? __ldg(reinterpret_cast<const float4*>(bp + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+};
+
 template <int NC>  // NC = d / 128 rounded up; d <= 128 * NC
-__device__ __forceinline__ void norm_row_warp(int b, const float* __restrict__ x, int d, const float* __restrict__ w,
-                                              const float* __restrict__ bias, const ActOut& out, int lane) {
+__device__ __forceinline__ void norm_row_warp(int b, const float* __restrict__ x, int d, const NormWeights<NC>& nw,
+                                              bool has_bias, const ActOut& out, int lane) {
     const float* xb = x + (size_t)b * d;
     float4 v[NC];
 #pragma unroll
@@ -161,7 +175,7 @@ __device__ __forceinline__ void norm_row_warp(int b, const float* __restrict__ x
         if (k < d) v[c] = *reinterpret_cast<const float4*>(xb + k);
     }
     float mean = 0.0f, inv;
-    if (bias) {
+    if (has_bias) {
         float s = 0.0f;
 #pragma unroll
         for (int c = 0; c < NC; c++) {
@@ -199,9 +213,9 @@ __device__ __forceinline__ void norm_row_warp(int b, const float* __restrict__ x
         bool ok = k < d;
         float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
         if (ok) {
-            float4 wv = *reinterpret_cast<const float4*>(w + k);
-            if (bias) {
-                float4 bv = *reinterpret_cast<const float4*>(bias + k);
+            const float4 wv = nw.w[c];
+            if (has_bias) {
+                const float4 bv = nw.b[c];
                 o.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[c].x, mean), inv), wv.x), bv.x);
                 o.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[c].y, mean), inv), wv.y), bv.y);
                 o.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[c].z, mean), inv), wv.z), bv.z);
@@ -237,11 +251,13 @@ __device__ __forceinline__ void norm_row_warp(int b, const float* __restrict__ x
 template <int NC>
 __global__ void k_norm(int n, const float* __restrict__ x, int d, const float* __restrict__ w,
                        const float* __restrict__ bias, ActOut out) {
+    NormWeights<NC> nw;
+    nw.load(w, bias, d, threadIdx.x & 31);
     pdl_wait();
     pdl_trigger();
     int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (b >= n) return;
-    norm_row_warp<NC>(b, x, d, w, bias, out, threadIdx.x & 31);
+    norm_row_warp<NC>(b, x, d, nw, bias != nullptr, out, threadIdx.x & 31);
 }
 
 // ------------------------------------------------------------------------------------------

@@ -399,7 +399,7 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
             wv.job[0] = job(Y.fv, p.aq0, p.as, p.x, D, kW8Add);
             project(wv, 1, st);
         }
-        launches += 11;
+        launches += 10;
     }
     {
         KScope k(kKNorm, st);
