@@ -70,6 +70,39 @@ def test_batch_bit_identical_to_v1_every_batch_size(ref_test_rbin, quant):
                 assert np.array_equal(bits(out[s]), bits(single[s, t])), (quant, n, s, t)
 
 
+@pytest.mark.parametrize("quant", ["f32", "q8"])
+@pytest.mark.parametrize("model", ["reftest", "gauss_small"])
+def test_large_batches_bit_identical_to_small(ref_test_rbin, small_gauss_rbin, model, quant):
+    """Large batches take other launch shapes (several streams per scan CTA, other projection
+    tiles): every stream still reproduces the bits of the same stream in a batch of four, with
+    slot resets in the middle of the window.  The two models cover a channel count that is not a
+    multiple of the scan's 256-channel CTA and dt ranks below and at one 8-lane body."""
+    base = ref_test_rbin if model == "reftest" else small_gauss_rbin
+    path = base if quant == "f32" else q8(base)
+    b = backend(path)
+    V = b.vocab_size
+    steps = 4
+    for n in (70, 300, 517):
+        toks = zipf_tokens(n, steps, vocab=V, seed_base=n)
+        cap = n + 3
+        slots = [(7 * s + 1) % cap for s in range(n)]
+        reset_at = {s for s in range(n) if s % 5 == 2}
+        b.batch_init(cap)
+        full = []
+        for t in range(steps):
+            if t == 2:
+                b.batch_reset([slots[s] for s in sorted(reset_at)])
+            full.append(b.forward_batch(slots, toks[:, t]).copy())
+        sub = [0, 2, n // 2, n - 1]
+        b.batch_init(8)
+        for t in range(steps):
+            if t == 2:
+                b.batch_reset([i for i, s in enumerate(sub) if s in reset_at])
+            out = b.forward_batch(list(range(len(sub))), toks[sub, t])
+            for i, s in enumerate(sub):
+                assert np.array_equal(bits(out[i]), bits(full[t][s])), (model, quant, n, s, t)
+
+
 def test_reset_then_step0_and_invalid_arguments(ref_test_rbin):
     b = backend(ref_test_rbin)
     V = b.vocab_size
