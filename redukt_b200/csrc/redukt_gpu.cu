@@ -20,6 +20,7 @@
 
 #include "../../include/redukt_gpu.h"
 #include "rk_kernels.cuh"
+#include "rk_fused.cuh"
 #include "rk_rwkv7.cuh"
 #include "rk_tc.cuh"
 
@@ -93,9 +94,12 @@ struct Pool {
     float* act_e = nullptr;      // [cap][kEStride]
     float* conv_out = nullptr;   // [cap][di]
     float* z = nullptr;          // [cap][di]
-    float* zp = nullptr;         // [cap][xr]
     float* logits = nullptr;     // [cap][V]
     float* red = nullptr;        // [cap][softmax partial slots] (max, sum) pairs
+    float* xpart = nullptr;      // x_proj group chains [cap][di/64][xr] (k_xproj_part, fused step)
+    float* zp = nullptr;         // [cap][xr] x_proj output (dt_raw, B, C)
+    uint32_t* xcount = nullptr;  // [cap/16] k_xproj_part arrival counters (self-resetting)
+    uint32_t* bar = nullptr;     // fused step: grid-barrier counter
     float* part = nullptr;       // split-K split sums [tiles][S][128][16] (Q8, up to 64 streams)
     size_t part_cap = 0;         // floats in `part`
     uint32_t* counter = nullptr; // split-K tile counters
@@ -130,9 +134,16 @@ struct Model {
     bool use_pdl = true;   // programmatic dependent launch between the step's kernels
     bool rwkv = false;     // an RWKV-7 model is loaded (rwkv7_engine.cuh) instead of Mamba
     bool ready = false;
+    // fused small-batch step (rk_fused.cuh)
+    bool fused = true;          // option "fused"
+    int fused_nc = 0;           // norm chunks of the instantiated kernel, 0 = shape not supported
+    int fused_ctas_per_sm = 2;  // option "fused_ctas"
+    int num_sms = 0;
+    FusedLayer* d_fused = nullptr;  // [nl] device copy of the layer pointers
 };
 
 Model G;
+bool prepare_fused();
 
 // ------------------------------------------------------------------------------------------
 // Allocation helpers
@@ -162,7 +173,8 @@ void pool_free(Pool* p) {
     p->graphs.clear();
     p->eager_done.clear();
     void* bufs[] = {p->conv, p->ssm, p->since, p->x, p->act_f, p->act_q, p->act_e, p->conv_out, p->z,
-                    p->zp, p->logits, p->red, p->part, p->counter, p->rflag, p->d_slots, p->d_tokens};
+                    p->logits, p->red, p->part, p->counter, p->rflag, p->d_slots, p->d_tokens,
+                    p->xpart, p->bar, p->zp, p->xcount};
     for (void* b : bufs) cudaFree(b);
     if (p->h_slots) cudaFreeHost(p->h_slots);
     if (p->h_tokens) cudaFreeHost(p->h_tokens);
@@ -188,7 +200,8 @@ bool pool_alloc(Pool* p, uint32_t cap) {
     size_t parts = (V + kSoftmaxTile - 1) / kSoftmaxTile;
     bool ok = dalloc(&p->conv, L * n * 3 * di) && dalloc(&p->ssm, L * n * kDState * di) &&
               dalloc(&p->since, n) && dalloc(&p->x, n * d) && dalloc(&p->conv_out, n * di) &&
-              dalloc(&p->z, n * di) && dalloc(&p->zp, n * G.xr) && dalloc(&p->logits, n * V) &&
+              dalloc(&p->z, n * di) && dalloc(&p->xpart, n * ((di + 63) / 64) * G.xr) && dalloc(&p->zp, n * G.xr) &&
+              dalloc(&p->xcount, (n + 15) / 16) && dalloc(&p->logits, n * V) &&
               dalloc(&p->red, n * parts * 2) && dalloc(&p->rflag, n) && dalloc(&p->d_slots, n) &&
               dalloc(&p->d_tokens, n);
     if (ok) {
@@ -201,6 +214,7 @@ bool pool_alloc(Pool* p, uint32_t cap) {
             p->part_cap = std::max(split_part_floats(2 * (int)di, (int)d / kGroup, nn),
                                    split_part_floats((int)d, (int)di / kGroup, nn));
             ok = ok && dalloc(&p->part, p->part_cap, false) && dalloc(&p->counter, kSplitMaxTiles);
+            ok = ok && dalloc(&p->bar, 1);
         }
     }
     if (ok) ok = cudaHostAlloc(reinterpret_cast<void**>(&p->h_slots), n * sizeof(uint32_t), cudaHostAllocDefault) ==
@@ -399,6 +413,7 @@ int load_weights(const char* path) {
         }
     }
     ok = ok && load_f32(r, &G.norm_f_w, d) && (!nb || load_f32(r, &G.norm_f_b, d));
+    if (ok && G.profile != kF32) ok = prepare_fused();
     G.head_tied = !untied;
     if (ok && untied) ok = load_mat(r, &G.head, G.V, G.d, true);
     if (ok && !untied) G.head = G.emb;
@@ -412,6 +427,56 @@ int load_weights(const char* path) {
         return BACKEND_WEIGHTS_NOT_FOUND;
     }
     return BACKEND_OK;
+}
+
+// The fused step's layer table and shape check (rk_fused.cuh).  Shapes it does not cover keep
+// the per-kernel path: d and d_inner in whole 64-column groups, at most kEStride groups, and a
+// norm width the kernel is instantiated for.
+bool prepare_fused() {
+    G.fused_nc = 0;
+    const int nc = (G.d + 127) / 128;
+    const bool shape_ok = G.d % 64 == 0 && G.di % 64 == 0 && G.d / 64 <= kEStride && G.di / 64 <= kEStride &&
+                          (nc == 1 || nc == 2 || nc == 6 || nc == 8) && G.xr % 4 == 0 && 8 * G.xr <= 4 * kFusedThreads;
+    std::vector<FusedLayer> h(G.nl);
+    const int ng = G.di / 64, xr = G.xr, dr = G.dr;
+    if (shape_ok) {
+        // per-channel-group copies of the small per-layer operands, so the fused step fetches each
+        // group's share with one contiguous copy: x_proj [ng][xr][68], conv taps + bias [ng][5][64],
+        // dt_proj columns + A + dt bias + D [ng][dr + 18][64]
+        for (int i = 0; i < G.nl; i++) {
+            const Layer& L = G.layers[i];
+            float *xw = nullptr, *ct = nullptr, *sb = nullptr;
+            if (!model_alloc(&xw, (size_t)ng * xr * 68) || !model_alloc(&ct, (size_t)ng * 5 * 64) ||
+                !model_alloc(&sb, (size_t)ng * (dr + 18) * 64))
+                return false;
+            bool ok = true;
+            const size_t row = 64 * sizeof(float), src_pitch = (size_t)G.di * sizeof(float);
+            for (int g = 0; ok && g < ng; g++) {
+                const size_t c0 = (size_t)g * 64;
+                ok = cudaMemcpy2D(xw + (size_t)g * xr * 68, 68 * sizeof(float), L.x_proj + c0, src_pitch, row, xr,
+                                  cudaMemcpyDeviceToDevice) == cudaSuccess &&
+                     cudaMemcpy2D(ct + (size_t)g * 5 * 64, row, L.conv_t + c0, src_pitch, row, 4,
+                                  cudaMemcpyDeviceToDevice) == cudaSuccess &&
+                     cudaMemcpy(ct + (size_t)g * 5 * 64 + 4 * 64, L.conv_b + c0, row, cudaMemcpyDeviceToDevice) ==
+                         cudaSuccess &&
+                     cudaMemcpy2D(sb + (size_t)g * (dr + 18) * 64, row, L.dt_wt + c0, src_pitch, row, dr,
+                                  cudaMemcpyDeviceToDevice) == cudaSuccess &&
+                     cudaMemcpy2D(sb + ((size_t)g * (dr + 18) + dr) * 64, row, L.a_t + c0, src_pitch, row, kDState,
+                                  cudaMemcpyDeviceToDevice) == cudaSuccess &&
+                     cudaMemcpy(sb + ((size_t)g * (dr + 18) + dr + 16) * 64, L.dt_b + c0, row,
+                                cudaMemcpyDeviceToDevice) == cudaSuccess &&
+                     cudaMemcpy(sb + ((size_t)g * (dr + 18) + dr + 17) * 64, L.dvec + c0, row,
+                                cudaMemcpyDeviceToDevice) == cudaSuccess;
+            }
+            if (!ok) return false;
+            h[i] = FusedLayer{L.norm_w, L.norm_b, L.in_proj.q, L.in_proj.s, L.out_proj.q, L.out_proj.s, xw, ct, sb};
+        }
+    }
+    if (!model_alloc(&G.d_fused, (size_t)G.nl)) return false;
+    if (cudaMemcpy(G.d_fused, h.data(), h.size() * sizeof(FusedLayer), cudaMemcpyHostToDevice) != cudaSuccess) return false;
+    cudaDeviceGetAttribute(&G.num_sms, cudaDevAttrMultiProcessorCount, G.device);
+    if (shape_ok && G.num_sms > 0) G.fused_nc = nc;
+    return true;
 }
 
 // ------------------------------------------------------------------------------------------
@@ -472,12 +537,13 @@ void gemv_f32(int M, int K, const float* W, const float* act, int ld, int n, Epi
     else gemv_f32_ns<RW, 1>(M, K, W, act, ld, n, epi, st);
 }
 
-// x_proj: few rows (dt_rank + 32), so streams are tiled finely to fill the GPU.
-template <class Epi>
-void gemv_f32_small_m(int M, int K, const float* W, const float* act, int ld, int n, Epi epi, cudaStream_t st) {
-    if (n >= 4) gemv_f32_ns<1, 4>(M, K, W, act, ld, n, epi, st);
-    else if (n >= 2) gemv_f32_ns<1, 2>(M, K, W, act, ld, n, epi, st);
-    else gemv_f32_ns<1, 1>(M, K, W, act, ld, n, epi, st);
+// x_proj of every profile: group chains into p.xpart[b][g][r], summed in group order into p.zp.
+void launch_xproj(const float* W, const Pool& p, int n, cudaStream_t st) {
+    const int ng = (G.di + kXGroup - 1) / kXGroup;
+    const size_t smem = ((size_t)G.xr * 68 + 16 * 68) * sizeof(float);
+    allow_smem(k_xproj_part, smem);
+    launch(k_xproj_part, dim3(ng, (n + 15) / 16), dim3(256), smem, st, G.xr, G.di, W, (const float*)p.conv_out, n,
+           p.xpart, p.zp, p.xcount);
 }
 
 template <int NS, int GI, class Epi>
@@ -668,10 +734,86 @@ struct KScope {
 
 int g_launches_per_step = 0;
 
+// ---- fused small-batch step (rk_fused.cuh) ----
+
+bool use_fused(int n) {
+    return G.profile != kF32 && G.fused && G.fused_nc > 0 && G.proj_path == 0 && !g_kt.on && n >= 1 &&
+           n <= kFusedMaxN;
+}
+
+template <int NC>
+void launch_fused_nc(const FusedArgs& fa, size_t smem, cudaStream_t st) {
+    auto k = k_step_fused<NC>;
+    allow_smem(k, smem);
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kFusedThreads, smem);
+    per_sm = std::min(per_sm, G.fused_ctas_per_sm);
+    if (per_sm < 1) per_sm = 1;  // the launch itself reports a grid that cannot be co-resident
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(G.num_sms * per_sm));
+    cfg.blockDim = dim3(kFusedThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the grid barriers need it
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, k, fa);
+}
+
+void launch_fused(Pool& p, int n, const uint32_t* d_slots, cudaStream_t st) {
+    FusedArgs fa{};
+    fa.n = n;
+    fa.cap = (int)p.cap;
+    fa.cap_pad = p.cap_pad;
+    fa.d = G.d;
+    fa.di = G.di;
+    fa.dr = G.dr;
+    fa.xr = G.xr;
+    fa.nl = G.nl;
+    fa.g_in = G.d / kGroup;
+    fa.s_in = q8_splits(fa.g_in);
+    fa.mpad_in = round_up(2 * G.di, 128);
+    fa.g_out = G.di / kGroup;
+    fa.s_out = q8_splits(fa.g_out);
+    fa.mpad_out = round_up(G.d, 128);
+    const int grid = G.num_sms * std::max(1, std::min(G.fused_ctas_per_sm, 1));
+    const int nmb = G.di / 64, nt = (n + 7) / 8;
+    fa.sga = 2 * nmb * nt <= grid ? 8 : 16;
+    fa.sgb = nmb * ((n + 3) / 4) <= grid ? 4 : 8;
+    fa.mc = (G.d / 16) * nt <= grid ? 16 : 32;
+    fa.pitch_a = G.d + 16;
+    fa.slots = d_slots;
+    fa.rflag = p.rflag;
+    fa.x = p.x;
+    fa.conv = p.conv;
+    fa.ssm = p.ssm;
+    fa.conv_out = p.conv_out;
+    fa.z = p.z;
+    fa.xpart = p.xpart;
+    fa.act_q = p.act_q;
+    fa.act_e = p.act_e;
+    fa.layers = G.d_fused;
+    fa.norm_f_w = G.norm_f_w;
+    fa.norm_f_b = G.norm_f_b;
+    fa.bar = p.bar;
+    fa.err = G.d_err;
+    fa.lay = fused_layout(fa);
+    const size_t smem = (size_t)fa.lay.total;
+    switch (G.fused_nc) {
+        case 1: launch_fused_nc<1>(fa, smem, st); break;
+        case 2: launch_fused_nc<2>(fa, smem, st); break;
+        case 6: launch_fused_nc<6>(fa, smem, st); break;
+        default: launch_fused_nc<8>(fa, smem, st); break;
+    }
+}
+
 // Enqueues one decode step for n streams whose slots/tokens are already on the device.
 int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_tokens, float* d_out, bool probs,
                  cudaStream_t st) {
-    StepArgs sa{n, (int)p.cap, d_slots, d_tokens, p.rflag, p.since, G.reset_every, G.d_err};
+    const bool fused = use_fused(n);
+    StepArgs sa{n, (int)p.cap, d_slots, d_tokens, p.rflag, p.since, G.reset_every, G.d_err, fused ? p.bar : nullptr};
     const Mat& emb = G.emb;
     int launches = 0;
     {
@@ -680,7 +822,11 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
                G.V, p.x);
         launches++;
     }
-    for (int li = 0; li < G.nl; li++) {
+    if (fused) {  // every layer and the final norm in one persistent kernel
+        launch_fused(p, n, d_slots, st);
+        launches++;
+    }
+    for (int li = 0; !fused && li < G.nl; li++) {
         const Layer& L = G.layers[li];
         {
             KScope k(kKNorm, st);
@@ -694,7 +840,7 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
         }
         {
             KScope k(kKXProj, st);
-            gemv_f32_small_m(G.xr, G.di, L.x_proj, p.conv_out, G.di, n, EpiStore{p.zp, G.xr}, st);
+            launch_xproj(L.x_proj, p, n, st);
         }
         {
             KScope k(kKScan, st);
@@ -711,7 +857,7 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
         }
         launches += 4;
     }
-    {
+    if (!fused) {
         KScope k(kKNorm, st);
         launch_norm(p, n, G.norm_f_w, G.norm_f_b, G.d, st);
         launches++;
@@ -755,7 +901,8 @@ int capture_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
 }
 
 uint64_t graph_key(int n, bool probs) {
-    return (uint64_t)n | ((uint64_t)probs << 13) | ((uint64_t)G.proj_path << 14) | ((uint64_t)G.reset_every << 16);
+    return (uint64_t)n | ((uint64_t)probs << 13) | ((uint64_t)G.proj_path << 14) | ((uint64_t)G.reset_every << 16) |
+           ((uint64_t)G.fused << 60);
 }
 
 // Enqueue one step for this pool's fixed buffers.  The first call for a (n, probs, options)
@@ -1166,7 +1313,7 @@ int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* m
                     EpiInProj ein{G.di, (int)p.cap, li, p.d_slots, p.rflag, p.conv, L.conv_t, L.conv_b, p.conv_out, p.z};
                     project(L.in_proj, p, nn, ein, st);
                 }
-                if (cls == kKXProj) gemv_f32_small_m(G.xr, G.di, L.x_proj, p.conv_out, G.di, nn, EpiStore{p.zp, G.xr}, st);
+                if (cls == kKXProj) launch_xproj(L.x_proj, p, nn, st);
                 if (cls == kKScan) {
                     ScanArgs sc{G.di, G.dr, G.xr, (int)p.cap, li, p.d_slots, p.rflag, p.zp, p.conv_out, p.z,
                                 L.dt_wt, L.dt_b, L.a_t, L.dvec, p.ssm};
@@ -1252,6 +1399,18 @@ int32_t redukt_b200_set_option(const char* key, int64_t value) {
         for (Pool* p : {&G.v1, &G.batch}) {  // captured graphs hold the old grids
             for (auto& kv : p->graphs) cudaGraphExecDestroy(kv.second);
             p->graphs.clear();
+        }
+        clear_dev_graphs();
+        return BACKEND_OK;
+    }
+    if (!strcmp(key, "fused") || !strcmp(key, "fused_ctas")) {
+        if (!strcmp(key, "fused")) G.fused = value != 0;
+        else if (value < 1 || value > 4) return BACKEND_INVALID_ARGUMENT;
+        else G.fused_ctas_per_sm = (int)value;
+        for (Pool* p : {&G.v1, &G.batch}) {  // captured graphs hold the old launch sequence
+            for (auto& kv : p->graphs) cudaGraphExecDestroy(kv.second);
+            p->graphs.clear();
+            p->eager_done.clear();
         }
         clear_dev_graphs();
         return BACKEND_OK;

@@ -97,6 +97,7 @@ struct StepArgs {
     uint32_t* since;              // [cap] forwards since the slot's last reset
     uint32_t reset_every;         // 0 = never (host-driven resets only)
     uint32_t* err;                // device error word (bad slot/token seen on device)
+    uint32_t* bar = nullptr;      // grid-barrier counter of the fused step, zeroed here
 };
 
 // Embedding row + the periodic reset decision (MambaState::maybe_periodic_reset,
@@ -107,6 +108,7 @@ __global__ void k_embed(StepArgs a, const float* __restrict__ emb_f, const int8_
     pdl_wait();
     pdl_trigger();
     int b = blockIdx.x;
+    if (a.bar && b == 0 && threadIdx.x == 0) *a.bar = 0u;
     if (b >= a.n) return;
     uint32_t tok = a.tokens[b], slot = a.slots[b];
     bool bad = tok >= (uint32_t)vocab || slot >= (uint32_t)a.cap;
@@ -163,17 +165,21 @@ struct NormWeights {
     }
 };
 
-template <int NC>  // NC = d / 128 rounded up; d <= 128 * NC
-__device__ __forceinline__ void norm_row_warp(int b, const float* __restrict__ x, int d, const NormWeights<NC>& nw,
-                                              bool has_bias, const ActOut& out, int lane) {
-    const float* xb = x + (size_t)b * d;
-    float4 v[NC];
+// The stream's row, lane l holding columns 128c + 4l .. 128c + 4l + 3 (zeros past d).
+template <int NC>
+__device__ __forceinline__ void norm_load(const float* xb, int d, int lane, float4 (&v)[NC]) {
 #pragma unroll
     for (int c = 0; c < NC; c++) {
         int k = c * 128 + lane * 4;
         v[c] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (k < d) v[c] = *reinterpret_cast<const float4*>(xb + k);
     }
+}
+
+// Normalises the loaded row in place (columns past d become zero).
+template <int NC>  // NC = d / 128 rounded up; d <= 128 * NC
+__device__ __forceinline__ void norm_apply(float4 (&v)[NC], int d, const NormWeights<NC>& nw, bool has_bias,
+                                           int lane) {
     float mean = 0.0f, inv;
     if (has_bias) {
         float s = 0.0f;
@@ -210,9 +216,8 @@ __device__ __forceinline__ void norm_row_warp(int b, const float* __restrict__ x
 #pragma unroll
     for (int c = 0; c < NC; c++) {
         int k = c * 128 + lane * 4;
-        bool ok = k < d;
         float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (ok) {
+        if (k < d) {
             const float4 wv = nw.w[c];
             if (has_bias) {
                 const float4 bv = nw.b[c];
@@ -227,24 +232,57 @@ __device__ __forceinline__ void norm_row_warp(int b, const float* __restrict__ x
                 o.w = __fmul_rn(__fmul_rn(v[c].w, inv), wv.w);
             }
         }
-        if (out.f) {
-            if (ok) *reinterpret_cast<float4*>(out.f + (size_t)b * out.K + k) = o;
-        } else {
-            // 64-column groups: lanes 0-15 hold group 2c, lanes 16-31 group 2c+1.
-            float m = fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w)));
-            m = warp_allmax(m, 16);
-            float ginv, gs = group_scale(m, &ginv);
-            if (ok) {
-                Digits3 a0 = split_digits(o.x, ginv), a1 = split_digits(o.y, ginv);
-                Digits3 a2 = split_digits(o.z, ginv), a3 = split_digits(o.w, ginv);
-                // four consecutive columns stay inside one 16-byte chunk of the swizzled row
-                *reinterpret_cast<int*>(out.q + dq_off(out.cap_pad, 0, b, k)) = pack4(a0.d1, a1.d1, a2.d1, a3.d1);
-                *reinterpret_cast<int*>(out.q + dq_off(out.cap_pad, 1, b, k)) = pack4(a0.d2, a1.d2, a2.d2, a3.d2);
-                *reinterpret_cast<int*>(out.q + dq_off(out.cap_pad, 2, b, k)) = pack4(a0.d3, a1.d3, a2.d3, a3.d3);
-                if ((lane & 15) == 0) out.e[(size_t)b * kEStride + (k / kGroup)] = gs;
-            }
+        v[c] = o;
+    }
+}
+
+// Digit planes of a normalised row over 64-column groups: lanes 0-15 hold group 2c, lanes 16-31
+// group 2c+1.  sink(k, d1x4, d2x4, d3x4, gs, lead) receives lane-packed digits of columns
+// k .. k+3 (k < d only); `lead` marks the group's first lane, which also passes the exponent.
+template <int NC, class Sink>
+__device__ __forceinline__ void norm_emit_q(const float4 (&o)[NC], int d, int lane, Sink sink) {
+#pragma unroll
+    for (int c = 0; c < NC; c++) {
+        int k = c * 128 + lane * 4;
+        float m = fmaxf(fmaxf(fabsf(o[c].x), fabsf(o[c].y)), fmaxf(fabsf(o[c].z), fabsf(o[c].w)));
+        m = warp_allmax(m, 16);
+        float ginv, gs = group_scale(m, &ginv);
+        if (k < d) {
+            Digits3 a0 = split_digits(o[c].x, ginv), a1 = split_digits(o[c].y, ginv);
+            Digits3 a2 = split_digits(o[c].z, ginv), a3 = split_digits(o[c].w, ginv);
+            sink(k, pack4(a0.d1, a1.d1, a2.d1, a3.d1), pack4(a0.d2, a1.d2, a2.d2, a3.d2),
+                 pack4(a0.d3, a1.d3, a2.d3, a3.d3), gs, (lane & 15) == 0);
         }
     }
+}
+
+// Norm of one stream by one warp into an activation sink (f32 row or tiled digit planes).
+template <int NC>
+__device__ __forceinline__ void norm_emit(int b, const float4 (&o)[NC], int d, const ActOut& out, int lane) {
+    if (out.f) {
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            int k = c * 128 + lane * 4;
+            if (k < d) *reinterpret_cast<float4*>(out.f + (size_t)b * out.K + k) = o[c];
+        }
+        return;
+    }
+    // four consecutive columns stay inside one 16-byte chunk of the swizzled row
+    norm_emit_q<NC>(o, d, lane, [&](int k, int p1, int p2, int p3, float gs, bool lead) {
+        *reinterpret_cast<int*>(out.q + dq_off(out.cap_pad, 0, b, k)) = p1;
+        *reinterpret_cast<int*>(out.q + dq_off(out.cap_pad, 1, b, k)) = p2;
+        *reinterpret_cast<int*>(out.q + dq_off(out.cap_pad, 2, b, k)) = p3;
+        if (lead) out.e[(size_t)b * kEStride + (k / kGroup)] = gs;
+    });
+}
+
+template <int NC>
+__device__ __forceinline__ void norm_row_warp(int b, const float* x, int d, const NormWeights<NC>& nw,
+                                              bool has_bias, const ActOut& out, int lane) {
+    float4 v[NC];
+    norm_load<NC>(x + (size_t)b * d, d, lane, v);
+    norm_apply<NC>(v, d, nw, has_bias, lane);
+    norm_emit<NC>(b, v, d, out, lane);
 }
 
 // One stream per warp.
@@ -315,6 +353,17 @@ struct EpiResidual {  // x[b][row] += v (src/infrastructure/mamba/model.rs:716-7
     }
 };
 
+// One channel of the causal conv1d step + SiLU: taps t0..t3 over (s0, s1, s2, v), then the bias.
+__device__ __forceinline__ float conv_silu_taps(float s0, float s1, float s2, float v, float t0, float t1, float t2,
+                                                float t3, float bias) {
+    float val = __fadd_rn(0.0f, __fmul_rn(s0, t0));
+    val = __fadd_rn(val, __fmul_rn(s1, t1));
+    val = __fadd_rn(val, __fmul_rn(s2, t2));
+    val = __fadd_rn(val, __fmul_rn(v, t3));
+    val = __fadd_rn(val, bias);
+    return __fmul_rn(val, lane_sigmoid(val));
+}
+
 // in_proj epilogue: rows [0, di) are the x-branch, fed straight into the causal conv1d + SiLU
 // (conv_silu_block, src/infrastructure/mamba/model.rs:134-153: val = sum_k st[k]*w[k] + x*w[3]
 // + b, shift, SiLU); rows [di, 2di) are the gate z.
@@ -329,12 +378,8 @@ struct EpiInProj {
     float* z;                 // [stream][di]
 
     __device__ __forceinline__ float conv_silu(int j, float s0, float s1, float s2, float v) const {
-        float val = __fadd_rn(0.0f, __fmul_rn(s0, conv_t[j]));
-        val = __fadd_rn(val, __fmul_rn(s1, conv_t[di + j]));
-        val = __fadd_rn(val, __fmul_rn(s2, conv_t[2 * di + j]));
-        val = __fadd_rn(val, __fmul_rn(v, conv_t[3 * di + j]));
-        val = __fadd_rn(val, conv_b[j]);
-        return __fmul_rn(val, lane_sigmoid(val));
+        return conv_silu_taps(s0, s1, s2, v, conv_t[j], conv_t[di + j], conv_t[2 * di + j], conv_t[3 * di + j],
+                              conv_b[j]);
     }
 
     __device__ __forceinline__ void operator()(int row, int b, float v) const {
@@ -550,6 +595,158 @@ __global__ void __launch_bounds__(256) k_gemv_f32(int M, int K, const float* __r
 }
 
 // ------------------------------------------------------------------------------------------
+// x_proj: (dt_raw, B, C)[b][r] = W_x[r] . conv_out[b] in a fixed two-level order.  Each 64-channel
+// group g gives a sequential FMA chain over its channels from zero (xproj_chain); the group sums
+// are then added in group order.  The fused step kernel evaluates the group chains in the CTAs
+// that produce those channels and adds them in the same order, so both give the same bits.
+// ------------------------------------------------------------------------------------------
+constexpr int kXGroup = 64;
+
+__device__ __forceinline__ float xproj_chain(const float* w, const float* x, int len) {
+    float acc = 0.0f;
+#pragma unroll 16
+    for (int c = 0; c < len; c++) acc = __fmaf_rn(w[c], x[c], acc);
+    return acc;
+}
+
+// The same chain with the weights read as 16-byte vectors (len == 64, w 16-byte aligned).
+__device__ __forceinline__ float xproj_chain64_v(const float* __restrict__ w, const float* x) {
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    float4 wv[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) wv[i] = __ldg(w4 + i);
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        acc = __fmaf_rn(wv[i].x, x[4 * i], acc);
+        acc = __fmaf_rn(wv[i].y, x[4 * i + 1], acc);
+        acc = __fmaf_rn(wv[i].z, x[4 * i + 2], acc);
+        acc = __fmaf_rn(wv[i].w, x[4 * i + 3], acc);
+    }
+    return acc;
+}
+
+// (dt_raw, B, C) of stream b: its x_proj group chains [G][M] added in group order.
+__device__ __forceinline__ void xproj_sum_groups(const float* pb, int G, int M, float* out) {
+    for (int r = threadIdx.x; r < M; r += blockDim.x) {
+        float v[32];
+        float tot = 0.0f;
+        for (int g0 = 0; g0 < G; g0 += 32) {
+#pragma unroll
+            for (int q = 0; q < 32; q++) v[q] = g0 + q < G ? __ldcg(pb + (size_t)(g0 + q) * M + r) : 0.0f;
+#pragma unroll
+            for (int q = 0; q < 32; q++)
+                if (g0 + q < G) tot = (g0 + q == 0) ? v[q] : __fadd_rn(tot, v[q]);
+        }
+        out[r] = tot;
+    }
+}
+
+// Group chains of x_proj for one 64-channel group and up to 16 streams: part[b][g][r].  Grid
+// (groups, stream tiles of 16).  The group's weights [M][64] and activations [16][64] are staged in
+// shared memory (rows padded to 68 floats), and each thread runs a 2-row x 4-stream block of chains
+// with 16-byte shared loads.  The last of a stream tile's G CTAs (a per-tile arrival counter, reset
+// by that CTA) adds each (stream, row)'s chains in group order into zp[b][r].
+__global__ void __launch_bounds__(256) k_xproj_part(int M, int K, const float* __restrict__ W, const float* act,
+                                                    int n, float* part, float* zp, uint32_t* tile_count) {
+    extern __shared__ float4 smem_f4[];
+    float* xw = reinterpret_cast<float*>(smem_f4);  // [M][68]
+    float* xc = xw + M * 68;                         // [16][68]
+    const int g = blockIdx.x, G = gridDim.x, b0 = blockIdx.y * 16, ns = min(16, n - b0);
+    const int c0 = g * kXGroup, len = min(kXGroup, K - c0);
+    const int tid = threadIdx.x;
+    // the weights are constant: staged before the dependency wait
+    for (int i = tid; i < M * 64; i += 256) {
+        const int r = i >> 6, c = i & 63;
+        xw[r * 68 + c] = c < len ? __ldg(W + (size_t)r * K + c0 + c) : 0.0f;
+    }
+    pdl_wait();
+    pdl_trigger();
+    for (int i = tid; i < 16 * 64; i += 256) {
+        const int sidx = i >> 6, c = i & 63;
+        xc[sidx * 68 + c] = (sidx < ns && c < len) ? act[(size_t)(b0 + sidx) * K + c0 + c] : 0.0f;
+    }
+    __syncthreads();
+    const int nsb = (ns + 3) >> 2, nblk = ((M + 1) >> 1) * nsb;
+    for (int t = tid; t < nblk; t += 256) {
+        const int r0 = (t / nsb) * 2, s0 = (t % nsb) * 4;
+        const float* w0 = xw + r0 * 68;
+        const float* w1 = xw + min(r0 + 1, M - 1) * 68;
+        float acc[2][4];
+#pragma unroll
+        for (int i = 0; i < 2; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+        if (len == kXGroup) {
+#pragma unroll 4
+            for (int c = 0; c < 64; c += 4) {
+                const float4 wa = *reinterpret_cast<const float4*>(w0 + c);
+                const float4 wb = *reinterpret_cast<const float4*>(w1 + c);
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const float4 xv = *reinterpret_cast<const float4*>(xc + (s0 + j) * 68 + c);
+                    acc[0][j] = __fmaf_rn(wa.x, xv.x, acc[0][j]);
+                    acc[0][j] = __fmaf_rn(wa.y, xv.y, acc[0][j]);
+                    acc[0][j] = __fmaf_rn(wa.z, xv.z, acc[0][j]);
+                    acc[0][j] = __fmaf_rn(wa.w, xv.w, acc[0][j]);
+                    acc[1][j] = __fmaf_rn(wb.x, xv.x, acc[1][j]);
+                    acc[1][j] = __fmaf_rn(wb.y, xv.y, acc[1][j]);
+                    acc[1][j] = __fmaf_rn(wb.z, xv.z, acc[1][j]);
+                    acc[1][j] = __fmaf_rn(wb.w, xv.w, acc[1][j]);
+                }
+            }
+        } else {  // a last, shorter group (F32 shapes only)
+            for (int c = 0; c < len; c++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    acc[0][j] = __fmaf_rn(w0[c], xc[(s0 + j) * 68 + c], acc[0][j]);
+                    acc[1][j] = __fmaf_rn(w1[c], xc[(s0 + j) * 68 + c], acc[1][j]);
+                }
+        }
+#pragma unroll
+        for (int i = 0; i < 2; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (r0 + i < M && s0 + j < ns) part[((size_t)(b0 + s0 + j) * G + g) * M + r0 + i] = acc[i][j];
+    }
+    __shared__ int s_last;
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        s_last = atomicAdd(&tile_count[blockIdx.y], 1u) == (uint32_t)(G - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if ((M & 3) == 0 && G <= 32) {
+        // thread = (stream, 4 consecutive rows): every group's 16 bytes requested at once
+        const int nq = M >> 2;
+        for (int o = tid; o < ns * nq; o += 256) {
+            const int sidx = o / nq, r4 = (o - sidx * nq) * 4;
+            const float4* pp = reinterpret_cast<const float4*>(part + (size_t)(b0 + sidx) * G * M + r4);
+            float4 v[32];
+#pragma unroll
+            for (int q = 0; q < 32; q++) v[q] = q < G ? __ldcg(pp + (size_t)q * nq) : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 t = v[0];
+#pragma unroll
+            for (int q = 1; q < 32; q++) {
+                if (q < G) {
+                    t.x = __fadd_rn(t.x, v[q].x);
+                    t.y = __fadd_rn(t.y, v[q].y);
+                    t.z = __fadd_rn(t.z, v[q].z);
+                    t.w = __fadd_rn(t.w, v[q].w);
+                }
+            }
+            *reinterpret_cast<float4*>(zp + (size_t)(b0 + sidx) * M + r4) = t;
+        }
+    } else {
+        for (int sidx = 0; sidx < ns; sidx++)
+            xproj_sum_groups(part + (size_t)(b0 + sidx) * G * M, G, M, zp + (size_t)(b0 + sidx) * M);
+    }
+    if (tid == 0) tile_count[blockIdx.y] = 0u;
+}
+
+// ------------------------------------------------------------------------------------------
 // Q8 GEMV on CUDA cores (dp4a).  Lane l covers 16 bytes (quarter q = l & 3) of group slot
 // gs = l >> 2; a warp covers 8 groups (512 weight bytes) per load.  The three digit sums of a
 // group are exact int32, reduced across the 4 quarter lanes with integer shuffles; the row then
@@ -674,18 +871,41 @@ struct ScanArgs {
 
 // One thread per channel (large batches: no repeated work) or four (small batches: shorter
 // dependency chains per thread).  Both evaluate the same trees in the same order.
-template <int TPC>
-__global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
-    extern __shared__ float4 smem_f4[];
-    float* zs = reinterpret_cast<float*>(smem_f4);  // [xr]
-    __shared__ float s_max[8];
+// One thread's pieces of the scan (the one-thread-per-channel form):
+//   dt_dot8_body  dt_proj over the 8-aligned body of dt_rank, lane l accumulating columns c + l,
+//                 then hsum8 ((l0+l4)+(l2+l6)) + ((l1+l5)+(l3+l7)); w(c) is column c's weight
+//   ssm_out16     hsum_ssm of s[l]*C[l] + s[l+8]*C[l+8]: ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7))
+template <class W>
+__device__ __forceinline__ float dt_dot8_body(const float* zs, int body, W w) {
+    float l[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int c = 0; c < body; c += 8) {
+#pragma unroll
+        for (int q = 0; q < 8; q++) l[q] = __fadd_rn(l[q], __fmul_rn(w(c + q), zs[c + q]));
+    }
+    return __fadd_rn(__fadd_rn(__fadd_rn(l[0], l[4]), __fadd_rn(l[2], l[6])),
+                     __fadd_rn(__fadd_rn(l[1], l[5]), __fadd_rn(l[3], l[7])));
+}
+
+__device__ __forceinline__ float ssm_out16(const float (&s)[kDState], const float* C) {
+    float ln[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) ln[q] = __fadd_rn(__fmul_rn(s[q], C[q]), __fmul_rn(s[q + 8], C[q + 8]));
+    return __fadd_rn(__fadd_rn(__fadd_rn(ln[0], ln[4]), __fadd_rn(ln[1], ln[5])),
+                     __fadd_rn(__fadd_rn(ln[2], ln[6]), __fadd_rn(ln[3], ln[7])));
+}
+
+// The work of one CTA (256 threads): stream b, channel block blk.  `fill(zs)` puts the stream's
+// x_proj output (dt_raw, B, C) into shared memory and synchronises the CTA; every operand that
+// does not depend on it is loaded first.
+template <int TPC, class Fill>
+__device__ __forceinline__ void scan_block(const ScanArgs& a, const ActOut& out, int b, int blk, float* zs,
+                                           float* s_max, Fill fill) {
     constexpr int kCh = 256 / TPC;           // channels per block
     constexpr int kSt = kDState / TPC;       // states per thread
-    const int b = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = TPC == 1 ? 0 : (lane & 3);
     const int jl = TPC == 1 ? threadIdx.x : warp * 8 + (lane >> 2);
-    const int j = blockIdx.x * kCh + jl;
+    const int j = blk * kCh + jl;
     const uint32_t slot = a.slots[b];
     const bool ok = j < a.di && slot < (uint32_t)a.cap;
     const bool fresh = a.rflag[b] != 0;
@@ -717,21 +937,10 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
 #pragma unroll
     for (int k = 0; k < kSt; k++) at[k] = __ldg(a.a_t + (size_t)(t + TPC * k) * a.di + jj);
     const float dtb = __ldg(a.dt_b + jj), dv = __ldg(a.dvec + jj);
-    pdl_wait();
-    pdl_trigger();
-    const float* zpb = a.zp + (size_t)b * a.xr;
-    for (int i = threadIdx.x; i < a.xr; i += blockDim.x) zs[i] = zpb[i];
-    __syncthreads();
+    fill(zs);
     float dt;
     if constexpr (TPC == 1) {
-        float l[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int c = 0; c < body; c += 8) {
-#pragma unroll
-            for (int q = 0; q < 8; q++) l[q] = __fadd_rn(l[q], __fmul_rn(wt[(size_t)(c + q) * a.di], zs[c + q]));
-        }
-        // hsum8: ((l0+l4)+(l2+l6)) + ((l1+l5)+(l3+l7))
-        dt = __fadd_rn(__fadd_rn(__fadd_rn(l[0], l[4]), __fadd_rn(l[2], l[6])),
-                       __fadd_rn(__fadd_rn(l[1], l[5]), __fadd_rn(l[3], l[7])));
+        dt = dt_dot8_body(zs, body, [&](int c) { return wt[(size_t)c * a.di]; });
     } else {
         // this thread holds lanes t and t+4; the quad finishes hsum8 with xor 2 then xor 1
         float la = 0.0f, lb = 0.0f;
@@ -774,11 +983,7 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
     // hsum_ssm = ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7))
     float h;
     if constexpr (TPC == 1) {
-        float ln[8];
-#pragma unroll
-        for (int q = 0; q < 8; q++) ln[q] = __fadd_rn(__fmul_rn(s[q], C[q]), __fmul_rn(s[q + 8], C[q + 8]));
-        h = __fadd_rn(__fadd_rn(__fadd_rn(ln[0], ln[4]), __fadd_rn(ln[1], ln[5])),
-                      __fadd_rn(__fadd_rn(ln[2], ln[6]), __fadd_rn(ln[3], ln[7])));
+        h = ssm_out16(s, C);
     } else {
         // states t, t+4, t+8, t+12 here: lanes t and t+4, then xor 1 and xor 2 across the quad
         const float l0 = __fadd_rn(__fmul_rn(s[0], C[t]), __fmul_rn(s[2], C[t + 8]));
@@ -809,6 +1014,21 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
     out.q[dq_off(out.cap_pad, 1, b, j)] = (int8_t)dg.d2;
     out.q[dq_off(out.cap_pad, 2, b, j)] = (int8_t)dg.d3;
     if ((j & (kGroup - 1)) == 0) out.e[(size_t)b * kEStride + j / kGroup] = gs;
+}
+
+template <int TPC>
+__global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
+    extern __shared__ float4 smem_f4[];
+    float* zs = reinterpret_cast<float*>(smem_f4);  // [xr]
+    __shared__ float s_max[8];
+    const int b = blockIdx.y;
+    scan_block<TPC>(a, out, b, blockIdx.x, zs, s_max, [&](float* z) {
+        pdl_wait();
+        pdl_trigger();
+        const float* zpb = a.zp + (size_t)b * a.xr;
+        for (int i = threadIdx.x; i < a.xr; i += blockDim.x) z[i] = zpb[i];
+        __syncthreads();
+    });
 }
 
 // Zero the conv and SSM state of the listed slots in every layer, and their reset counters.
