@@ -42,6 +42,7 @@ STREAMS = 32           # lockstep streams per GPU
 L2_BYTES = 126 * 2**20
 METRIC = "Mamba-130M decode tok/s (Q8, 32 lockstep streams per GPU)"
 SWEEP_N = (1, 128, 1024)
+FUSED_MAX_N = 32       # Q8 batches up to this size run the fused step kernel (rk_fused.cuh)
 RWKV_N = (1, 32, 256)  # configs[3] is 256 lockstep streams of uniform byte tokens
 
 
@@ -94,6 +95,9 @@ def kernel_bytes(cls: str, n: int, dims: rbin.MambaDims, profile: str) -> int:
         return n * d * 4 + d * 4 + act(d)
     if cls == "embed":
         return n * ((d + (d // 64) * 4) if q8 else d * 4) + n * d * 4
+    if cls == "step":  # the fused small-batch step: every layer's weights once, each stream's state in and out
+        w, _ = dims_bytes(dims, profile)
+        return w - mat(V, d) - d * 4 + n * 2 * dims.state_bytes()
     return 0
 
 
@@ -254,9 +258,12 @@ def run_b200(args, rank, world, local, dist):
 
     # per-kernel device times: each class's launches of one step replayed in isolation (CUDA graph,
     # L2 flushed before each replay), timed with CUDA events
-    kt = {c: b.time_kernel(c, n, reps=5) for c in ("embed", "norm", "in_proj", "x_proj", "scan", "out_proj", "head")}
+    # (batches of up to 32 streams run every layer in one persistent kernel, class "step")
+    fused = n <= FUSED_MAX_N
+    classes = ("embed", "step", "head") if fused else ("embed", "norm", "in_proj", "x_proj", "scan", "out_proj", "head")
+    kt = {c: b.time_kernel(c, n, reps=5) for c in classes}
     per_step_launches = {"embed": 1, "norm": dims.n_layer + 1, "in_proj": dims.n_layer, "x_proj": dims.n_layer,
-                         "scan": dims.n_layer, "out_proj": dims.n_layer, "head": 1}
+                         "scan": dims.n_layer, "out_proj": dims.n_layer, "head": 1, "step": 1}
 
     # e2e through the C ABI with host buffers (pinned output)
     h_out = torch.empty((n, V), dtype=torch.float32, pin_memory=True).numpy()
@@ -455,9 +462,10 @@ def run_reference(args, rank, world):
             "e2e": {"value": round(v, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
-def run_profile_case(n: int, quant: str = "q8") -> None:
+def run_profile_case(n: int, quant: str = "q8", fused: int = 1) -> None:
     """Small case for ncu captures: two eager (graph-free) steps of n streams through the C ABI.
-    quant "rwkv7" runs the RWKV-7 0.1B W8A8 model instead of Mamba-130M."""
+    quant "rwkv7" runs the RWKV-7 0.1B W8A8 model instead of Mamba-130M; fused 0 runs the Mamba
+    per-kernel step even where the fused step kernel would (Q8, n <= 32)."""
     from redukt_b200.plugin import PluginBackend
     if quant == "rwkv7":
         cache = os.environ.get("REDUKT_B200_MODEL_CACHE", os.path.join(tempfile.gettempdir(), "redukt_b200_models"))
@@ -474,6 +482,7 @@ def run_profile_case(n: int, quant: str = "q8") -> None:
     f32_path, q8_path = model_paths(0, 1, lambda: None)
     b = PluginBackend(q8_path if quant == "q8" else f32_path)
     b.set_option("graphs", 0)
+    b.set_option("fused", fused)
     b.batch_init(n)
     toks = zipf_tokens(n, 2, vocab=b.vocab_size)
     for t in range(2):
@@ -495,9 +504,11 @@ def main():
     ap.add_argument("--profile-case", type=int, default=0,
                     help="run two eager steps of N streams and exit (small case for ncu captures)")
     ap.add_argument("--profile-quant", default="q8", choices=["q8", "f32", "rwkv7"])
+    ap.add_argument("--profile-fused", type=int, default=1, choices=[0, 1],
+                    help="0: the per-kernel Mamba step even at n <= 32")
     args = ap.parse_args()
     if args.profile_case:
-        run_profile_case(args.profile_case, args.profile_quant)
+        run_profile_case(args.profile_case, args.profile_quant, args.profile_fused)
         return
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -142,16 +142,18 @@ int32_t redukt_b200_set_option(const char* key, int64_t value);
 
 /* Per-kernel-class device time: returns the CUDA-event time (ms) and launch count accumulated per
  * class since the previous call (0 embed, 1 norm, 2 in_proj, 3 x_proj, 4 scan, 5 out_proj, 6 head,
- * 7 softmax), then turns event bracketing on (enable != 0) or off.  While on, steps run without
- * CUDA graphs so each launch can be bracketed.  Synchronises the device.  RWKV-7 classes: 1 the
+ * 7 softmax, 8 the fused small-batch step), then turns event bracketing on (enable != 0) or off.  While on, steps run without
+ * CUDA graphs so each launch can be bracketed, and the per-kernel step replaces the fused one (class 8
+ * stays 0).  Synchronises the device.  RWKV-7 classes: 1 the
  * LayerNorm/shift/quantise kernels, 2 the r/k/v projections, 3 the LoRA down-projections, 4 the WKV
  * head update and its quantisation, 5 the output and FFN projections, 6 head, 7 softmax. */
 int32_t redukt_b200_kernel_times(int32_t enable, double* ms, uint32_t* launches, uint32_t n_classes);
 
 /* Device time of one kernel class in isolation, in ms per launch: the class's launches of one
  * step for n streams (every layer; the embedding and head once) replayed as a CUDA graph after an
- * L2 flush, `reps` times.  cls as in redukt_b200_kernel_times (0-6).  Needs a batch pool of at least
- * n slots and overwrites its scratch and the state of slots 0..n-1.  Mamba only. */
+ * L2 flush, `reps` times.  cls as in redukt_b200_kernel_times (0-6, or 8: the fused step kernel, all
+ * layers and the final norm in one launch, when it runs for n streams).  Needs a batch pool of at
+ * least n slots and overwrites its scratch and the state of slots 0..n-1.  Mamba only. */
 int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* ms_per_launch);
 
 /* Softmax of n_rows rows of vocab logits, device memory in and out, with no allocation.

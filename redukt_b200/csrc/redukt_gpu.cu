@@ -694,7 +694,7 @@ __global__ void k_softmax_final(const float* __restrict__ logits, int V, const f
 }
 
 // Kernel classes for the optional per-launch CUDA-event timing (redukt_b200_kernel_times).
-enum KClass { kKEmbed = 0, kKNorm, kKInProj, kKXProj, kKScan, kKOutProj, kKHead, kKSoftmax, kKClasses };
+enum KClass { kKEmbed = 0, kKNorm, kKInProj, kKXProj, kKScan, kKOutProj, kKHead, kKSoftmax, kKStep, kKClasses };
 
 struct KTiming {
     bool on = false;
@@ -1282,7 +1282,12 @@ int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* m
         set_err("time_kernel: per-class timing is implemented for the Mamba engine only");
         return BACKEND_INVALID_ARGUMENT;
     }
-    if (n == 0 || n > G.batch.cap || !ms_per_launch || cls < 0 || cls >= (int)kKSoftmax) return BACKEND_INVALID_ARGUMENT;
+    if (n == 0 || n > G.batch.cap || !ms_per_launch || cls < 0 || cls >= (int)kKClasses || cls == (int)kKSoftmax)
+        return BACKEND_INVALID_ARGUMENT;
+    if (cls == (int)kKStep && !use_fused((int)n)) {
+        set_err("time_kernel: the fused step does not run for %u streams with the current options", n);
+        return BACKEND_INVALID_ARGUMENT;
+    }
     Pool& p = G.batch;
     std::vector<uint32_t> idx(n);
     for (uint32_t i = 0; i < n; i++) idx[i] = i;
@@ -1304,6 +1309,10 @@ int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* m
             launches = 1;
         } else if (cls == kKHead) {
             project(G.head, p, nn, EpiStore{p.logits, G.V}, st);
+            launches = 1;
+        } else if (cls == kKStep) {  // every layer + the final norm in the fused kernel
+            cudaMemsetAsync(p.bar, 0, sizeof(uint32_t), st);
+            launch_fused(p, nn, p.d_slots, st);
             launches = 1;
         } else {
             for (int li = 0; li < G.nl; li++) {

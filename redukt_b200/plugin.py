@@ -35,7 +35,7 @@ EXT_SYMBOLS = ("redukt_backend_set_reset_every", "redukt_backend_forward_batch_p
                "redukt_b200_get_q8", "redukt_b200_info", "redukt_b200_set_option", "redukt_b200_kernel_times",
                "redukt_b200_time_kernel", "redukt_b200_softmax_noalloc", "redukt_b200_rwkv_get_state",
                "redukt_b200_last_error")
-KERNEL_CLASSES = ("embed", "norm", "in_proj", "x_proj", "scan", "out_proj", "head", "softmax")
+KERNEL_CLASSES = ("embed", "norm", "in_proj", "x_proj", "scan", "out_proj", "head", "softmax", "step")
 
 
 class BackendResult(enum.IntEnum):
