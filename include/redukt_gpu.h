@@ -135,8 +135,13 @@ int32_t redukt_b200_rwkv_get_state(uint32_t slot, float* x_att, float* wkv, floa
 int32_t redukt_b200_info(uint32_t* out, uint32_t n);
 
 /* Engine switches for tests and benchmarks:
- *   "proj_path"  0 = automatic, 1 = CUDA-core projections, 2 = tensor-core projections
- *   "graphs"     0/1 = replay each batch size's launch sequence from a captured CUDA graph
+ *   "proj_path"    0 = automatic, 1 = CUDA-core projections, 2 = tensor-core projections
+ *   "graphs"       0/1 = replay each batch size's launch sequence from a captured CUDA graph
+ *   "pdl"          0/1 = programmatic dependent launch between the step's kernels
+ *   "split_target" CTAs a split-K tensor-core launch may use (0 = never split)
+ *   "fused"        0/1 = run Q8 batches of up to 32 streams as one persistent step kernel
+ *                  (only with proj_path 0; same bits as the per-kernel step)
+ *   "fused_ctas"   1-4 = CTAs per SM the fused step may use (capped by occupancy)
  * Returns INVALID_ARGUMENT for an unknown key or value. */
 int32_t redukt_b200_set_option(const char* key, int64_t value);
 
