@@ -27,8 +27,11 @@ __device__ __forceinline__ float cephes_exp_core(float x) {
     const float P0 = 1.9875691500E-4f, P1 = 1.3981999507E-3f, P2 = 8.3334519073E-3f;
     const float P3 = 4.1665795894E-2f, P4 = 1.6666665459E-1f, P5 = 5.0000001201E-1f;
     float fx = __fmul_rn(x, LOG2E);
-    float nf = rintf(fx);  // round half to even, as the reference's 2^23 magic-constant trick
-    int n = __float2int_rz(nf);
+    // round half to even with the reference's 2^23 magic-constant trick (|fx| < 2^22 here); the
+    // integer comes from the same sum's bits, so no float-to-int conversion unit is involved
+    const float big = __fadd_rn(fx, 12582912.0f);
+    float nf = __fsub_rn(big, 12582912.0f);
+    int n = __float_as_int(big) - 0x4B400000;
     float r = __fsub_rn(__fsub_rn(x, __fmul_rn(nf, LN2_HI)), __fmul_rn(nf, LN2_LO));
     float r2 = __fmul_rn(r, r);
     float y = P0;
@@ -149,14 +152,23 @@ __device__ __forceinline__ float group_scale(float m, float* inv) {
     return __uint_as_float((unsigned)(127 + e) << 23);
 }
 
+// round(t) to nearest-even for |t| < 2^22, as a float and as an int: t + 1.5 * 2^23 lands where the
+// spacing is 1, so the sum is already rounded and its low mantissa bits are the integer.
+__device__ __forceinline__ float round_even_small(float t, int* i) {
+    const float big = __fadd_rn(t, 12582912.0f);
+    *i = __float_as_int(big) - 0x4B400000;
+    return __fsub_rn(big, 12582912.0f);
+}
+
 __device__ __forceinline__ Digits3 split_digits(float x, float inv) {
-    float t = __fmul_rn(x, inv);  // exact: power-of-two scaling
-    float d1 = rintf(t);
+    float t = __fmul_rn(x, inv);  // exact: power-of-two scaling, |t| < 64
+    Digits3 r;
+    float d1 = round_even_small(t, &r.d1);
     float t2 = __fmul_rn(__fsub_rn(t, d1), 128.0f);  // both exact
-    float d2 = rintf(t2);
+    float d2 = round_even_small(t2, &r.d2);
     float t3 = __fmul_rn(__fsub_rn(t2, d2), 128.0f);
-    float d3 = rintf(t3);
-    return {(int)d1, (int)d2, (int)d3};
+    round_even_small(t3, &r.d3);
+    return r;
 }
 
 // Exact int -> float for |a| < 2^22 without the conversion unit: the bits 0x4B400000 + a are
