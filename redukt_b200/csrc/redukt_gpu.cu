@@ -780,7 +780,12 @@ void launch_fused(Pool& p, int n, const uint32_t* d_slots, cudaStream_t st) {
     fa.mpad_out = round_up(G.d, 128);
     const int grid = G.num_sms * std::max(1, std::min(G.fused_ctas_per_sm, 1));
     const int nmb = G.di / 64, nt = (n + 7) / 8;
-    fa.sga = 2 * nmb * nt <= grid ? 8 : 16;
+    // phase A: x-half jobs (conv and x_proj work) take 8 streams while they fit; z-half jobs grow
+    // to 16 streams first
+    fa.sga = 8;
+    fa.sgz = 8;
+    if (2 * nmb * nt > grid) fa.sgz = 16;
+    if (nmb * (nt + (n + 15) / 16) > grid) fa.sga = 16;
     fa.sgb = nmb * ((n + 3) / 4) <= grid ? 4 : 8;
     fa.mc = (G.d / 16) * nt <= grid ? 16 : 32;
     fa.pitch_a = G.d + 16;

@@ -69,7 +69,7 @@ struct FusedArgs {
     int n, cap, cap_pad, d, di, dr, xr, nl;
     int g_in, s_in, mpad_in;     // in_proj: groups, accumulation splits, padded rows
     int g_out, s_out, mpad_out;  // out_proj
-    int sga, sgb, mc;            // streams per A job, streams per B job, rows per C job
+    int sga, sgz, sgb, mc;       // streams per A job (x half, z half: 8 or 16), per B job, rows per C job
     int pitch_a;                 // bytes per digit-plane row of phase A's planes (d + 16)
     FusedLayout lay;
     const uint32_t* slots;
@@ -111,13 +111,14 @@ inline FusedLayout fused_layout(const FusedArgs& a) {
     L.c_ws = o; o += align16(a.mc * a.g_out * 4);
     const int pc = o;
     const int big = align16(pa > pb ? (pa > pc ? pa : pc) : (pb > pc ? pb : pc));
+    const int sg = a.sga > a.sgz ? a.sga : a.sgz;
     const int sa = align16(a.sga * 3 * 64 * 4), sb = align16(a.sgb * 16 * 64 * 4), sc = align16(8 * a.mc * 4);
     L.a_conv = L.b_ssm = L.c_x = big;
     o = big + (sa > sb ? (sa > sc ? sa : sc) : (sb > sc ? sb : sc));
-    const int ta = a.sga / 8, tc = a.mc / 16;
-    const int bq_a = 3 * a.sga * a.pitch_a, bq_c = a.g_out * 3 * 8 * 64;
+    const int ta = sg / 8, tc = a.mc / 16;
+    const int bq_a = 3 * sg * a.pitch_a, bq_c = a.g_out * 3 * 8 * 64;
     L.bq = o;   o += align16(bq_a > bq_c ? bq_a : bq_c);
-    L.ae = o;   o += align16((a.sga > 8 ? a.sga : 8) * kEStride * 4);
+    L.ae = o;   o += align16(sg * kEStride * 4);
     const int pa_n = ta * 4 * a.s_in, pc_n = tc * a.s_out;
     L.part = o; o += align16((pa_n > pc_n ? pa_n : pc_n) * 128 * 4);
     L.xc = o;   o += align16(a.sga * 68 * 4);
@@ -347,13 +348,18 @@ __device__ __forceinline__ uint32_t live_slot(const FusedArgs& a, const StepMeta
 // ---- job decompositions and prefetches ------------------------------------------------------
 
 struct JobA {
-    int h, mb, g0;  // half (0 = x, 1 = z), 64-row block, first stream
+    int h, mb, g0, sg;  // half (0 = x, 1 = z), 64-row block, first stream, streams per job of this half
 };
+// x-half jobs first (a.sga streams each), then z-half jobs (a.sgz streams each)
 __device__ __forceinline__ JobA job_a(const FusedArgs& a, int job) {
-    const int nsg = (a.n + a.sga - 1) / a.sga, nmb = a.di / 64;
-    return {job / (nsg * nmb), (job / nsg) % nmb, (job % nsg) * a.sga};
+    const int nmb = a.di / 64, nx = (a.n + a.sga - 1) / a.sga, nz = (a.n + a.sgz - 1) / a.sgz;
+    if (job < nmb * nx) return {0, job / nx, (job % nx) * a.sga, a.sga};
+    job -= nmb * nx;
+    return {1, job / nz, (job % nz) * a.sgz, a.sgz};
 }
-__device__ __forceinline__ int jobs_a(const FusedArgs& a) { return 2 * (a.di / 64) * ((a.n + a.sga - 1) / a.sga); }
+__device__ __forceinline__ int jobs_a(const FusedArgs& a) {
+    return (a.di / 64) * ((a.n + a.sga - 1) / a.sga + (a.n + a.sgz - 1) / a.sgz);
+}
 
 struct JobB {
     int g, b0;  // 64-channel group, first stream
@@ -392,7 +398,7 @@ __device__ __forceinline__ void prefetch_a(const FusedArgs& a, const StepMeta& m
     cb.issued();
     const JobA jb = job_a(a, job);
     const int row0 = jb.h * a.di + jb.mb * 64, c0 = jb.mb * 64;
-    const int ns = min(a.sga, a.n - jb.g0);
+    const int ns = min(jb.sg, a.n - jb.g0);
     const bool xh = jb.h == 0;
     const int nb = L.norm_b ? 1 : 0;
     const int count = a.g_in + 2 + nb + (xh ? 2 : 0);
@@ -476,7 +482,7 @@ __device__ __forceinline__ bool run_a(const FusedArgs& a, const StepMeta& m, con
                                       char* sm, CopyBatch& pf, int* s_ok) {
     const JobA jb = job_a(a, job);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-    const int ns = min(a.sga, a.n - jb.g0);
+    const int ns = min(jb.sg, a.n - jb.g0);
     const int pitch = a.pitch_a, tile_bytes = 24 * pitch;
     int8_t* bq = reinterpret_cast<int8_t*>(sm + a.lay.bq);
     float* ae = reinterpret_cast<float*>(sm + a.lay.ae);
@@ -503,7 +509,7 @@ __device__ __forceinline__ bool run_a(const FusedArgs& a, const StepMeta& m, con
 #pragma unroll
         for (int u = 0; u < 2; u++) {
             const int s = warp + 8 * u;
-            if (s >= a.sga) break;
+            if (s >= jb.sg) break;
             int8_t* rows = bq + (s >> 3) * tile_bytes + (s & 7) * pitch;  // plane p at + p * 8 * pitch
             if (s < ns) {
                 float4 (&v)[NC] = v2[u];
