@@ -142,6 +142,8 @@ int32_t redukt_b200_info(uint32_t* out, uint32_t n);
  *   "fused"        0/1 = run Q8 batches of up to 32 streams as one persistent step kernel
  *                  (only with proj_path 0; same bits as the per-kernel step)
  *   "fused_ctas"   1-4 = CTAs per SM the fused step may use (capped by occupancy)
+ *   "head_ctas"    1 or 2 = tensor-core head tiles per SM at up to 64 streams (2: a 6-stage pipeline
+ *                  so two CTAs share an SM; 1: the 12-stage tile of the other projections)
  * Returns INVALID_ARGUMENT for an unknown key or value. */
 int32_t redukt_b200_set_option(const char* key, int64_t value);
 

@@ -138,6 +138,7 @@ struct Model {
     bool fused = true;          // option "fused"
     int fused_nc = 0;           // norm chunks of the instantiated kernel, 0 = shape not supported
     int fused_ctas_per_sm = 2;  // option "fused_ctas"
+    int head_ctas = 2;          // option "head_ctas": 2 = the two-CTAs-per-SM head tiles at small batch
     int num_sms = 0;
     FusedLayer* d_fused = nullptr;  // [nl] device copy of the layer pointers
 };
@@ -595,16 +596,16 @@ int split_for(int tiles, int rows, int groups, int n, size_t part_cap) {
     return 1;
 }
 
-template <int BN, class Epi>
+template <int BN, class Epi, int ST = tc::stages_for<BN>(), int MB = 1>
 void project_tc_bn(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st) {
-    auto k = tc::k_proj_q8_tc<BN, Epi>;
-    size_t smem = tc::launch_smem<BN>();
+    auto k = tc::k_proj_q8_tc<BN, Epi, ST, MB>;
+    size_t smem = tc::launch_smem<BN, ST>();
     allow_smem(k, smem);
     const int gx = (n + BN - 1) / BN, gy = (m.rows + tc::kBM - 1) / tc::kBM;
     tc::SplitK sk{1, p.part, p.counter};
     if (BN == 16 && p.part) sk.splits = split_for(gx * gy, m.rows, m.cols / kGroup, n, p.part_cap);
     dim3 grid(gx, gy, sk.splits);
-    launch(k, grid, dim3(tc::TileCfg<BN>::kThreads), smem, st, (const int8_t*)m.q, (const int8_t*)p.act_q, m.rows, m.cols,
+    launch(k, grid, dim3(tc::TileCfg<BN, ST, MB>::kThreads), smem, st, (const int8_t*)m.q, (const int8_t*)p.act_q, m.rows, m.cols,
            p.cap_pad, n, (const float*)m.s, (const float*)p.act_e, G.d_err, epi, sk);
 }
 
@@ -620,6 +621,15 @@ void project(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st) {
     } else {
         gemv_q8(m, p.act_q, p.act_e, p.cap_pad, n, epi, st);
     }
+}
+
+// The LM head: hundreds of row tiles, so at small batch a shallower pipeline (6 stages) that lets
+// two CTAs share an SM (TMEM: 2 x 256 columns) keeps more tiles in flight than one deep CTA.
+void project_head(const Pool& p, int n, float* out, cudaStream_t st) {
+    if (G.profile != kF32 && use_tc(n) && n <= 64 && G.head_ctas == 2)
+        project_tc_bn<16, EpiStore, 6, 2>(G.head, p, n, EpiStore{out, G.V}, st);
+    else
+        project(G.head, p, n, EpiStore{out, G.V}, st);
 }
 
 // Four threads per channel while the batch is small (latency), one when it is large (no repeated
@@ -870,7 +880,7 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
     float* lo = probs ? p.logits : d_out;
     {
         KScope k(kKHead, st);
-        project(G.head, p, n, EpiStore{lo, G.V}, st);
+        project_head(p, n, lo, st);
     }
     launches += 1;
     if (probs) {
@@ -1313,7 +1323,7 @@ int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* m
                    (const float*)G.emb.s, G.d, G.V, p.x);
             launches = 1;
         } else if (cls == kKHead) {
-            project(G.head, p, nn, EpiStore{p.logits, G.V}, st);
+            project_head(p, nn, p.logits, st);
             launches = 1;
         } else if (cls == kKStep) {  // every layer + the final norm in the fused kernel
             cudaMemsetAsync(p.bar, 0, sizeof(uint32_t), st);
@@ -1417,8 +1427,12 @@ int32_t redukt_b200_set_option(const char* key, int64_t value) {
         clear_dev_graphs();
         return BACKEND_OK;
     }
-    if (!strcmp(key, "fused") || !strcmp(key, "fused_ctas")) {
+    if (!strcmp(key, "fused") || !strcmp(key, "fused_ctas") || !strcmp(key, "head_ctas")) {
         if (!strcmp(key, "fused")) G.fused = value != 0;
+        else if (!strcmp(key, "head_ctas")) {
+            if (value < 1 || value > 2) return BACKEND_INVALID_ARGUMENT;
+            G.head_ctas = (int)value;
+        }
         else if (value < 1 || value > 4) return BACKEND_INVALID_ARGUMENT;
         else G.fused_ctas_per_sm = (int)value;
         for (Pool* p : {&G.v1, &G.batch}) {  // captured graphs hold the old launch sequence

@@ -33,7 +33,7 @@ constexpr int kAutoMinStreams = 1;   // the tensor-core kernel serves every batc
 // clock is lower): far beyond any legitimate wait.  clock64 is a cheap per-SM counter.
 constexpr long long kWaitLimitCycles = 4000000000ll;
 
-template <int BN>
+template <int BN, int ST = stages_for<BN>(), int MB = 1>
 struct TileCfg {
     static constexpr int kBufs = BN == 16 ? 4 : 2;          // TMEM accumulator sets in flight
     static constexpr int kColsUsed = kBufs * 3 * BN;
@@ -41,20 +41,20 @@ struct TileCfg {
     static constexpr int kEG = 2;                            // epilogue warpgroups (each owns BN/2 streams)
     static constexpr int kSPT = BN / kEG;                    // streams per epilogue thread
     static constexpr int kThreads = 64 + 128 * kEG;          // producer + MMA warp + epilogue
-    static constexpr int kMinBlocks = 1;                     // CTAs per SM the registers must allow (shared memory allows one)
+    static constexpr int kMinBlocks = MB;                    // CTAs per SM the registers must allow
 };
 
-template <int BN>
+template <int BN, int ST = stages_for<BN>()>
 struct alignas(1024) Smem {
-    static constexpr int kStages = stages_for<BN>();
+    static constexpr int kStages = ST;
     int8_t a[kStages][kBM * kBK];         // 8 KB per stage, 1024-aligned (64B-swizzle atoms)
     int8_t b[kStages][3 * BN * kBK];      // digit planes: [16-stream block][plane][16 rows][64 B]
     uint64_t full[kStages];
     uint64_t empty[kStages];
     uint32_t slot[BN];                    // stream metadata of the tile (in_proj epilogue)
     uint32_t fresh[BN];
-    uint64_t tfull[TileCfg<BN>::kBufs];
-    uint64_t tempty[TileCfg<BN>::kBufs];
+    uint64_t tfull[TileCfg<BN, ST>::kBufs];
+    uint64_t tempty[TileCfg<BN, ST>::kBufs];
     uint64_t gather;                      // split-K: the last CTA's copy of the tile's partial sums
     int last;                             // split-K: this CTA combines the tile
     uint32_t tmem_base;
@@ -185,14 +185,14 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 
 template <int BN>
 __host__ __device__ constexpr uint32_t tmem_cols() {
-    return TileCfg<BN>::kCols;
+    return TileCfg<BN>::kCols;  // the same for every stage count
 }
 
 // Dynamic shared memory for a launch: enough for the tile, and enough that no more CTAs become
 // resident on one SM than its 512 TMEM columns can serve at once (at most 227 KB).
-template <int BN>
+template <int BN, int ST = stages_for<BN>()>
 constexpr size_t launch_smem() {
-    constexpr size_t need = sizeof(Smem<BN>) + 1024;
+    constexpr size_t need = sizeof(Smem<BN, ST>) + 1024;
     constexpr size_t per_sm = 512 / tmem_cols<BN>();
     constexpr size_t floor_bytes = (size_t)233472 / (per_sm + 1) + 1024;
     constexpr size_t want = need > floor_bytes ? need : floor_bytes;
@@ -213,18 +213,18 @@ struct SplitK {
 };
 
 // One (128-row, BN-stream) output tile over all K groups (or one split) of one Q8 projection.
-template <int BN, class Epi>
-__global__ void __launch_bounds__(TileCfg<BN>::kThreads, TileCfg<BN>::kMinBlocks)
+template <int BN, class Epi, int ST = stages_for<BN>(), int MB = 1>
+__global__ void __launch_bounds__(TileCfg<BN, ST, MB>::kThreads, TileCfg<BN, ST, MB>::kMinBlocks)
 k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M, int K, int cap_pad, int n,
              const float* __restrict__ w_scale, const float* __restrict__ act_e, uint32_t* err, Epi epi, SplitK sk) {
     extern __shared__ uint8_t smem_raw[];
-    Smem<BN>& S = *reinterpret_cast<Smem<BN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    constexpr int kBufs = TileCfg<BN>::kBufs;
-    constexpr int kEG = TileCfg<BN>::kEG;
-    constexpr int kSPT = TileCfg<BN>::kSPT;
-    constexpr int kThreads = TileCfg<BN>::kThreads;
-    constexpr int kStages = Smem<BN>::kStages;
-    constexpr uint32_t kCols = TileCfg<BN>::kCols;
+    Smem<BN, ST>& S = *reinterpret_cast<Smem<BN, ST>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int kBufs = TileCfg<BN, ST, MB>::kBufs;
+    constexpr int kEG = TileCfg<BN, ST, MB>::kEG;
+    constexpr int kSPT = TileCfg<BN, ST, MB>::kSPT;
+    constexpr int kThreads = TileCfg<BN, ST, MB>::kThreads;
+    constexpr int kStages = Smem<BN, ST>::kStages;
+    constexpr uint32_t kCols = TileCfg<BN, ST, MB>::kCols;
     constexpr uint32_t kStageBytes = kBM * kBK + 3 * BN * kBK;
     const int G = K / kBK;                          // groups of a row
     const int NS = q8_splits(G);                     // splits of the accumulation order
@@ -478,7 +478,7 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
         }
         bool emit = true;
         if constexpr (BN == 16) {
-            static_assert(sizeof(Smem<BN>::a) + sizeof(Smem<BN>::b) >= (size_t)kMaxGatherSplits * kBM * BN * sizeof(float),
+            static_assert(sizeof(Smem<BN, ST>::a) + sizeof(Smem<BN, ST>::b) >= (size_t)kMaxGatherSplits * kBM * BN * sizeof(float),
                           "the stage buffers hold the gathered sums of kMaxGatherSplits splits");
             if (split) {
                 // this CTA's split sums are published (split_end); the tile's last CTA adds all
