@@ -794,8 +794,10 @@ void launch_fused(Pool& p, int n, const uint32_t* d_slots, cudaStream_t st) {
     // to 16 streams first
     fa.sga = 8;
     fa.sgz = 8;
-    if (2 * nmb * nt > grid) fa.sgz = 16;
-    if (nmb * (nt + (n + 15) / 16) > grid) fa.sga = 16;
+    fa.rz = 64;
+    if (2 * nmb * nt > grid && G.di % 128 == 0) fa.rz = 128;  // z half: 128 rows x 8 streams
+    if (nmb * nt + (G.di / fa.rz) * nt > grid) fa.sgz = 16;
+    if (nmb * nt + (G.di / fa.rz) * ((n + fa.sgz - 1) / fa.sgz) > grid) fa.sga = 16;
     fa.sgb = nmb * ((n + 3) / 4) <= grid ? 4 : 8;
     fa.mc = (G.d / 16) * nt <= grid ? 16 : 32;
     fa.pitch_a = G.d + 16;

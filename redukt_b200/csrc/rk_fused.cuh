@@ -70,6 +70,7 @@ struct FusedArgs {
     int g_in, s_in, mpad_in;     // in_proj: groups, accumulation splits, padded rows
     int g_out, s_out, mpad_out;  // out_proj
     int sga, sgz, sgb, mc;       // streams per A job (x half, z half: 8 or 16), per B job, rows per C job
+    int rz;                      // rows per z-half A job (64 or 128; x-half jobs are 64 rows)
     int pitch_a;                 // bytes per digit-plane row of phase A's planes (d + 16)
     FusedLayout lay;
     const uint32_t* slots;
@@ -97,8 +98,9 @@ inline FusedLayout fused_layout(const FusedArgs& a) {
     // byte is written by one proxy after the other and no proxy fence is needed between phases.
     FusedLayout L{};
     int o = 0;
-    L.a_w = o;    o += align16(64 * a.d);
-    L.a_ws = o;   o += align16(64 * a.g_in * 4);
+    const int ra = a.rz > 64 ? a.rz : 64;
+    L.a_w = o;    o += align16(ra * a.d);
+    L.a_ws = o;   o += align16(ra * a.g_in * 4);
     L.a_nw = o;   o += align16(2 * a.d * 4);
     L.a_xw = o;   o += align16(a.xr * 68 * 4);
     L.a_ct = o;   o += align16(5 * 64 * 4);
@@ -119,7 +121,7 @@ inline FusedLayout fused_layout(const FusedArgs& a) {
     const int bq_a = 3 * sg * a.pitch_a, bq_c = a.g_out * 3 * 8 * 64;
     L.bq = o;   o += align16(bq_a > bq_c ? bq_a : bq_c);
     L.ae = o;   o += align16(sg * kEStride * 4);
-    const int pa_n = ta * 4 * a.s_in, pc_n = tc * a.s_out;
+    const int pa_n = (ta * 4 > a.rz / 16 ? ta * 4 : a.rz / 16) * a.s_in, pc_n = tc * a.s_out;
     L.part = o; o += align16((pa_n > pc_n ? pa_n : pc_n) * 128 * 4);
     L.xc = o;   o += align16(a.sga * 68 * 4);
     L.zs = o;   o += align16(a.sgb * a.xr * 4);
@@ -348,17 +350,17 @@ __device__ __forceinline__ uint32_t live_slot(const FusedArgs& a, const StepMeta
 // ---- job decompositions and prefetches ------------------------------------------------------
 
 struct JobA {
-    int h, mb, g0, sg;  // half (0 = x, 1 = z), 64-row block, first stream, streams per job of this half
+    int h, r0, rows, g0, sg;  // half (0 = x, 1 = z), first row within the half, rows, first stream, streams
 };
-// x-half jobs first (a.sga streams each), then z-half jobs (a.sgz streams each)
+// x-half jobs first (64 rows x a.sga streams), then z-half jobs (a.rz rows x a.sgz streams)
 __device__ __forceinline__ JobA job_a(const FusedArgs& a, int job) {
     const int nmb = a.di / 64, nx = (a.n + a.sga - 1) / a.sga, nz = (a.n + a.sgz - 1) / a.sgz;
-    if (job < nmb * nx) return {0, job / nx, (job % nx) * a.sga, a.sga};
+    if (job < nmb * nx) return {0, (job / nx) * 64, 64, (job % nx) * a.sga, a.sga};
     job -= nmb * nx;
-    return {1, job / nz, (job % nz) * a.sgz, a.sgz};
+    return {1, (job / nz) * a.rz, a.rz, (job % nz) * a.sgz, a.sgz};
 }
 __device__ __forceinline__ int jobs_a(const FusedArgs& a) {
-    return (a.di / 64) * ((a.n + a.sga - 1) / a.sga + (a.n + a.sgz - 1) / a.sgz);
+    return (a.di / 64) * ((a.n + a.sga - 1) / a.sga) + (a.di / a.rz) * ((a.n + a.sgz - 1) / a.sgz);
 }
 
 struct JobB {
@@ -397,12 +399,13 @@ __device__ __forceinline__ void prefetch_a(const FusedArgs& a, const StepMeta& m
     uint64_t* bar = cb.bar;
     cb.issued();
     const JobA jb = job_a(a, job);
-    const int row0 = jb.h * a.di + jb.mb * 64, c0 = jb.mb * 64;
+    const int row0 = jb.h * a.di + jb.r0, c0 = jb.r0, mb = jb.r0 / 64;
     const int ns = min(jb.sg, a.n - jb.g0);
     const bool xh = jb.h == 0;
     const int nb = L.norm_b ? 1 : 0;
     const int count = a.g_in + 2 + nb + (xh ? 2 : 0);
-    const uint32_t bytes = a.g_in * 4096 + 64 * a.g_in * 4 + a.d * 4 * (1 + nb) + (xh ? a.xr * 68 * 4 + 5 * 64 * 4 : 0);
+    const uint32_t bytes =
+        a.g_in * jb.rows * 64 + jb.rows * a.g_in * 4 + a.d * 4 * (1 + nb) + (xh ? a.xr * 68 * 4 + 5 * 64 * 4 : 0);
     if (xh) {  // conv state: 256-byte pieces, as 16-byte copies spread over the CTA
         float* cv = reinterpret_cast<float*>(P + a.lay.a_conv);
         for (int i = threadIdx.x; i < ns * 3 * 16; i += kFusedThreads) {
@@ -414,17 +417,18 @@ __device__ __forceinline__ void prefetch_a(const FusedArgs& a, const StepMeta& m
     cp_async_commit();
     issue_copies(bar, bytes, count, [&](int k) {
         if (k < a.g_in) {
-            tc::bulk_load(P + a.lay.a_w + k * 4096, L.in_q + ((size_t)k * a.mpad_in + row0) * 64, 4096, bar);
+            tc::bulk_load(P + a.lay.a_w + k * jb.rows * 64, L.in_q + ((size_t)k * a.mpad_in + row0) * 64, jb.rows * 64,
+                          bar);
         } else if (k == a.g_in) {
-            tc::bulk_load(P + a.lay.a_ws, L.in_s + (size_t)row0 * a.g_in, 64 * a.g_in * 4, bar);
+            tc::bulk_load(P + a.lay.a_ws, L.in_s + (size_t)row0 * a.g_in, jb.rows * a.g_in * 4, bar);
         } else if (k == a.g_in + 1) {
             tc::bulk_load(P + a.lay.a_nw, L.norm_w, a.d * 4, bar);
         } else if (nb && k == a.g_in + 2) {
             tc::bulk_load(P + a.lay.a_nw + a.d * 4, L.norm_b, a.d * 4, bar);
         } else {
             const int q = k - (a.g_in + 2 + nb);
-            if (q == 0) tc::bulk_load(P + a.lay.a_xw, L.xw_blk + (size_t)jb.mb * a.xr * 68, a.xr * 68 * 4, bar);
-            else tc::bulk_load(P + a.lay.a_ct, L.ct_blk + (size_t)jb.mb * 5 * 64, 5 * 64 * 4, bar);
+            if (q == 0) tc::bulk_load(P + a.lay.a_xw, L.xw_blk + (size_t)mb * a.xr * 68, a.xr * 68 * 4, bar);
+            else tc::bulk_load(P + a.lay.a_ct, L.ct_blk + (size_t)mb * 5 * 64, 5 * 64 * 4, bar);
         }
     });
 }
@@ -529,13 +533,14 @@ __device__ __forceinline__ bool run_a(const FusedArgs& a, const StepMeta& m, con
         }
     }
     __syncthreads();
-    const int ntask = ((ns + 7) >> 3) * 4 * a.s_in;
+    const int nmt = jb.rows >> 4;  // 16-row tiles of the job
+    const int ntask = ((ns + 7) >> 3) * nmt * a.s_in;
     const int gid = lane >> 2, tig = lane & 3;
     for (int task = warp; task < ntask; task += 8) {
-        const int t = task / (4 * a.s_in), rem = task - t * 4 * a.s_in, mt = rem / a.s_in, sp = rem - mt * a.s_in;
+        const int t = task / (nmt * a.s_in), rem = task - t * nmt * a.s_in, mt = rem / a.s_in, sp = rem - mt * a.s_in;
         const int8_t* bt = bq + t * tile_bytes + gid * pitch + tig * 4;
         float acc[4];
-        q8_tile16_split(reinterpret_cast<const int8_t*>(sm + a.lay.a_w), 64, mt * 16,
+        q8_tile16_split(reinterpret_cast<const int8_t*>(sm + a.lay.a_w), jb.rows, mt * 16,
                         reinterpret_cast<const float*>(sm + a.lay.a_ws), a.g_in, a.g_in * sp / a.s_in,
                         a.g_in * (sp + 1) / a.s_in,
                         [&](int p, int g, int c) {
@@ -547,11 +552,12 @@ __device__ __forceinline__ bool run_a(const FusedArgs& a, const StepMeta& m, con
     __syncthreads();
     const float* cv = reinterpret_cast<const float*>(sm + a.lay.a_conv);
     const float* ct = reinterpret_cast<const float*>(sm + a.lay.a_ct);
-    for (int o = tid; o < 64 * ns; o += kFusedThreads) {
-        const int rl = o & 63, s = o >> 6, b = jb.g0 + s;
+    const int rsh = jb.rows == 128 ? 7 : 6;
+    for (int o = tid; o < (ns << rsh); o += kFusedThreads) {
+        const int rl = o & (jb.rows - 1), s = o >> rsh, b = jb.g0 + s;
         const float tot =
-            sum_splits(part + (size_t)((s >> 3) * 4 + (rl >> 4)) * a.s_in * 128, a.s_in, (rl & 15) * 8 + (s & 7));
-        const int j = jb.mb * 64 + rl;
+            sum_splits(part + (size_t)((s >> 3) * nmt + (rl >> 4)) * a.s_in * 128, a.s_in, (rl & 15) * 8 + (s & 7));
+        const int j = jb.r0 + rl;
         if (jb.h) {
             a.z[(size_t)b * a.di + j] = tot;
             continue;
@@ -615,7 +621,7 @@ __device__ __forceinline__ bool run_a(const FusedArgs& a, const StepMeta& m, con
 #pragma unroll
                 for (int j = 0; j < 4; j++)
                     if (r0 + i < a.xr && s0 + j < ns)
-                        a.xpart[((size_t)(jb.g0 + s0 + j) * (a.di / 64) + jb.mb) * a.xr + r0 + i] = acc[i][j];
+                        a.xpart[((size_t)(jb.g0 + s0 + j) * (a.di / 64) + jb.r0 / 64) * a.xr + r0 + i] = acc[i][j];
         }
     }
     return true;

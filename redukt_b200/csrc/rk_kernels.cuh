@@ -655,16 +655,35 @@ __global__ void __launch_bounds__(256) k_xproj_part(int M, int K, const float* _
     const int g = blockIdx.x, G = gridDim.x, b0 = blockIdx.y * 16, ns = min(16, n - b0);
     const int c0 = g * kXGroup, len = min(kXGroup, K - c0);
     const int tid = threadIdx.x;
-    // the weights are constant: staged before the dependency wait
-    for (int i = tid; i < M * 64; i += 256) {
-        const int r = i >> 6, c = i & 63;
-        xw[r * 68 + c] = c < len ? __ldg(W + (size_t)r * K + c0 + c) : 0.0f;
+    // the weights are constant: staged before the dependency wait, eight loads in flight per
+    // thread before their stores
+    for (int base = 0; base < M * 64; base += 8 * 256) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = base + u * 256 + tid, r = i >> 6, c = i & 63;
+            v[u] = (i < M * 64 && c < len) ? __ldg(W + (size_t)r * K + c0 + c) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = base + u * 256 + tid;
+            if (i < M * 64) xw[(i >> 6) * 68 + (i & 63)] = v[u];
+        }
     }
     pdl_wait();
     pdl_trigger();
-    for (int i = tid; i < 16 * 64; i += 256) {
-        const int sidx = i >> 6, c = i & 63;
-        xc[sidx * 68 + c] = (sidx < ns && c < len) ? act[(size_t)(b0 + sidx) * K + c0 + c] : 0.0f;
+    {
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int i = u * 256 + tid, sidx = i >> 6, c = i & 63;
+            v[u] = (sidx < ns && c < len) ? act[(size_t)(b0 + sidx) * K + c0 + c] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int i = u * 256 + tid;
+            xc[(i >> 6) * 68 + (i & 63)] = v[u];
+        }
     }
     __syncthreads();
     const int nsb = (ns + 3) >> 2, nblk = ((M + 1) >> 1) * nsb;
