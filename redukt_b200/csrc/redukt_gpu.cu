@@ -470,7 +470,21 @@ bool prepare_fused() {
                                 cudaMemcpyDeviceToDevice) == cudaSuccess;
             }
             if (!ok) return false;
-            h[i] = FusedLayer{L.norm_w, L.norm_b, L.in_proj.q, L.in_proj.s, L.out_proj.q, L.out_proj.s, xw, ct, sb};
+            // in_proj by 64-row block and out_proj by 16-row block, every group of a block adjacent,
+            // so a fused-step job's weight tile is one contiguous copy per block
+            int8_t *ib = nullptr, *ob = nullptr;
+            const int gi = G.d / 64, go = G.di / 64;
+            const size_t mi = (size_t)round_up(2 * G.di, 128), mo = (size_t)round_up(G.d, 128);
+            if (!model_alloc(&ib, (size_t)2 * G.di * G.d) || !model_alloc(&ob, (size_t)G.d * G.di)) return false;
+            for (int b = 0; ok && b < 2 * G.di / 64; b++)
+                ok = cudaMemcpy2D(ib + (size_t)b * gi * 4096, 4096, L.in_proj.q + (size_t)b * 64 * 64, mi * 64, 4096, gi,
+                                  cudaMemcpyDeviceToDevice) == cudaSuccess;
+            for (int b = 0; ok && b < G.d / 16; b++)
+                ok = cudaMemcpy2D(ob + (size_t)b * go * 1024, 1024, L.out_proj.q + (size_t)b * 16 * 64, mo * 64, 1024, go,
+                                  cudaMemcpyDeviceToDevice) == cudaSuccess;
+            if (!ok) return false;
+            h[i] = FusedLayer{L.norm_w, L.norm_b, L.in_proj.q, L.in_proj.s, L.out_proj.q, L.out_proj.s, xw, ct, sb,
+                              ib, ob};
         }
     }
     if (!model_alloc(&G.d_fused, (size_t)G.nl)) return false;

@@ -52,6 +52,8 @@ struct FusedLayer {
     const float* xw_blk;   // x_proj by channel group [di/64][xr][68] (4 zero floats per row)
     const float* ct_blk;   // conv taps 0..3 and bias by channel group [di/64][5][64]
     const float* sb_blk;   // dt_proj columns, A, dt bias, D by channel group [di/64][dr + 18][64]
+    const int8_t* in_blk;  // in_proj by 64-row block [2 di/64][G][64][64] (tiled rows, swizzle kept)
+    const int8_t* out_blk; // out_proj by 16-row block [d/16][G][16][64]
 };
 
 // Shared-memory map (byte offsets).  One prefetch region P holds the current phase's copied
@@ -403,7 +405,8 @@ __device__ __forceinline__ void prefetch_a(const FusedArgs& a, const StepMeta& m
     const int ns = min(jb.sg, a.n - jb.g0);
     const bool xh = jb.h == 0;
     const int nb = L.norm_b ? 1 : 0;
-    const int count = a.g_in + 2 + nb + (xh ? 2 : 0);
+    const int nwb = jb.rows / 64;  // 64-row weight blocks, one contiguous copy each
+    const int count = nwb + 2 + nb + (xh ? 2 : 0);
     const uint32_t bytes =
         a.g_in * jb.rows * 64 + jb.rows * a.g_in * 4 + a.d * 4 * (1 + nb) + (xh ? a.xr * 68 * 4 + 5 * 64 * 4 : 0);
     if (xh) {  // conv state: 256-byte pieces, as 16-byte copies spread over the CTA
@@ -416,17 +419,17 @@ __device__ __forceinline__ void prefetch_a(const FusedArgs& a, const StepMeta& m
     }
     cp_async_commit();
     issue_copies(bar, bytes, count, [&](int k) {
-        if (k < a.g_in) {
-            tc::bulk_load(P + a.lay.a_w + k * jb.rows * 64, L.in_q + ((size_t)k * a.mpad_in + row0) * 64, jb.rows * 64,
-                          bar);
-        } else if (k == a.g_in) {
+        if (k < nwb) {
+            tc::bulk_load(P + a.lay.a_w + k * a.g_in * 4096, L.in_blk + (size_t)(row0 / 64 + k) * a.g_in * 4096,
+                          a.g_in * 4096, bar);
+        } else if (k == nwb) {
             tc::bulk_load(P + a.lay.a_ws, L.in_s + (size_t)row0 * a.g_in, jb.rows * a.g_in * 4, bar);
-        } else if (k == a.g_in + 1) {
+        } else if (k == nwb + 1) {
             tc::bulk_load(P + a.lay.a_nw, L.norm_w, a.d * 4, bar);
-        } else if (nb && k == a.g_in + 2) {
+        } else if (nb && k == nwb + 2) {
             tc::bulk_load(P + a.lay.a_nw + a.d * 4, L.norm_b, a.d * 4, bar);
         } else {
-            const int q = k - (a.g_in + 2 + nb);
+            const int q = k - (nwb + 2 + nb);
             if (q == 0) tc::bulk_load(P + a.lay.a_xw, L.xw_blk + (size_t)mb * a.xr * 68, a.xr * 68 * 4, bar);
             else tc::bulk_load(P + a.lay.a_ct, L.ct_blk + (size_t)mb * 5 * 64, 5 * 64 * 4, bar);
         }
@@ -468,9 +471,11 @@ __device__ __forceinline__ void prefetch_c(const FusedArgs& a, const FusedLayer&
     }
     cp_async_commit();
     const uint32_t bytes = a.g_out * a.mc * 64 + a.mc * a.g_out * 4;
-    issue_copies(bar, bytes, a.g_out + 1, [&](int k) {
-        if (k < a.g_out)
-            tc::bulk_load(P + a.lay.c_w + k * a.mc * 64, L.out_q + ((size_t)k * a.mpad_out + jb.row0) * 64, a.mc * 64, bar);
+    const int nwb = a.mc / 16;  // 16-row weight blocks, one contiguous copy each
+    issue_copies(bar, bytes, nwb + 1, [&](int k) {
+        if (k < nwb)
+            tc::bulk_load(P + a.lay.c_w + k * a.g_out * 1024, L.out_blk + (size_t)(jb.row0 / 16 + k) * a.g_out * 1024,
+                          a.g_out * 1024, bar);
         else
             tc::bulk_load(P + a.lay.c_ws, L.out_s + (size_t)jb.row0 * a.g_out, a.mc * a.g_out * 4, bar);
     });
@@ -540,8 +545,10 @@ __device__ __forceinline__ bool run_a(const FusedArgs& a, const StepMeta& m, con
         const int t = task / (nmt * a.s_in), rem = task - t * nmt * a.s_in, mt = rem / a.s_in, sp = rem - mt * a.s_in;
         const int8_t* bt = bq + t * tile_bytes + gid * pitch + tig * 4;
         float acc[4];
-        q8_tile16_split(reinterpret_cast<const int8_t*>(sm + a.lay.a_w), jb.rows, mt * 16,
-                        reinterpret_cast<const float*>(sm + a.lay.a_ws), a.g_in, a.g_in * sp / a.s_in,
+        // weight block mt / 4 ([G][64][64]), its 16-row tile mt % 4; scales [rows][G]
+        q8_tile16_split(reinterpret_cast<const int8_t*>(sm + a.lay.a_w) + (mt >> 2) * a.g_in * 4096, 64, (mt & 3) * 16,
+                        reinterpret_cast<const float*>(sm + a.lay.a_ws) + (mt >> 2) * 64 * a.g_in, a.g_in,
+                        a.g_in * sp / a.s_in,
                         a.g_in * (sp + 1) / a.s_in,
                         [&](int p, int g, int c) {
                             return *reinterpret_cast<const uint32_t*>(bt + p * 8 * pitch + g * 64 + c * 16);
@@ -760,8 +767,10 @@ __device__ __forceinline__ bool run_c(const FusedArgs& a, int job, char* sm, Cop
     for (int task = warp; task < ntask; task += 8) {
         const int mt = task / a.s_out, sp = task - mt * a.s_out;
         float acc[4];
-        q8_tile16_split(reinterpret_cast<const int8_t*>(sm + a.lay.c_w), a.mc, mt * 16,
-                        reinterpret_cast<const float*>(sm + a.lay.c_ws), a.g_out, a.g_out * sp / a.s_out,
+        // weight block mt ([G][16][64]); scales [rows][G]
+        q8_tile16_split(reinterpret_cast<const int8_t*>(sm + a.lay.c_w) + mt * a.g_out * 1024, 16, 0,
+                        reinterpret_cast<const float*>(sm + a.lay.c_ws) + mt * 16 * a.g_out, a.g_out,
+                        a.g_out * sp / a.s_out,
                         a.g_out * (sp + 1) / a.s_out,
                         [&](int p, int g, int c) {
                             return *reinterpret_cast<const uint32_t*>(brow + (g * 3 + p) * 512 + ((c ^ bsw) << 4));
