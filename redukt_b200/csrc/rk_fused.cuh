@@ -6,7 +6,7 @@
 // cooperative launch) and walks the layers in three phases separated by grid-wide barriers:
 //
 //   A  norm + in_proj + causal conv/SiLU + x_proj group chains
-//      job = (half of in_proj, 64-row block, group of 8 or 16 streams).  The CTA normalises its
+//      job = (half of in_proj, 64 or 128 rows, 8 or 16 streams).  The CTA normalises its
 //      streams itself (their digit planes never leave shared memory), multiplies them with
 //      warp-level int8 MMAs, finishes each (row, stream) with the split-order combine and the
 //      in_proj epilogue, and for x-half blocks evaluates the x_proj chains of that channel group.
@@ -17,9 +17,10 @@
 //
 // Everything a phase reads that the phase before it does not write (weights and scales, the
 // conv and SSM state of earlier steps, the residual rows a job updates) is fetched into shared
-// memory by a few bulk copies (cp.async.bulk, one mbarrier) issued between the CTA's arrival at
-// the barrier before the phase and its wait there, so the copies overlap the barrier.  The
-// per-group operands are stored group-blocked in HBM (FusedLayer) so each is one contiguous copy.
+// memory by a few bulk copies (cp.async.bulk, one mbarrier) and 16-byte copies issued between the
+// CTA's arrival at the barrier before the phase and its wait there, so the copies overlap the
+// barrier.  Weight tiles and the per-group operands are stored job-blocked in HBM (FusedLayer), so
+// each is one contiguous copy.
 // After the barrier a job only reads its predecessor's outputs (from L2).  After the last layer
 // the final norm writes the head's digit planes; the host launches the head projection.
 //
