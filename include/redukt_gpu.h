@@ -53,7 +53,8 @@ typedef struct {
  * (version 3 with flag bit 4, this engine's model-kind extension; W8A8 like the reference's
  * default RWKV-7 quantisation, src/infrastructure/rwkv7/model.rs:245).  Every entry point below
  * serves both kinds unless its comment says otherwise; BackendInfo.name says which is loaded
- * ("b200-mamba-*" or "b200-rwkv7-w8a8"). */
+ * ("b200-mamba-*" or "b200-rwkv7-w8a8").  Mamba header flag bits 2/3 select the Q8 profile, and bit 6
+ * (with bit 2) marks Q8 matrices stored as int8 + group scales in the file (no quantisation at load). */
 BackendResult redukt_backend_init(const uint8_t* weights_path, int32_t device_id, BackendInfo* info_out);
 
 /* One step of the v1 stream; writes vocab_size logits.  Replaces mamba_cuda.cu:710-715. */

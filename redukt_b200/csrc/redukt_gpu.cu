@@ -33,6 +33,7 @@ constexpr uint32_t kFlagNormBias = 1u << 0;
 constexpr uint32_t kFlagUntiedHead = 1u << 1;
 constexpr uint32_t kFlagQ8 = 1u << 2;
 constexpr uint32_t kFlagQ8PerRow = 1u << 3;
+constexpr uint32_t kFlagQ8Payload = 1u << 6;  // Q8 matrices stored as int8 + group scales (no quantise at load)
 constexpr uint32_t kMaxStreams = 4096u;  // batch_init cap (mamba_cuda.cu:55)
 
 enum Profile { kF32 = 0, kQ8 = 1, kQ8Row = 2 };
@@ -139,6 +140,7 @@ struct Model {
     int fused_nc = 0;           // norm chunks of the instantiated kernel, 0 = shape not supported
     int fused_ctas_per_sm = 2;  // option "fused_ctas"
     int head_ctas = 2;          // option "head_ctas": 2 = the two-CTAs-per-SM head tiles at small batch
+    bool q8_payload = false;    // the loaded file stores its Q8 matrices quantised (flag bit 6)
     int num_sms = 0;
     FusedLayer* d_fused = nullptr;  // [nl] device copy of the layer pointers
 };
@@ -264,6 +266,19 @@ struct Reader {
         if (f) fclose(f);
         if (staging) cudaFreeHost(staging);
     }
+    // Reads `bytes` bytes into the device buffer `dst`.
+    bool read_bytes(void* dst, size_t bytes) {
+        const size_t cap = staging_n * sizeof(float);
+        size_t done = 0;
+        while (done < bytes) {
+            size_t chunk = std::min(cap, bytes - done);
+            if (fread(staging, 1, chunk, f) != chunk) return false;
+            if (cudaMemcpy(static_cast<char*>(dst) + done, staging, chunk, cudaMemcpyHostToDevice) != cudaSuccess)
+                return false;
+            done += chunk;
+        }
+        return true;
+    }
     // Reads `count` floats into the device buffer `dst`.
     bool read_to(float* dst, size_t count) {
         size_t done = 0;
@@ -289,7 +304,6 @@ bool load_mat(Reader& r, Mat* m, int rows, int cols, bool quantise) {
     m->cols = cols;
     size_t count = (size_t)rows * cols;
     if (!quantise || G.profile == kF32) return load_f32(r, &m->f, count);
-    if (!r.read_to(g_tmp, count)) return false;
     int groups = cols / kGroup;
     const int rows_pad = round_up(rows, tc::kBM);
     int8_t* q_rm = nullptr;  // row-major quantised copy, then tiled
@@ -298,7 +312,15 @@ bool load_mat(Reader& r, Mat* m, int rows, int cols, bool quantise) {
         cudaFree(q_rm);
         return false;
     }
-    if (G.profile == kQ8) {
+    if (G.q8_payload) {  // stored quantised: int8 [rows][cols], then f32 scales [rows][groups]
+        if (!r.read_bytes(q_rm, count) || !r.read_to(m->s, (size_t)rows * groups)) {
+            cudaFree(q_rm);
+            return false;
+        }
+    } else if (!r.read_to(g_tmp, count)) {
+        cudaFree(q_rm);
+        return false;
+    } else if (G.profile == kQ8) {
         size_t ng = count / kGroup;
         k_quantize_q8<<<(unsigned)((ng + 7) / 8), 256>>>(g_tmp, ng, kGroup, q_rm, m->s);
     } else {
@@ -368,17 +390,27 @@ int load_weights(const char* path) {
         else if (!strcmp(e, "q8")) G.profile = kQ8;
         else if (!strcmp(e, "q8row")) G.profile = kQ8Row;
     }
+    G.q8_payload = (h.flags & kFlagQ8Payload) != 0;
+    if (G.q8_payload && G.profile != kQ8) {
+        set_err("%s: a Q8 payload file holds group-64 int8 weights; it loads only as the Q8 (group 64) profile", path);
+        return BACKEND_WEIGHTS_NOT_FOUND;
+    }
     // expected file size
     size_t d = G.d, di = G.di, V = G.V, xr = G.xr, dr = G.dr;
     bool nb = h.flags & kFlagNormBias, untied = h.flags & kFlagUntiedHead;
     size_t per_layer = d * (nb ? 2 : 1) + 2 * di * d + di * kDConv + di + xr * di + di * dr + di + di * kDState +
                        di + d * di;
     size_t total = V * d + G.nl * per_layer + d * (nb ? 2 : 1) + (untied ? V * d : 0);
+    size_t body = total * 4;
+    if (G.q8_payload) {  // the Q8 matrices take 1 byte a weight + 4 bytes a 64-column group
+        const size_t q8_elems = V * d * (untied ? 2 : 1) + G.nl * (2 * di * d + d * di);
+        body = (total - q8_elems) * 4 + q8_elems + q8_elems / kGroup * 4;
+    }
     fseek(r.f, 0, SEEK_END);
     long fsz = ftell(r.f);
     fseek(r.f, (long)sizeof(h), SEEK_SET);
-    if (fsz < 0 || (size_t)fsz != sizeof(h) + total * 4) {
-        set_err("%s: size %ld does not match the header (%zu expected)", path, fsz, sizeof(h) + total * 4);
+    if (fsz < 0 || (size_t)fsz != sizeof(h) + body) {
+        set_err("%s: size %ld does not match the header (%zu expected)", path, fsz, sizeof(h) + body);
         return BACKEND_WEIGHTS_NOT_FOUND;
     }
     r.staging_n = (size_t)16 << 20;

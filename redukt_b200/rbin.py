@@ -11,7 +11,11 @@ Flag bits 0 (LayerNorm bias) and 1 (untied head) are the reference's.  Bits 2 an
 engine's additive selectors for the Q8 weight-only profile (quantised at load with the
 reference recipe, `src/domain/gemv.rs:251-273`): bit 2 = Q8 with one scale per 64 columns
 (`Q8_GROUP`, `src/infrastructure/mamba/model.rs:50-56`), bit 3 (with bit 2) = one scale per row.
-The reference plugin ignores both bits and runs F32.
+The reference plugin ignores both bits and runs F32.  Bit 6 (with bit 2, group scales) marks a
+native Q8 payload: the Q8 matrices (embedding, in_proj, out_proj, untied head) are stored as int8
+[rows][cols] followed by their f32 scales [rows][cols/64], already quantised with the same recipe,
+so loading skips the f32 read and the quantisation (`to_q8_payload` converts an F32 file).  Such a
+file is this engine's only; the reference plugin cannot read it.
 
 No real checkpoint is available, so every model here is generated from a seed.
 """
@@ -31,6 +35,8 @@ FLAG_NORM_BIAS = 1 << 0
 FLAG_UNTIED_HEAD = 1 << 1
 FLAG_Q8 = 1 << 2
 FLAG_Q8_PER_ROW = 1 << 3
+FLAG_Q8_PAYLOAD = 1 << 6
+Q8_GROUP = 64
 TOK_BYTE, TOK_BPE = 0, 1
 
 MAMBA130M_SEED = 0x5EED0130
@@ -122,8 +128,80 @@ def write_rbin(path: str, dims: MambaDims, arrays: Iterator[Tuple[str, np.ndarra
     return h.hexdigest()
 
 
+def is_q8_matrix(name: str) -> bool:
+    """The matrices the Q8 profile quantises (src/infrastructure/mamba/model.rs:375-376)."""
+    return name in ("embeddings", "lm_head_w") or name.endswith(("in_proj_w", "out_proj_w"))
+
+
+def q8_quantize(w: np.ndarray) -> Tuple[np.ndarray, np.ndarray]:
+    """Q8wMatrix::quantize (src/domain/gemv.rs:256-273) with one scale per 64 columns, in f32:
+    scale = max|w| / 127 (1 for an all-zero group), q = clamp(round(w * (1 / scale)), -127, 127),
+    round half away from zero.  Returns (int8 [rows][cols], f32 [rows][cols / 64])."""
+    rows, cols = w.shape
+    g = np.ascontiguousarray(w, dtype=np.float32).reshape(rows, cols // Q8_GROUP, Q8_GROUP)
+    amax = np.abs(g).max(axis=2)
+    scale = np.where(amax > 0, amax / np.float32(127.0), np.float32(1.0)).astype(np.float32)
+    inv = (np.float32(1.0) / scale).astype(np.float32)
+    prod = (g * inv[:, :, None]).astype(np.float32)
+    t = np.trunc(prod)
+    r = t + np.where(np.abs(prod - t) >= np.float32(0.5), np.sign(prod), np.float32(0.0))
+    q = np.clip(r, -127, 127).astype(np.int8).reshape(rows, cols)
+    return q, scale
+
+
+def to_q8_payload(src: str, dst: str) -> str:
+    """Rewrite an F32 Mamba .rbin as a native Q8 payload file (flags |= FLAG_Q8 | FLAG_Q8_PAYLOAD):
+    each Q8 matrix becomes its int8 values followed by its group scales; the rest is copied."""
+    dims, flags, tok = read_header(src)
+    if flags & (FLAG_Q8_PAYLOAD | FLAG_Q8_PER_ROW):
+        raise ValueError(f"{src}: already a payload file, or per-row scales (the payload has group scales)")
+    _, _, arrays = read_arrays(src)
+    with open(src, "rb") as f:
+        w = list(RBIN_HEADER.unpack(f.read(RBIN_HEADER.size)))
+    w[9] = flags | FLAG_Q8 | FLAG_Q8_PAYLOAD
+    with open(dst + ".part", "wb") as g:
+        g.write(RBIN_HEADER.pack(*w))
+        for name, _shape in array_order(dims, flags):
+            a = arrays[name]
+            if is_q8_matrix(name):
+                q, sc = q8_quantize(a)
+                g.write(q.tobytes())
+                g.write(np.ascontiguousarray(sc, dtype="<f4").tobytes())
+            else:
+                g.write(np.ascontiguousarray(a, dtype="<f4").tobytes())
+    os.replace(dst + ".part", dst)
+    return dst
+
+
+def read_q8_payload(path: str) -> Tuple[MambaDims, int, Dict[str, object]]:
+    """Arrays of a payload file: f32 arrays as they are, Q8 matrices as (int8 q, f32 scales)."""
+    dims, flags, _ = read_header(path)
+    if not flags & FLAG_Q8_PAYLOAD:
+        raise ValueError(f"{path}: not a Q8 payload file")
+    raw = np.fromfile(path, dtype=np.uint8, offset=RBIN_HEADER.size)
+    out: Dict[str, object] = {}
+    off = 0
+    for name, shape in array_order(dims, flags & ~(FLAG_Q8 | FLAG_Q8_PAYLOAD)):
+        n = int(np.prod(shape))
+        if is_q8_matrix(name):
+            q = raw[off:off + n].view(np.int8).reshape(shape)
+            off += n
+            ns = shape[0] * (shape[1] // Q8_GROUP)
+            sc = raw[off:off + 4 * ns].view("<f4").reshape(shape[0], shape[1] // Q8_GROUP)
+            off += 4 * ns
+            out[name] = (q, sc)
+        else:
+            out[name] = raw[off:off + 4 * n].view("<f4").reshape(shape)
+            off += 4 * n
+    if off != raw.size:
+        raise ValueError(f"{path}: {raw.size - off} trailing bytes")
+    return dims, flags, out
+
+
 def read_arrays(path: str) -> Tuple[MambaDims, int, Dict[str, np.ndarray]]:
     dims, flags, _ = read_header(path)
+    if flags & FLAG_Q8_PAYLOAD:
+        raise ValueError(f"{path}: a Q8 payload file (read_q8_payload)")
     mm = np.memmap(path, dtype="<f4", mode="r", offset=RBIN_HEADER.size)
     out, off = {}, 0
     for name, shape in array_order(dims, flags):
@@ -251,7 +329,7 @@ def with_flags(src: str, dst: str, set_flags: int, clear_flags: int = 0) -> str:
     """Copy an .rbin with header flag bits changed (the body is unchanged)."""
     dims, flags, tok = read_header(src)
     new = (flags | set_flags) & ~clear_flags
-    if (new ^ flags) & (FLAG_NORM_BIAS | FLAG_UNTIED_HEAD):
+    if (new ^ flags) & (FLAG_NORM_BIAS | FLAG_UNTIED_HEAD | FLAG_Q8_PAYLOAD):
         raise ValueError("layout bits cannot be changed without rewriting the body")
     if os.path.exists(dst):
         try:
