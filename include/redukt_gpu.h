@@ -180,6 +180,32 @@ int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* m
 int32_t redukt_b200_softmax_noalloc(const float* d_logits, uint32_t n_rows, uint32_t vocab, float* d_probs,
                                     void* cuda_stream);
 
+/* The range coder's frequency table, computed on the device: for each of n_rows rows of vocab f32
+ * logits, the vocab + 1 cumulative frequencies (cdf[0] = 0, cdf[vocab] = 2^24, every symbol >= 1)
+ * that the reference host builds with cdf_from_logits_with(row, NumericContract::FmathV1)
+ * (src/application/codec.rs:785-798: max, binary64 exp of fmath v1, sequential binary64 sum,
+ * f32 probabilities) and Cdf::from_probs (src/domain/coder.rs:43-82).  Bit-identical to it.
+ * It replaces the host CDF pass that follows the plugin's forward_batch
+ * (src/application/lockstep.rs:315,330).
+ * d_logits: device rows at stride ld_logits (>= vocab); d_cdf: device rows at stride ld_cdf
+ * (>= vocab + 1), also used as the row's workspace.  Optional queries, three uint32 per row in
+ * d_query_out (device): with d_symbols (encoder), {symbol, cdf[symbol], cdf[symbol + 1]}; with
+ * d_cum_freqs (decoder), {Cdf::lookup(cum), cdf[sym], cdf[sym + 1]} (coder.rs:100-114); an
+ * out-of-range symbol or a cum >= 2^24 gives {.., UINT32_MAX, UINT32_MAX}.  At most one of
+ * d_symbols / d_cum_freqs.  Work is enqueued on cuda_stream (NULL = the legacy default stream),
+ * not synchronised, and allocates nothing.  INVALID_ARGUMENT when vocab is 0 or >= 2^24 or a
+ * stride is too small.  Needs no model loaded. */
+int32_t redukt_b200_cdf_device(const float* d_logits, uint32_t n_rows, uint32_t vocab, uint32_t ld_logits,
+                               uint32_t* d_cdf, uint32_t ld_cdf, const uint32_t* d_symbols,
+                               const uint32_t* d_cum_freqs, uint32_t* d_query_out, void* cuda_stream);
+
+/* redukt_b200_cdf_device on host buffers (contiguous rows): copies the logits in, computes on the
+ * library's stream, and copies back whatever is asked for: cdf_out (n_rows x (vocab + 1), may be
+ * NULL) and, with symbols or cum_freqs (host), query_out (n_rows x 3).  Synchronous.  Device
+ * buffers are kept by the library between calls and grown when a call needs more. */
+int32_t redukt_b200_cdf(const float* logits, uint32_t n_rows, uint32_t vocab, uint32_t* cdf_out,
+                        const uint32_t* symbols, const uint32_t* cum_freqs, uint32_t* query_out);
+
 /* Last error message of this library (empty string when none). */
 const char* redukt_b200_last_error(void);
 

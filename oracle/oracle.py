@@ -1,4 +1,4 @@
-"""ctypes view of the CPU oracle (mamba_oracle.c; RWKV-7 in rwkv7.py) -- TEST INFRASTRUCTURE ONLY.
+"""ctypes view of the CPU oracle (mamba_oracle.c, cdf_oracle.c; RWKV-7 in rwkv7.py) -- TEST INFRASTRUCTURE ONLY.
 
 Only tests/, `__graft_entry__.smoke()` and bench.py's CPU-baseline leg import this module, and
 only as the checker or the timed CPU baseline.  The product path (redukt_b200) never does.
@@ -29,7 +29,7 @@ def build(ref: bool = False) -> None:
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
-        srcs = [os.path.join(HERE, f) for f in ("mamba_oracle.c", "rwkv7_oracle.c", "oracle_internal.h")]
+        srcs = [os.path.join(HERE, f) for f in ("mamba_oracle.c", "rwkv7_oracle.c", "cdf_oracle.c", "oracle_internal.h")]
         if not os.path.exists(LIB_PATH) or any(
                 os.path.exists(s) and os.path.getmtime(s) > os.path.getmtime(LIB_PATH) for s in srcs):
             build(ref=False)
@@ -58,6 +58,9 @@ def lib() -> ctypes.CDLL:
         L.orc_set_threads.argtypes = [i32]
         L.orc_get_threads.restype = i32
         L.orc_set_simd.argtypes = [i32]
+        L.orc_exp_f64.argtypes, L.orc_exp_f64.restype = [ctypes.c_double], ctypes.c_double
+        L.orc_cdf_from_logits.argtypes, L.orc_cdf_from_logits.restype = [vp, u32, u32, u32, vp, u32, i32], i32
+        L.orc_cdf_lookup.argtypes, L.orc_cdf_lookup.restype = [vp, u32, u32], u32
         _lib = L
     return _lib
 
@@ -76,6 +79,28 @@ def lnf(x: float) -> float:
 
 def softplus(x: float) -> float:
     return lib().orc_softplus(x)
+
+
+def exp_f64(x: float) -> float:
+    """The reference's portable binary64 exp (fmath-v1, src/domain/fmath.rs:383-429)."""
+    return lib().orc_exp_f64(x)
+
+
+def cdf_from_logits(logits: np.ndarray, threads: int = 1) -> np.ndarray:
+    """Rows of f32 logits -> rows of vocab+1 uint32 CDF entries (total 2^24), the reference's
+    `cdf_from_logits_with(.., FmathV1)` + `Cdf::from_probs` (codec.rs:785-798, coder.rs:43-82)."""
+    x = np.ascontiguousarray(np.atleast_2d(logits), dtype=np.float32)
+    n, v = x.shape
+    out = np.empty((n, v + 1), dtype=np.uint32)
+    if lib().orc_cdf_from_logits(_p(x), n, v, v, _p(out), v + 1, int(threads)) != 0:
+        raise ValueError(f"cdf_from_logits: invalid shape {x.shape}")
+    return out
+
+
+def cdf_lookup(cdf_row: np.ndarray, cum_freq: int) -> int:
+    """`Cdf::lookup` (coder.rs:100-114): the symbol whose interval holds cum_freq."""
+    c = np.ascontiguousarray(cdf_row, dtype=np.uint32)
+    return int(lib().orc_cdf_lookup(_p(c), c.shape[0] - 1, int(cum_freq)))
 
 
 def set_threads(n: int) -> None:

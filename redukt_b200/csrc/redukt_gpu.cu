@@ -23,6 +23,7 @@
 #include "rk_fused.cuh"
 #include "rk_rwkv7.cuh"
 #include "rk_tc.cuh"
+#include "rk_cdf.cuh"
 
 namespace {
 
@@ -1087,6 +1088,35 @@ static __device__ __align__(256) float g_noalloc_scratch[kNoAllocMaxRows * kNoAl
 std::mutex g_noalloc_mu;
 float* g_noalloc_ptr[kNoAllocMaxDevices] = {};  // device address of g_noalloc_scratch, per device
 
+// Device buffers of the host-buffer CDF entry point (redukt_b200_cdf), grown on demand.
+struct CdfHostBuffers {
+    std::mutex mu;
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    float* logits = nullptr;
+    uint32_t* cdf = nullptr;
+    uint32_t* query_in = nullptr;
+    uint32_t* query_out = nullptr;
+    size_t logit_cap = 0, cdf_cap = 0, row_cap = 0;
+};
+CdfHostBuffers g_cdf_host;
+
+int32_t check_cdf_args(uint32_t n_rows, uint32_t vocab, uint32_t ld_logits, uint32_t ld_cdf) {
+    if (vocab == 0 || vocab >= cdf::kTotal) {
+        set_err("cdf: vocab %u outside [1, 2^24)", vocab);
+        return BACKEND_INVALID_ARGUMENT;
+    }
+    if (ld_logits < vocab || ld_cdf < vocab + 1) {
+        set_err("cdf: strides %u / %u too small for %u logits", ld_logits, ld_cdf, vocab);
+        return BACKEND_INVALID_ARGUMENT;
+    }
+    if (n_rows > 0x7fffffffu) {
+        set_err("cdf: %u rows", n_rows);
+        return BACKEND_INVALID_ARGUMENT;
+    }
+    return BACKEND_OK;
+}
+
 }  // namespace
 
 // ==========================================================================================
@@ -1543,6 +1573,78 @@ int32_t redukt_b200_softmax_noalloc(const float* d_logits, uint32_t n_rows, uint
     k_softmax_final<<<dim3(std::max(1, std::min(64, (int)vocab / 1024)), n_rows), 256, 0, st>>>(
         d_logits, (int)vocab, scratch, parts, d_probs);
     CK(cudaGetLastError(), BACKEND_FORWARD_FAILED);
+    return BACKEND_OK;
+}
+
+int32_t redukt_b200_cdf_device(const float* d_logits, uint32_t n_rows, uint32_t vocab, uint32_t ld_logits,
+                               uint32_t* d_cdf, uint32_t ld_cdf, const uint32_t* d_symbols,
+                               const uint32_t* d_cum_freqs, uint32_t* d_query_out, void* cuda_stream) {
+    if (!d_logits || !d_cdf) return BACKEND_INVALID_ARGUMENT;
+    if (int32_t rc = check_cdf_args(n_rows, vocab, ld_logits, ld_cdf)) return rc;
+    if ((d_symbols || d_cum_freqs) && !d_query_out) return BACKEND_INVALID_ARGUMENT;
+    if (d_symbols && d_cum_freqs) {
+        set_err("cdf: give symbols or cum_freqs, not both");
+        return BACKEND_INVALID_ARGUMENT;
+    }
+    if (n_rows == 0) return BACKEND_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(cuda_stream);
+    cdf::k_cdf_rows<<<n_rows, cdf::kThreads, 0, st>>>(d_logits, (int)vocab, (int)ld_logits, d_cdf, (int)ld_cdf,
+                                                       d_symbols, d_cum_freqs,
+                                                       (d_symbols || d_cum_freqs) ? d_query_out : nullptr);
+    CK(cudaGetLastError(), BACKEND_FORWARD_FAILED);
+    return BACKEND_OK;
+}
+
+int32_t redukt_b200_cdf(const float* logits, uint32_t n_rows, uint32_t vocab, uint32_t* cdf_out,
+                        const uint32_t* symbols, const uint32_t* cum_freqs, uint32_t* query_out) {
+    if (!logits) return BACKEND_INVALID_ARGUMENT;
+    if (int32_t rc = check_cdf_args(n_rows, vocab, vocab, vocab + 1)) return rc;
+    const bool query = symbols || cum_freqs;
+    if ((query && !query_out) || (symbols && cum_freqs)) return BACKEND_INVALID_ARGUMENT;
+    if (n_rows == 0) return BACKEND_OK;
+    CdfHostBuffers& B = g_cdf_host;
+    std::lock_guard<std::mutex> lock(B.mu);
+    int dev = 0;
+    CK(cudaGetDevice(&dev), BACKEND_FORWARD_FAILED);
+    if (B.device != dev) {   // buffers belong to one device: start over on another
+        if (B.stream) { cudaStreamDestroy(B.stream); B.stream = nullptr; }
+        cudaFree(B.logits); cudaFree(B.cdf); cudaFree(B.query_in); cudaFree(B.query_out);
+        B.logits = nullptr; B.cdf = nullptr; B.query_in = B.query_out = nullptr;
+        B.logit_cap = B.cdf_cap = B.row_cap = 0;
+        B.device = dev;
+        CK(cudaStreamCreateWithFlags(&B.stream, cudaStreamNonBlocking), BACKEND_FORWARD_FAILED);
+    }
+    const size_t nl = (size_t)n_rows * vocab, nc = (size_t)n_rows * (vocab + 1);
+    if (nl > B.logit_cap) {
+        cudaFree(B.logits); B.logits = nullptr; B.logit_cap = 0;
+        CK(cudaMalloc(&B.logits, nl * sizeof(float)), BACKEND_FORWARD_FAILED);
+        B.logit_cap = nl;
+    }
+    if (nc > B.cdf_cap) {
+        cudaFree(B.cdf); B.cdf = nullptr; B.cdf_cap = 0;
+        CK(cudaMalloc(&B.cdf, nc * sizeof(uint32_t)), BACKEND_FORWARD_FAILED);
+        B.cdf_cap = nc;
+    }
+    if (n_rows > B.row_cap) {
+        cudaFree(B.query_in); cudaFree(B.query_out); B.query_in = B.query_out = nullptr; B.row_cap = 0;
+        CK(cudaMalloc(&B.query_in, (size_t)n_rows * sizeof(uint32_t)), BACKEND_FORWARD_FAILED);
+        CK(cudaMalloc(&B.query_out, (size_t)n_rows * 3 * sizeof(uint32_t)), BACKEND_FORWARD_FAILED);
+        B.row_cap = n_rows;
+    }
+    CK(cudaMemcpyAsync(B.logits, logits, nl * sizeof(float), cudaMemcpyHostToDevice, B.stream), BACKEND_FORWARD_FAILED);
+    if (query)
+        CK(cudaMemcpyAsync(B.query_in, symbols ? symbols : cum_freqs, (size_t)n_rows * sizeof(uint32_t),
+                           cudaMemcpyHostToDevice, B.stream), BACKEND_FORWARD_FAILED);
+    int32_t rc = redukt_b200_cdf_device(B.logits, n_rows, vocab, vocab, B.cdf, vocab + 1,
+                                        symbols ? B.query_in : nullptr, cum_freqs ? B.query_in : nullptr,
+                                        B.query_out, B.stream);
+    if (rc != BACKEND_OK) return rc;
+    if (cdf_out)
+        CK(cudaMemcpyAsync(cdf_out, B.cdf, nc * sizeof(uint32_t), cudaMemcpyDeviceToHost, B.stream), BACKEND_FORWARD_FAILED);
+    if (query)
+        CK(cudaMemcpyAsync(query_out, B.query_out, (size_t)n_rows * 3 * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                           B.stream), BACKEND_FORWARD_FAILED);
+    CK(cudaStreamSynchronize(B.stream), BACKEND_FORWARD_FAILED);
     return BACKEND_OK;
 }
 

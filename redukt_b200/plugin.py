@@ -34,7 +34,7 @@ EXT_SYMBOLS = ("redukt_backend_set_reset_every", "redukt_backend_forward_batch_p
                "redukt_b200_forward_batch_device", "redukt_b200_device_error", "redukt_b200_get_state",
                "redukt_b200_get_q8", "redukt_b200_info", "redukt_b200_set_option", "redukt_b200_kernel_times",
                "redukt_b200_time_kernel", "redukt_b200_softmax_noalloc", "redukt_b200_rwkv_get_state",
-               "redukt_b200_last_error")
+               "redukt_b200_cdf_device", "redukt_b200_cdf", "redukt_b200_last_error")
 KERNEL_CLASSES = ("embed", "norm", "in_proj", "x_proj", "scan", "out_proj", "head", "softmax", "step")
 
 
@@ -139,6 +139,10 @@ class PluginLibrary:
             L.redukt_b200_rwkv_get_state.argtypes = [u32, f32p, f32p, f32p, f32p]
             L.redukt_b200_rwkv_get_state.restype = i32
             L.redukt_b200_softmax_noalloc.restype = i32
+            L.redukt_b200_cdf_device.argtypes = [vp, u32, u32, u32, vp, u32, vp, vp, vp, vp]
+            L.redukt_b200_cdf_device.restype = i32
+            L.redukt_b200_cdf.argtypes = [f32p, u32, u32, u32p, u32p, u32p, u32p]
+            L.redukt_b200_cdf.restype = i32
             L.redukt_b200_last_error.argtypes, L.redukt_b200_last_error.restype = [], ctypes.c_char_p
 
     def softmax_noalloc(self, d_logits: int, n_rows: int, vocab: int, d_probs: int, stream: int = 0) -> BackendResult:
@@ -146,6 +150,36 @@ class PluginLibrary:
         (redukt_b200_softmax_noalloc); raw device addresses, stream 0 = legacy default stream."""
         return BackendResult.from_code(self.lib.redukt_b200_softmax_noalloc(d_logits, n_rows, vocab, d_probs,
                                                                             stream or None))
+
+    def cdf_device(self, d_logits: int, n_rows: int, vocab: int, ld_logits: int, d_cdf: int, ld_cdf: int,
+                   d_symbols: int = 0, d_cum_freqs: int = 0, d_query_out: int = 0, stream: int = 0) -> BackendResult:
+        """The coder CDF of device logit rows into device rows of vocab + 1 words
+        (redukt_b200_cdf_device); raw device addresses, stream 0 = legacy default stream."""
+        return BackendResult.from_code(self.lib.redukt_b200_cdf_device(
+            d_logits, n_rows, vocab, ld_logits, d_cdf, ld_cdf, d_symbols or None, d_cum_freqs or None,
+            d_query_out or None, stream or None))
+
+    def cdf(self, logits: np.ndarray, symbols: Optional[np.ndarray] = None, cum_freqs: Optional[np.ndarray] = None,
+            want_cdf: bool = True):
+        """Host rows of f32 logits -> (cdf [n, vocab + 1] uint32 or None, queries [n, 3] uint32 or None),
+        the reference's cdf_from_logits_with(.., FmathV1) + Cdf::from_probs (redukt_b200_cdf).  Raises
+        ValueError on INVALID_ARGUMENT and RuntimeError on any other failure."""
+        x = np.ascontiguousarray(np.atleast_2d(logits), dtype=np.float32)
+        n, v = x.shape
+        out = np.empty((n, v + 1), dtype=np.uint32) if want_cdf else None
+        q_in = symbols if symbols is not None else cum_freqs
+        q_in = None if q_in is None else np.ascontiguousarray(q_in, dtype=np.uint32).reshape(n)
+        q_out = np.empty((n, 3), dtype=np.uint32) if q_in is not None else None
+        u32p = ctypes.POINTER(ctypes.c_uint32)
+        ptr = (lambda a: a.ctypes.data_as(u32p) if a is not None else None)
+        code = BackendResult.from_code(self.lib.redukt_b200_cdf(
+            x.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n, v, ptr(out),
+            ptr(q_in) if symbols is not None else None, ptr(q_in) if cum_freqs is not None else None, ptr(q_out)))
+        if code == BackendResult.INVALID_ARGUMENT:
+            raise ValueError(f"cdf: invalid argument ({self.last_error()})")
+        if code != BackendResult.OK:
+            raise RuntimeError(f"cdf failed: {code.name} ({self.last_error()})")
+        return out, q_out
 
     def last_error(self) -> str:
         if not self.has_ext:
