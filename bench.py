@@ -322,6 +322,8 @@ def run_b200(args, rank, world, local, dist):
 
     if world == 1 and not args.no_sweep:
         res["sweep"] = sweep(b, f32_path, q8_path, dims, args, dev, peaks)
+    if world == 1 and not args.no_cdf:
+        res["coder_cdf"] = coder_cdf(b.libobj, n, V, dev, with_cpu=rank == 0 and not args.no_cpu_baseline)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         b.close()
         res["cpu_baseline"] = cpu_baseline(q8_path, n, args.cpu_seconds)
@@ -462,6 +464,88 @@ def run_reference(args, rank, world):
             "e2e": {"value": round(v, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def coder_cdf(lib, n: int, vocab: int, dev, with_cpu: bool, reps: int = 20) -> dict:
+    """The coder's 24-bit CDF for the step's n rows (redukt_b200_cdf_device), the reference's
+    cdf_from_logits_with(.., FmathV1) + Cdf::from_probs: device time of the kernel (CUDA events, L2
+    flushed before each launch), end to end through the host-buffer C ABI in encoder mode (logits in,
+    {symbol, low, high} out), a bit-exactness check against the C oracle, and the oracle on all host
+    cores.  Seeded synthetic logits N(0, 3^2), the spread of a trained LM's logits."""
+    import torch
+    from redukt_b200.plugin import BackendResult
+    rng = np.random.default_rng(2024)
+    x = (rng.standard_normal((n, vocab)) * 3).astype(np.float32)
+    d_x = torch.from_numpy(x).to(dev)
+    d_c = torch.empty((n, vocab + 1), dtype=torch.int32, device=dev)
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def call():
+        rc = lib.cdf_device(d_x.data_ptr(), n, vocab, vocab, d_c.data_ptr(), vocab + 1, stream=st.cuda_stream)
+        assert rc == BackendResult.OK, lib.last_error()
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(reps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        call()
+        e1.record(st)
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    ms = sorted(a.elapsed_time(b) for a, b in evs)[reps // 2]
+    from oracle import oracle as O
+    got = d_c.cpu().numpy().view(np.uint32)
+    k = min(n, 4)
+    exact = bool(np.array_equal(got[:k], O.cdf_from_logits(x[:k])))
+
+    sym = rng.integers(0, vocab, n).astype(np.uint32)
+    for _ in range(3):
+        lib.cdf(x, symbols=sym, want_cdf=False)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        _, q = lib.cdf(x, symbols=sym, want_cdf=False)
+    e2e_s = (time.perf_counter() - t0) / reps
+    bytes_per_row = vocab * 4 + (vocab + 1) * 4
+    out = {"rows": n, "vocab": vocab, "kernel_ms": round(ms, 4), "rows_per_s": round(n / (ms / 1e3), 1),
+           "e2e_rows_per_s": round(n / e2e_s, 1), "e2e": "host logits in, {symbol, cdf[symbol], cdf[symbol+1]} out",
+           "h2d_bytes_per_call": n * vocab * 4 + n * 4, "d2h_bytes_per_call": n * 12,
+           "gpu_launches_per_call": 1, "bit_exact_vs_oracle_rows": k if exact else -1,
+           "bound": "latency: two exact binary64 index-order sums per row as binade-blocked scan rounds",
+           "algorithmic_bytes": n * bytes_per_row,
+           "achieved_gbs": round(n * bytes_per_row / (ms / 1e3) / 1e9, 1)}
+    if with_cpu:
+        thr = os.cpu_count() or 1
+        rows = min(max(n, 2 * thr), 512)
+        xs = np.resize(x, (rows, vocab))
+        O.cdf_from_logits(xs[:thr], threads=thr)
+        t0 = time.perf_counter()
+        calls = 0
+        while calls < 2 or time.perf_counter() - t0 < 3.0:
+            O.cdf_from_logits(xs, threads=thr)
+            calls += 1
+        dt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": round(rows * calls / dt, 1), "unit": "rows/s", "cores": thr, "kind": "port",
+                               "sample": f"{calls} x {rows} rows of {vocab} logits ({dt:.1f} s), "
+                                         f"oracle/cdf_oracle.c (scalar, one row per thread)"}
+    return out
+
+
+def run_profile_cdf(n: int) -> None:
+    """Small case for ncu captures of the CDF kernel: two launches over n rows of 50,280 logits."""
+    import torch
+    from redukt_b200.plugin import BackendResult, PluginLibrary
+    lib = PluginLibrary()
+    V = rbin.MAMBA_130M.vocab
+    x = (torch.randn((n, V), generator=torch.Generator().manual_seed(1)) * 3).cuda()
+    c = torch.empty((n, V + 1), dtype=torch.int32, device="cuda")
+    for _ in range(2):
+        assert lib.cdf_device(x.data_ptr(), n, V, V, c.data_ptr(), V + 1) == BackendResult.OK, lib.last_error()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_cdf": n, "vocab": V, "launches": 2}))
+
+
 def run_profile_case(n: int, quant: str = "q8", fused: int = 1) -> None:
     """Small case for ncu captures: two eager (graph-free) steps of n streams through the C ABI.
     quant "rwkv7" runs the RWKV-7 0.1B W8A8 model instead of Mamba-130M; fused 0 runs the Mamba
@@ -506,7 +590,13 @@ def main():
     ap.add_argument("--profile-quant", default="q8", choices=["q8", "f32", "rwkv7"])
     ap.add_argument("--profile-fused", type=int, default=1, choices=[0, 1],
                     help="0: the per-kernel Mamba step even at n <= 32")
+    ap.add_argument("--no-cdf", action="store_true", help="skip the coder-CDF measurement")
+    ap.add_argument("--profile-cdf", type=int, default=0,
+                    help="run two launches of the CDF kernel over N rows and exit (small case for ncu)")
     args = ap.parse_args()
+    if args.profile_cdf:
+        run_profile_cdf(args.profile_cdf)
+        return
     if args.profile_case:
         run_profile_case(args.profile_case, args.profile_quant, args.profile_fused)
         return
