@@ -39,6 +39,10 @@ constexpr int kPer = 8;                       // consecutive terms per thread in
 constexpr int kChunk = kThreads * kPer;       // 4096 terms per scan round
 constexpr int kWarps = kThreads / 32;
 constexpr uint32_t kTotal = 1u << 24;         // coder.rs:12 (TOP)
+// The first kHead terms of each sum are added one by one by a single thread: there the running
+// sum is still small and crosses a binade every few terms, and each crossing would cost a scan
+// round over the whole chunk.
+constexpr int kHead = 512;
 
 __device__ __forceinline__ double dbits(uint64_t u) { return __longlong_as_double((long long)u); }
 __device__ __forceinline__ uint64_t bitsd(double x) { return (uint64_t)__double_as_longlong(x); }
@@ -119,6 +123,8 @@ struct Smem {
     float wmax[kWarps];
     double xv;                 // the term at the first break of a scan round
     unsigned long long pbefore;  // rounded partial sum (units of u) just before it
+    double head[kHead];        // the first kHead terms of a sum, added by one thread
+    double hs;
 };
 
 // Exclusive block scan of one u64 per thread; returns the thread's offset, total in *tot.
@@ -228,9 +234,8 @@ __device__ __forceinline__ PMap block_scan_maps(const PMap& v, Smem& sm, PMap* a
 // Adds this thread's kPer terms x[] (chunk-local indices threadIdx.x * kPer + k, in order
 // across the block) to the block-uniform running sum s, exactly as the sequential loop
 // `for x in chunk { s += x }` would.  Terms must be >= 0 or NaN.
-__device__ void chain_chunk(const double (&x)[kPer], double& s, Smem& sm) {
+__device__ void chain_chunk(const double (&x)[kPer], double& s, Smem& sm, int pos = 0) {
     const int j0 = threadIdx.x * kPer;
-    int pos = 0;
     while (pos < kChunk) {
         if (s != s) return;                          // NaN absorbs the rest
         const bool zero = s == 0.0;
@@ -244,67 +249,78 @@ __device__ void chain_chunk(const double (&x)[kPer], double& s, Smem& sm) {
             su = (unsigned long long)__dmul_rn(s, up);     // s / u, an integer in [2^52, 2^53)
             thr = (1ull << 53) - su;
         }
-        // per term: increment for running parity 0 / 1 (ties round to even), or a break
-        unsigned long long i0[kPer], i1[kPer];
-        bool brk[kPer];
-        bool any_tie = false;
-        PMap mine = pm_identity();
+        // per term: the increment in units of u (f, or f + 1 past a half), with a tie flag and
+        // the parity of f, or a break
+        unsigned long long inc[kPer];
+        uint32_t brk = 0, tie = 0, odd = 0;            // bit k: term k
+        const bool live = j0 + kPer > pos;             // has terms at or after pos
+        unsigned long long mine = 0;
 #pragma unroll
         for (int k = 0; k < kPer; k++) {
             const int j = j0 + k;
-            i0[k] = i1[k] = 0;
-            brk[k] = false;
-            if (j >= pos) {
+            inc[k] = 0;
+            if (live && j >= pos) {
                 if (zero || tiny) {
-                    brk[k] = x[k] != 0.0;                  // s + 0 = s: zeros never break
+                    if (x[k] != 0.0) brk |= 1u << k;      // s + 0 = s: zeros never break
                 } else {
                     const double t = __dmul_rn(x[k], up);  // exact: scaling by a power of two
                     if (!(t < 0x1p53)) {                   // leaves the binade on its own (or NaN)
-                        i0[k] = i1[k] = 1ull << 53;
-                        brk[k] = true;
+                        inc[k] = 1ull << 53;
+                        brk |= 1u << k;
                     } else {
                         const double f = floor(t);
                         const double fr = __dsub_rn(t, f);   // exact
                         const unsigned long long fi = (unsigned long long)f;
-                        const unsigned long long up1 = fr > 0.5 ? 1ull : 0ull;
-                        const bool tie = fr == 0.5;
-                        any_tie |= tie;
-                        const unsigned long long odd = fi & 1ull;
-                        i0[k] = fi + up1 + (tie && odd ? 1ull : 0ull);    // running sum even
-                        i1[k] = fi + up1 + (tie && !odd ? 1ull : 0ull);   // running sum odd
+                        inc[k] = fi + (fr > 0.5 ? 1ull : 0ull);
+                        if (fr == 0.5) tie |= 1u << k;
+                        odd |= (uint32_t)(fi & 1ull) << k;
                     }
                 }
             }
-            const PMap m = {i0[k], i1[k], (uint32_t)(i0[k] & 1ull) | (uint32_t)(((1ull + i1[k]) & 1ull) << 1)};
-            mine = pm_then(mine, m);
+            mine += inc[k];
         }
+        // a tie adds one more unit when the running sum would otherwise end odd: for running
+        // parity 0 when f is odd, for parity 1 when f is even
         const uint32_t p_start = (uint32_t)(su & 1ull);
         unsigned long long run, total;
-        uint32_t par;
-        if (__syncthreads_or(any_tie)) {
+        uint32_t par = 0;
+        const bool ties = __syncthreads_or(tie != 0);
+        if (ties) {
+            PMap m_all = pm_identity();
+#pragma unroll
+            for (int k = 0; k < kPer; k++) {
+                if (!live) break;
+                const unsigned long long a0 = inc[k] + ((tie & odd) >> k & 1u);
+                const unsigned long long a1 = inc[k] + ((tie & ~odd) >> k & 1u);
+                const PMap m = {a0, a1, (uint32_t)(a0 & 1ull) | (uint32_t)(((1ull + a1) & 1ull) << 1)};
+                m_all = pm_then(m_all, m);
+            }
             PMap all;
-            const PMap pre = block_scan_maps(mine, sm, &all);
+            const PMap pre = block_scan_maps(m_all, sm, &all);
             run = p_start ? pre.i1 : pre.i0;          // units of u added before this thread
             par = (pre.par >> p_start) & 1u;
             total = p_start ? all.i1 : all.i0;
         } else {                                       // no tie: increments do not depend on parity
-            run = block_scan(mine.i0, sm, &total);
-            par = 0;                                   // unused: i0 == i1 for every term
+            run = block_scan(mine, sm, &total);
         }
         int first = kChunk;
         double my_x = 0.0;
         unsigned long long my_pb = 0;
+        if (live) {
 #pragma unroll
-        for (int k = 0; k < kPer; k++) {
-            const int j = j0 + k;
-            const unsigned long long pb = run;
-            run += par ? i1[k] : i0[k];
-            par = (uint32_t)((par + (par ? i1[k] : i0[k])) & 1ull);
-            const bool over = !zero && !tiny && run >= thr;
-            if (first == kChunk && j >= pos && (brk[k] || over)) {
-                first = j;
-                my_x = x[k];
-                my_pb = pb;
+            for (int k = 0; k < kPer; k++) {
+                const int j = j0 + k;
+                const unsigned long long pb = run;
+                const unsigned long long d =
+                    inc[k] + ((tie >> k) & 1u & (((odd >> k) & 1u) ^ par));   // tie: even result
+                run += d;
+                par = (uint32_t)((par + d) & 1ull);
+                const bool over = !zero && !tiny && run >= thr;
+                if (first == kChunk && j >= pos && (((brk >> k) & 1u) || over)) {
+                    first = j;
+                    my_x = x[k];
+                    my_pb = pb;
+                }
             }
         }
         const int fb = block_min(first, sm);
@@ -323,6 +339,26 @@ __device__ void chain_chunk(const double (&x)[kPer], double& s, Smem& sm) {
         s = __dadd_rn(s, sm.xv);
         pos = fb + 1;
     }
+}
+
+// Adds the chunk's first kHead terms to s (block-uniform) one by one, as the sequential loop
+// would; the caller continues the chunk at kHead.
+__device__ __forceinline__ void add_head(const double (&x)[kPer], double& s, Smem& sm) {
+#pragma unroll
+    for (int k = 0; k < kPer; k++) {
+        const int j = threadIdx.x * kPer + k;
+        if (j < kHead) sm.head[j] = x[k];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double a = s;
+#pragma unroll 16
+        for (int j = 0; j < kHead; j++) a = __dadd_rn(a, sm.head[j]);
+        sm.hs = a;
+    }
+    __syncthreads();
+    s = sm.hs;
+    __syncthreads();   // sm.hs and sm.head are free again
 }
 
 // One CTA per row.  cdf row: vocab + 1 words (cdf[0] = 0, cdf[vocab] = 2^24); it is also the
@@ -362,7 +398,8 @@ k_cdf_rows(const float* __restrict__ logits, int vocab, int ld_logits, uint32_t*
             const int i = base + tid * kPer + k;
             x[k] = i < vocab ? exp_f64(__dsub_rn((double)__ldg(L + i), max_l), sm.tab) : 0.0;
         }
-        chain_chunk(x, s, sm);
+        if (base == 0) add_head(x, s, sm);
+        chain_chunk(x, s, sm, base == 0 ? kHead : 0);
     }
     const double inv_sum = __ddiv_rn(1.0, s);
 
@@ -382,7 +419,8 @@ k_cdf_rows(const float* __restrict__ logits, int vocab, int ld_logits, uint32_t*
                 x[k] = 0.0;
             }
         }
-        chain_chunk(x, sp, sm);
+        if (base == 0) add_head(x, sp, sm);
+        chain_chunk(x, sp, sm, base == 0 ? kHead : 0);
     }
 
     // freqs = 1 + round(p * inv * remaining) (coder.rs:53-63); extra_used; last maximum
