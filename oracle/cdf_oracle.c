@@ -182,6 +182,16 @@ int orc_cdf_from_logits(const float* logits, uint32_t n_rows, uint32_t vocab, ui
     return rc;
 }
 
+/* coder.rs:43-82 on caller probabilities (the reference's coder unit tests build CDFs this way). */
+int orc_cdf_from_probs(const float* probs, uint32_t v, uint32_t* cdf) {
+    if (v == 0 || v >= (1u << 24)) return -1;
+    uint32_t* freqs = (uint32_t*)malloc((size_t)v * sizeof(uint32_t));
+    if (!freqs) return -1;
+    cdf_from_probs_row(probs, v, freqs, cdf);
+    free(freqs);
+    return 0;
+}
+
 /* coder.rs:100-114: the symbol whose interval holds cum_freq (binary search, lowest match). */
 uint32_t orc_cdf_lookup(const uint32_t* cdf, uint32_t vocab, uint32_t cum_freq) {
     uint32_t lo = 0, hi = vocab;

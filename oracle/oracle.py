@@ -61,6 +61,7 @@ def lib() -> ctypes.CDLL:
         L.orc_exp_f64.argtypes, L.orc_exp_f64.restype = [ctypes.c_double], ctypes.c_double
         L.orc_cdf_from_logits.argtypes, L.orc_cdf_from_logits.restype = [vp, u32, u32, u32, vp, u32, i32], i32
         L.orc_cdf_lookup.argtypes, L.orc_cdf_lookup.restype = [vp, u32, u32], u32
+        L.orc_cdf_from_probs.argtypes, L.orc_cdf_from_probs.restype = [vp, u32, vp], i32
         _lib = L
     return _lib
 
@@ -94,6 +95,15 @@ def cdf_from_logits(logits: np.ndarray, threads: int = 1) -> np.ndarray:
     out = np.empty((n, v + 1), dtype=np.uint32)
     if lib().orc_cdf_from_logits(_p(x), n, v, v, _p(out), v + 1, int(threads)) != 0:
         raise ValueError(f"cdf_from_logits: invalid shape {x.shape}")
+    return out
+
+
+def cdf_from_probs(probs: np.ndarray) -> np.ndarray:
+    """`Cdf::from_probs` (coder.rs:43-82) of one row of f32 probabilities -> vocab+1 uint32 entries."""
+    p = np.ascontiguousarray(probs, dtype=np.float32).reshape(-1)
+    out = np.empty(p.shape[0] + 1, dtype=np.uint32)
+    if lib().orc_cdf_from_probs(_p(p), p.shape[0], _p(out)) != 0:
+        raise ValueError(f"cdf_from_probs: invalid length {p.shape[0]}")
     return out
 
 

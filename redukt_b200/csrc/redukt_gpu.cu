@@ -1588,7 +1588,20 @@ int32_t redukt_b200_cdf_device(const float* d_logits, uint32_t n_rows, uint32_t 
     }
     if (n_rows == 0) return BACKEND_OK;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(cuda_stream);
-    cdf::k_cdf_rows<<<n_rows, cdf::kThreads, 0, st>>>(d_logits, (int)vocab, (int)ld_logits, d_cdf, (int)ld_cdf,
+    const size_t dyn = cdf::cdf_dyn_smem((int)vocab);
+    if (dyn > 0) {   // per device, the attribute is set once
+        static std::mutex mu;
+        static bool done[kNoAllocMaxDevices] = {};
+        int dev = 0;
+        CK(cudaGetDevice(&dev), BACKEND_FORWARD_FAILED);
+        std::lock_guard<std::mutex> lock(mu);
+        if (dev >= 0 && dev < kNoAllocMaxDevices && !done[dev]) {
+            CK(cudaFuncSetAttribute(cdf::k_cdf_rows, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)cdf::cdf_dyn_smem(cdf::kSmemVocab)), BACKEND_FORWARD_FAILED);
+            done[dev] = true;
+        }
+    }
+    cdf::k_cdf_rows<<<n_rows, cdf::kThreads, dyn, st>>>(d_logits, (int)vocab, (int)ld_logits, d_cdf, (int)ld_cdf,
                                                        d_symbols, d_cum_freqs,
                                                        (d_symbols || d_cum_freqs) ? d_query_out : nullptr);
     CK(cudaGetLastError(), BACKEND_FORWARD_FAILED);

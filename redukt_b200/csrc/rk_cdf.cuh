@@ -43,6 +43,10 @@ constexpr uint32_t kTotal = 1u << 24;         // coder.rs:12 (TOP)
 // sum is still small and crosses a binade every few terms, and each crossing would cost a scan
 // round over the whole chunk.
 constexpr int kHead = 512;
+// Rows of up to this many logits keep their per-symbol workspace (f32 probabilities, then
+// frequencies) in dynamic shared memory; longer rows use the output row itself.
+constexpr int kSmemVocab = 53248;   // 208 KB
+static_assert(kPer == 8, "the shared-workspace paths move kPer words as two 16-byte vectors");
 
 __device__ __forceinline__ double dbits(uint64_t u) { return __longlong_as_double((long long)u); }
 __device__ __forceinline__ uint64_t bitsd(double x) { return (uint64_t)__double_as_longlong(x); }
@@ -361,8 +365,9 @@ __device__ __forceinline__ void add_head(const double (&x)[kPer], double& s, Sme
     __syncthreads();   // sm.hs and sm.head are free again
 }
 
-// One CTA per row.  cdf row: vocab + 1 words (cdf[0] = 0, cdf[vocab] = 2^24); it is also the
-// row's workspace.  Optional per-row queries, three words each in q_out:
+// One CTA per row.  cdf row: vocab + 1 words (cdf[0] = 0, cdf[vocab] = 2^24); rows longer than
+// kSmemVocab also use it as their workspace.  Launch with vocab * 4 bytes of dynamic shared memory
+// when vocab <= kSmemVocab (cdf_dyn_smem).  Optional per-row queries, three words each in q_out:
 //   symbols  (encoder): {symbol, cdf[symbol], cdf[symbol + 1]}, or {symbol, ~0u, ~0u} when
 //                       symbol >= vocab;
 //   cum_freqs (decoder): {lookup(cum), cdf[sym], cdf[sym + 1]} with Cdf::lookup's binary search;
@@ -372,9 +377,11 @@ k_cdf_rows(const float* __restrict__ logits, int vocab, int ld_logits, uint32_t*
            int ld_cdf, const uint32_t* __restrict__ symbols, const uint32_t* __restrict__ cum_freqs,
            uint32_t* __restrict__ q_out) {
     __shared__ Smem sm;
+    extern __shared__ __align__(16) uint32_t dyn_ws[];
     const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const float* L = logits + (size_t)row * ld_logits;
     uint32_t* c = cdf_all + (size_t)row * ld_cdf;
+    uint32_t* ws = vocab <= kSmemVocab ? dyn_ws : c + 1;   // ws[i]: symbol i's probability, then frequency
     for (int i = tid; i < 256; i += kThreads) sm.tab[i] = g_exp_tab[i];
 
     // max_l = fold(-inf, f64::max): f32 max is the same value, NaN ignored (codec.rs:787)
@@ -403,21 +410,33 @@ k_cdf_rows(const float* __restrict__ logits, int vocab, int ld_logits, uint32_t*
     }
     const double inv_sum = __ddiv_rn(1.0, s);
 
-    // p = (e * inv_sum) as f32 (codec.rs:795), kept in cdf[i + 1]; sum_p in index order (coder.rs:52)
+    // p = (e * inv_sum) as f32 (codec.rs:795), kept in ws; sum_p in index order (coder.rs:52)
+    const bool vec = ws == dyn_ws;   // shared workspace: 16-byte aligned, kPer words per thread at once
     double sp = 0.0;
     for (int base = 0; base < vocab; base += kChunk) {
         double x[kPer];
+        uint32_t pb[kPer];
+        const int i0 = base + tid * kPer;
 #pragma unroll
         for (int k = 0; k < kPer; k++) {
-            const int i = base + tid * kPer + k;
+            const int i = i0 + k;
+            pb[k] = 0;
             if (i < vocab) {
                 const double e = exp_f64(__dsub_rn((double)__ldg(L + i), max_l), sm.tab);
                 const float p = __double2float_rn(__dmul_rn(e, inv_sum));
-                c[i + 1] = __float_as_uint(p);
+                pb[k] = __float_as_uint(p);
                 x[k] = (double)p;
             } else {
                 x[k] = 0.0;
             }
+        }
+        if (vec && i0 + kPer <= vocab) {
+            reinterpret_cast<uint4*>(ws + i0)[0] = make_uint4(pb[0], pb[1], pb[2], pb[3]);
+            reinterpret_cast<uint4*>(ws + i0)[1] = make_uint4(pb[4], pb[5], pb[6], pb[7]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < kPer; k++)
+                if (i0 + k < vocab) ws[i0 + k] = pb[k];
         }
         if (base == 0) add_head(x, sp, sm);
         chain_chunk(x, sp, sm, base == 0 ? kHead : 0);
@@ -431,12 +450,12 @@ k_cdf_rows(const float* __restrict__ logits, int vocab, int ld_logits, uint32_t*
     uint32_t best_f = 0;
     int best_i = -1;
     for (int i = tid; i < vocab; i += kThreads) {
-        const float p = __uint_as_float(c[i + 1]);
+        const float p = __uint_as_float(ws[i]);
         const double t = __dadd_rn(__dmul_rn(__dmul_rn((double)p, inv), rem_d), 0.5);
         unsigned long long extra = 0;
         if (t == t && t > 0.0) extra = t >= 0x1p64 ? ~0ull : __double2ull_rz(t);   // Rust `as u64`
         const uint32_t f = 1u + (uint32_t)extra;
-        c[i + 1] = f;
+        ws[i] = f;
         used += extra;
         if (f >= best_f) { best_f = f; best_i = i; }   // i increases: ties keep the later index
     }
@@ -458,7 +477,7 @@ k_cdf_rows(const float* __restrict__ logits, int vocab, int ld_logits, uint32_t*
             if (sm.wfreq[i] > bf || (sm.wfreq[i] == bf && sm.widx[i] > bi)) { bf = sm.wfreq[i]; bi = sm.widx[i]; }
         }
         const long long diff = (long long)remaining - (long long)u_all;   // coder.rs:66-72
-        if (diff != 0 && bi >= 0) c[bi + 1] = (uint32_t)((long long)bf + diff);
+        if (diff != 0 && bi >= 0) ws[bi] = (uint32_t)((long long)bf + diff);
         c[0] = 0;
     }
     __syncthreads();
@@ -468,10 +487,17 @@ k_cdf_rows(const float* __restrict__ logits, int vocab, int ld_logits, uint32_t*
     for (int base = 0; base < vocab; base += kChunk) {
         uint32_t f[kPer];
         uint32_t acc = 0;
+        const int i0 = base + tid * kPer;
+        if (vec && i0 + kPer <= vocab) {
+            const uint4 a = reinterpret_cast<const uint4*>(ws + i0)[0];
+            const uint4 b = reinterpret_cast<const uint4*>(ws + i0)[1];
+            f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+        } else {
+#pragma unroll
+            for (int k = 0; k < kPer; k++) f[k] = i0 + k < vocab ? ws[i0 + k] : 0u;
+        }
 #pragma unroll
         for (int k = 0; k < kPer; k++) {
-            const int i = base + tid * kPer + k;
-            f[k] = i < vocab ? c[i + 1] : 0u;
             acc += f[k];
             f[k] = acc;
         }
@@ -505,6 +531,10 @@ k_cdf_rows(const float* __restrict__ logits, int vocab, int ld_logits, uint32_t*
         q[1] = lo < (uint32_t)vocab ? c[lo] : ~0u;
         q[2] = lo < (uint32_t)vocab ? c[lo + 1] : ~0u;
     }
+}
+
+__host__ __device__ constexpr size_t cdf_dyn_smem(int vocab) {
+    return vocab <= kSmemVocab ? (size_t)vocab * sizeof(uint32_t) : 0;
 }
 
 }  // namespace cdf

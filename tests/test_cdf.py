@@ -9,7 +9,9 @@ CPU tests pin the oracle: its exp against the reference's golden bit patterns
 (src/domain/fmath.rs:525-550, extracted by golden/make_exp_golden.py), its CDF against a
 pure-Python restatement on small rows, and the exactness argument of the device kernel's
 binade-blocked summation against plain sequential summation.  GPU tests compare the kernel with the
-oracle on ragged, masked, peaked, flat and full-size rows, and the encoder / decoder queries.
+oracle on ragged, masked, peaked, flat and full-size rows (rows of up to 53,248 logits keep their
+workspace in shared memory, longer ones in the output row: both sides of that limit are covered),
+and the encoder / decoder queries.
 """
 import json
 import math
@@ -219,7 +221,7 @@ def _rows(v: int, seed: int) -> np.ndarray:
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("vocab", [50280, 4096, 4097, 1000, 3, 1])
+@pytest.mark.parametrize("vocab", [50280, 4096, 4097, 1000, 3, 1, 53248, 53249, 65536])
 def test_device_cdf_bit_identical_to_oracle(vocab):
     from redukt_b200.plugin import PluginLibrary
 
