@@ -320,10 +320,11 @@ def run_b200(args, rank, world, local, dist):
                        "algorithmic_bytes_per_launch": kd["bytes_per_launch"], "peak_source": peaks["source"]}
     res["kernels"] = kernels
 
+    if world == 1 and not args.no_cdf:   # before the sweep, which replaces the loaded model
+        res["coder_cdf"] = coder_cdf(b.libobj, n, V, dev, with_cpu=rank == 0 and not args.no_cpu_baseline,
+                                     backend=b, windows=windows)
     if world == 1 and not args.no_sweep:
         res["sweep"] = sweep(b, f32_path, q8_path, dims, args, dev, peaks)
-    if world == 1 and not args.no_cdf:
-        res["coder_cdf"] = coder_cdf(b.libobj, n, V, dev, with_cpu=rank == 0 and not args.no_cpu_baseline)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         b.close()
         res["cpu_baseline"] = cpu_baseline(q8_path, n, args.cpu_seconds)
@@ -464,7 +465,7 @@ def run_reference(args, rank, world):
             "e2e": {"value": round(v, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
-def coder_cdf(lib, n: int, vocab: int, dev, with_cpu: bool, reps: int = 20) -> dict:
+def coder_cdf(lib, n: int, vocab: int, dev, with_cpu: bool, reps: int = 20, backend=None, windows=None) -> dict:
     """The coder's 24-bit CDF for the step's n rows (redukt_b200_cdf_device), the reference's
     cdf_from_logits_with(.., FmathV1) + Cdf::from_probs: device time of the kernel (CUDA events, L2
     flushed before each launch), end to end through the host-buffer C ABI in encoder mode (logits in,
@@ -508,6 +509,21 @@ def coder_cdf(lib, n: int, vocab: int, dev, with_cpu: bool, reps: int = 20) -> d
         _, q = lib.cdf(x, symbols=sym, want_cdf=False)
     e2e_s = (time.perf_counter() - t0) / reps
     bytes_per_row = vocab * 4 + (vocab + 1) * 4
+    step_cdf = None
+    if backend is not None:
+        # the coder's view of a step: redukt_b200_forward_batch_cdf in encoder mode (tokens and next
+        # symbols in, {symbol, low, high} out: the step and the CDF on the device, 12 bytes per stream back)
+        slots = list(range(n))
+        T = windows.shape[1]
+        for i in range(3):
+            backend.forward_batch_cdf(slots, windows[:, i % T], symbols=windows[:, (i + 1) % T])
+        t0 = time.perf_counter()
+        for i in range(reps):
+            backend.forward_batch_cdf(slots, windows[:, (3 + i) % T], symbols=windows[:, (4 + i) % T])
+        dt = (time.perf_counter() - t0) / reps
+        step_cdf = {"value": round(n / dt, 1), "unit": "tok/s", "ms_per_step": round(dt * 1e3, 4),
+                    "h2d_bytes_per_step": n * 12, "d2h_bytes_per_step": n * 12,
+                    "what": "redukt_b200_forward_batch_cdf: step + coder CDF on the device, encoder queries back"}
     out = {"rows": n, "vocab": vocab, "kernel_ms": round(ms, 4), "rows_per_s": round(n / (ms / 1e3), 1),
            "e2e_rows_per_s": round(n / e2e_s, 1), "e2e": "host logits in, {symbol, cdf[symbol], cdf[symbol+1]} out",
            "h2d_bytes_per_call": n * vocab * 4 + n * 4, "d2h_bytes_per_call": n * 12,
@@ -515,6 +531,8 @@ def coder_cdf(lib, n: int, vocab: int, dev, with_cpu: bool, reps: int = 20) -> d
            "bound": "latency: two exact binary64 index-order sums per row as binade-blocked scan rounds",
            "algorithmic_bytes": n * bytes_per_row,
            "achieved_gbs": round(n * bytes_per_row / (ms / 1e3) / 1e9, 1)}
+    if step_cdf is not None:
+        out["e2e_step_and_cdf"] = step_cdf
     if with_cpu:
         thr = os.cpu_count() or 1
         rows = min(max(n, 2 * thr), 512)

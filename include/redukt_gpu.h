@@ -206,6 +206,18 @@ int32_t redukt_b200_cdf_device(const float* d_logits, uint32_t n_rows, uint32_t 
 int32_t redukt_b200_cdf(const float* logits, uint32_t n_rows, uint32_t vocab, uint32_t* cdf_out,
                         const uint32_t* symbols, const uint32_t* cum_freqs, uint32_t* query_out);
 
+/* One lockstep step followed by the coder CDF of its logits, all on the device, with only the
+ * coder's words coming back: forward_batch's slots/tokens (checked on the host, as forward_batch
+ * does), then per stream r the query of redukt_b200_cdf_device on that step's logits row:
+ * symbols[r] (encoder) or cum_freqs[r] (decoder) -> query_out[3r..3r+2].  cdf_out (NULL, or
+ * n_streams x (vocab + 1)) also returns the whole tables; with neither query it is required.
+ * This replaces forward_batch + the host's cdf_from_logits for each stream
+ * (src/application/lockstep.rs:297-337, without the host CM ensemble): 12 bytes per stream come
+ * back instead of vocab logits.  Synchronous, on the library's stream. */
+int32_t redukt_b200_forward_batch_cdf(uint32_t n_streams, const uint32_t* slots, const uint32_t* tokens,
+                                      const uint32_t* symbols, const uint32_t* cum_freqs, uint32_t* query_out,
+                                      uint32_t* cdf_out);
+
 /* Last error message of this library (empty string when none). */
 const char* redukt_b200_last_error(void);
 

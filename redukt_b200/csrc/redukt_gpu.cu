@@ -1097,9 +1097,51 @@ struct CdfHostBuffers {
     uint32_t* cdf = nullptr;
     uint32_t* query_in = nullptr;
     uint32_t* query_out = nullptr;
+    uint32_t* slots = nullptr;    // forward_batch_cdf: the step's slots and tokens
+    uint32_t* tokens = nullptr;
+    uint32_t* h_err = nullptr;    // pinned copy of the engine's device error word
     size_t logit_cap = 0, cdf_cap = 0, row_cap = 0;
 };
 CdfHostBuffers g_cdf_host;
+
+// Grows the host entry points' device buffers to n_rows rows of vocab logits; caller holds B.mu.
+int32_t cdf_buffers(uint32_t n_rows, uint32_t vocab) {
+    CdfHostBuffers& B = g_cdf_host;
+    int dev = 0;
+    CK(cudaGetDevice(&dev), BACKEND_FORWARD_FAILED);
+    if (B.device != dev) {   // buffers belong to one device: start over on another
+        if (B.stream) { cudaStreamDestroy(B.stream); B.stream = nullptr; }
+        cudaFree(B.logits); cudaFree(B.cdf); cudaFree(B.query_in); cudaFree(B.query_out);
+        cudaFree(B.slots); cudaFree(B.tokens);
+        B.logits = nullptr; B.cdf = nullptr; B.query_in = B.query_out = nullptr;
+        B.slots = B.tokens = nullptr;
+        B.logit_cap = B.cdf_cap = B.row_cap = 0;
+        B.device = dev;
+        CK(cudaStreamCreateWithFlags(&B.stream, cudaStreamNonBlocking), BACKEND_FORWARD_FAILED);
+    }
+    const size_t nl = (size_t)n_rows * vocab, nc = (size_t)n_rows * (vocab + 1);
+    if (nl > B.logit_cap) {
+        cudaFree(B.logits); B.logits = nullptr; B.logit_cap = 0;
+        CK(cudaMalloc(&B.logits, nl * sizeof(float)), BACKEND_FORWARD_FAILED);
+        B.logit_cap = nl;
+    }
+    if (nc > B.cdf_cap) {
+        cudaFree(B.cdf); B.cdf = nullptr; B.cdf_cap = 0;
+        CK(cudaMalloc(&B.cdf, nc * sizeof(uint32_t)), BACKEND_FORWARD_FAILED);
+        B.cdf_cap = nc;
+    }
+    if (n_rows > B.row_cap) {
+        cudaFree(B.query_in); cudaFree(B.query_out); cudaFree(B.slots); cudaFree(B.tokens);
+        B.query_in = B.query_out = B.slots = B.tokens = nullptr;
+        B.row_cap = 0;
+        CK(cudaMalloc(&B.query_in, (size_t)n_rows * sizeof(uint32_t)), BACKEND_FORWARD_FAILED);
+        CK(cudaMalloc(&B.query_out, (size_t)n_rows * 3 * sizeof(uint32_t)), BACKEND_FORWARD_FAILED);
+        CK(cudaMalloc(&B.slots, (size_t)n_rows * sizeof(uint32_t)), BACKEND_FORWARD_FAILED);
+        CK(cudaMalloc(&B.tokens, (size_t)n_rows * sizeof(uint32_t)), BACKEND_FORWARD_FAILED);
+        B.row_cap = n_rows;
+    }
+    return BACKEND_OK;
+}
 
 int32_t check_cdf_args(uint32_t n_rows, uint32_t vocab, uint32_t ld_logits, uint32_t ld_cdf) {
     if (vocab == 0 || vocab >= cdf::kTotal) {
@@ -1617,33 +1659,8 @@ int32_t redukt_b200_cdf(const float* logits, uint32_t n_rows, uint32_t vocab, ui
     if (n_rows == 0) return BACKEND_OK;
     CdfHostBuffers& B = g_cdf_host;
     std::lock_guard<std::mutex> lock(B.mu);
-    int dev = 0;
-    CK(cudaGetDevice(&dev), BACKEND_FORWARD_FAILED);
-    if (B.device != dev) {   // buffers belong to one device: start over on another
-        if (B.stream) { cudaStreamDestroy(B.stream); B.stream = nullptr; }
-        cudaFree(B.logits); cudaFree(B.cdf); cudaFree(B.query_in); cudaFree(B.query_out);
-        B.logits = nullptr; B.cdf = nullptr; B.query_in = B.query_out = nullptr;
-        B.logit_cap = B.cdf_cap = B.row_cap = 0;
-        B.device = dev;
-        CK(cudaStreamCreateWithFlags(&B.stream, cudaStreamNonBlocking), BACKEND_FORWARD_FAILED);
-    }
+    if (int32_t rc = cdf_buffers(n_rows, vocab)) return rc;
     const size_t nl = (size_t)n_rows * vocab, nc = (size_t)n_rows * (vocab + 1);
-    if (nl > B.logit_cap) {
-        cudaFree(B.logits); B.logits = nullptr; B.logit_cap = 0;
-        CK(cudaMalloc(&B.logits, nl * sizeof(float)), BACKEND_FORWARD_FAILED);
-        B.logit_cap = nl;
-    }
-    if (nc > B.cdf_cap) {
-        cudaFree(B.cdf); B.cdf = nullptr; B.cdf_cap = 0;
-        CK(cudaMalloc(&B.cdf, nc * sizeof(uint32_t)), BACKEND_FORWARD_FAILED);
-        B.cdf_cap = nc;
-    }
-    if (n_rows > B.row_cap) {
-        cudaFree(B.query_in); cudaFree(B.query_out); B.query_in = B.query_out = nullptr; B.row_cap = 0;
-        CK(cudaMalloc(&B.query_in, (size_t)n_rows * sizeof(uint32_t)), BACKEND_FORWARD_FAILED);
-        CK(cudaMalloc(&B.query_out, (size_t)n_rows * 3 * sizeof(uint32_t)), BACKEND_FORWARD_FAILED);
-        B.row_cap = n_rows;
-    }
     CK(cudaMemcpyAsync(B.logits, logits, nl * sizeof(float), cudaMemcpyHostToDevice, B.stream), BACKEND_FORWARD_FAILED);
     if (query)
         CK(cudaMemcpyAsync(B.query_in, symbols ? symbols : cum_freqs, (size_t)n_rows * sizeof(uint32_t),
@@ -1658,6 +1675,55 @@ int32_t redukt_b200_cdf(const float* logits, uint32_t n_rows, uint32_t vocab, ui
         CK(cudaMemcpyAsync(query_out, B.query_out, (size_t)n_rows * 3 * sizeof(uint32_t), cudaMemcpyDeviceToHost,
                            B.stream), BACKEND_FORWARD_FAILED);
     CK(cudaStreamSynchronize(B.stream), BACKEND_FORWARD_FAILED);
+    return BACKEND_OK;
+}
+
+int32_t redukt_b200_forward_batch_cdf(uint32_t n, const uint32_t* slots, const uint32_t* tokens,
+                                      const uint32_t* symbols, const uint32_t* cum_freqs, uint32_t* query_out,
+                                      uint32_t* cdf_out) {
+    if (!G.ready || batch_cap() == 0) return BACKEND_INIT_FAILED;
+    if (n > batch_cap()) return BACKEND_INVALID_ARGUMENT;
+    if (n == 0) return BACKEND_OK;
+    const bool query = symbols || cum_freqs;
+    if (!slots || !tokens || (query && !query_out) || (symbols && cum_freqs) || (!query && !cdf_out))
+        return BACKEND_INVALID_ARGUMENT;
+    const uint32_t V = (uint32_t)G.V;
+    {   // the host path's checks (pool_forward): slots in the pool and distinct, tokens in the vocabulary
+        std::vector<uint8_t> seen(batch_cap(), 0);
+        for (uint32_t b = 0; b < n; b++) {
+            if (slots[b] >= batch_cap() || seen[slots[b]] || tokens[b] >= V) return BACKEND_INVALID_ARGUMENT;
+            seen[slots[b]] = 1;
+        }
+    }
+    CdfHostBuffers& B = g_cdf_host;
+    std::lock_guard<std::mutex> lock(B.mu);
+    CK(cudaSetDevice(G.device), BACKEND_FORWARD_FAILED);
+    if (int32_t rc = cdf_buffers(n, V)) return rc;
+    cudaStream_t st = G.stream;
+    const size_t ib = (size_t)n * sizeof(uint32_t);
+    CK(cudaMemcpyAsync(B.slots, slots, ib, cudaMemcpyHostToDevice, st), BACKEND_FORWARD_FAILED);
+    CK(cudaMemcpyAsync(B.tokens, tokens, ib, cudaMemcpyHostToDevice, st), BACKEND_FORWARD_FAILED);
+    if (query)
+        CK(cudaMemcpyAsync(B.query_in, symbols ? symbols : cum_freqs, ib, cudaMemcpyHostToDevice, st),
+           BACKEND_FORWARD_FAILED);
+    int32_t rc = redukt_b200_forward_batch_device(n, B.slots, B.tokens, B.logits, V, 0, st);
+    if (rc != BACKEND_OK) return rc;
+    rc = redukt_b200_cdf_device(B.logits, n, V, V, B.cdf, V + 1, symbols ? B.query_in : nullptr,
+                                cum_freqs ? B.query_in : nullptr, B.query_out, st);
+    if (rc != BACKEND_OK) return rc;
+    if (query)
+        CK(cudaMemcpyAsync(query_out, B.query_out, ib * 3, cudaMemcpyDeviceToHost, st), BACKEND_FORWARD_FAILED);
+    if (cdf_out)
+        CK(cudaMemcpyAsync(cdf_out, B.cdf, (size_t)n * (V + 1) * sizeof(uint32_t), cudaMemcpyDeviceToHost, st),
+           BACKEND_FORWARD_FAILED);
+    if (!B.h_err) CK(cudaMallocHost(&B.h_err, sizeof(uint32_t)), BACKEND_FORWARD_FAILED);
+    CK(cudaMemcpyAsync(B.h_err, G.d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, st), BACKEND_FORWARD_FAILED);
+    CK(cudaStreamSynchronize(st), BACKEND_FORWARD_FAILED);
+    if (*B.h_err) {
+        set_err("forward_batch_cdf: device error word 0x%x (2 = a tensor-core pipeline wait timed out)", *B.h_err);
+        cudaMemset(G.d_err, 0, sizeof(uint32_t));
+        return BACKEND_FORWARD_FAILED;
+    }
     return BACKEND_OK;
 }
 

@@ -34,7 +34,8 @@ EXT_SYMBOLS = ("redukt_backend_set_reset_every", "redukt_backend_forward_batch_p
                "redukt_b200_forward_batch_device", "redukt_b200_device_error", "redukt_b200_get_state",
                "redukt_b200_get_q8", "redukt_b200_info", "redukt_b200_set_option", "redukt_b200_kernel_times",
                "redukt_b200_time_kernel", "redukt_b200_softmax_noalloc", "redukt_b200_rwkv_get_state",
-               "redukt_b200_cdf_device", "redukt_b200_cdf", "redukt_b200_last_error")
+               "redukt_b200_cdf_device", "redukt_b200_cdf", "redukt_b200_forward_batch_cdf",
+               "redukt_b200_last_error")
 KERNEL_CLASSES = ("embed", "norm", "in_proj", "x_proj", "scan", "out_proj", "head", "softmax", "step")
 
 
@@ -143,6 +144,8 @@ class PluginLibrary:
             L.redukt_b200_cdf_device.restype = i32
             L.redukt_b200_cdf.argtypes = [f32p, u32, u32, u32p, u32p, u32p, u32p]
             L.redukt_b200_cdf.restype = i32
+            L.redukt_b200_forward_batch_cdf.argtypes = [u32, u32p, u32p, u32p, u32p, u32p, u32p]
+            L.redukt_b200_forward_batch_cdf.restype = i32
             L.redukt_b200_last_error.argtypes, L.redukt_b200_last_error.restype = [], ctypes.c_char_p
 
     def softmax_noalloc(self, d_logits: int, n_rows: int, vocab: int, d_probs: int, stream: int = 0) -> BackendResult:
@@ -281,6 +284,25 @@ class PluginBackend:
                             out: Optional[np.ndarray] = None) -> np.ndarray:
         return self._batch_call(self.lib.redukt_backend_forward_batch_probs, "redukt_backend_forward_batch_probs",
                                 slots, tokens, out, True)
+
+    def forward_batch_cdf(self, slots: Sequence[int], tokens: Sequence[int], symbols: Optional[Sequence[int]] = None,
+                          cum_freqs: Optional[Sequence[int]] = None, want_cdf: bool = False):
+        """One step, then the coder CDF of its logits on the device (redukt_b200_forward_batch_cdf):
+        returns (queries [n, 3] uint32 or None, cdf [n, vocab + 1] uint32 or None)."""
+        n = len(slots)
+        sl = np.ascontiguousarray(slots, dtype=np.uint32)
+        tk = np.ascontiguousarray(tokens, dtype=np.uint32)
+        qi = symbols if symbols is not None else cum_freqs
+        qi = None if qi is None else np.ascontiguousarray(qi, dtype=np.uint32)
+        q = np.empty((n, 3), dtype=np.uint32) if qi is not None else None
+        c = np.empty((n, self.vocab_size + 1), dtype=np.uint32) if want_cdf else None
+        ptr = (lambda a: _u32p(a) if a is not None else None)
+        code = BackendResult.from_code(self.lib.redukt_b200_forward_batch_cdf(
+            n, _u32p(sl), _u32p(tk), ptr(qi) if symbols is not None else None,
+            ptr(qi) if cum_freqs is not None else None, ptr(q), ptr(c)))
+        if code != BackendResult.OK:
+            raise PluginError("redukt_b200_forward_batch_cdf", code, self.libobj.last_error())
+        return q, c
 
     def set_reset_every(self, every: int) -> None:
         code = BackendResult.from_code(self.lib.redukt_backend_set_reset_every(every))

@@ -155,6 +155,44 @@ def _engine_decode(b, lib, archives, T):
     return out
 
 
+def _fused_encode(b, windows):
+    """_engine_encode through redukt_b200_forward_batch_cdf: the step and the CDF on the device,
+    12 bytes per stream back."""
+    n, T = windows.shape
+    cu = RC.uniform(b.vocab_size)
+    encs = [RC.RangeEncoder() for _ in range(n)]
+    for r in range(n):
+        s = int(windows[r, 0])
+        encs[r].encode(cu[0][s], cu[0][s + 1], cu[1])
+    slots = list(range(n))
+    b.batch_reset(slots)
+    for t in range(1, T):
+        q, _ = b.forward_batch_cdf(slots, windows[:, t - 1], symbols=windows[:, t])
+        for r in range(n):
+            encs[r].encode(int(q[r, 1]), int(q[r, 2]), TOTAL)
+    return [e.finish() for e in encs]
+
+
+def _fused_decode(b, archives, T):
+    n = len(archives)
+    cu = RC.uniform(b.vocab_size)
+    decs = [RC.RangeDecoder(a) for a in archives]
+    out = np.zeros((n, T), dtype=np.int64)
+    for r in range(n):
+        s = RC.lookup(cu[0], decs[r].get_freq(cu[1]))
+        decs[r].update(cu[0][s], cu[0][s + 1], cu[1])
+        out[r, 0] = s
+    slots = list(range(n))
+    b.batch_reset(slots)
+    for t in range(1, T):
+        cum = [d.get_freq(TOTAL) for d in decs]
+        q, _ = b.forward_batch_cdf(slots, out[:, t - 1], cum_freqs=cum)
+        for r in range(n):
+            decs[r].update(int(q[r, 1]), int(q[r, 2]), TOTAL)
+            out[r, t] = q[r, 0]
+    return out
+
+
 def _zipf_windows(n, T, vocab, seed):
     rng = np.random.default_rng(seed)
     ranks = rng.zipf(1.1, size=(n, T))
@@ -175,6 +213,33 @@ def test_mamba_archive_roundtrip(small_gauss_rbin):
     assert all(len(a) > 0 for a in archives)
     back = _engine_decode(b, lib, archives, T)
     np.testing.assert_array_equal(back, w)
+    # the same loop through the one-call step + CDF entry point: same bytes, same tokens back
+    assert _fused_encode(b, w) == archives
+    np.testing.assert_array_equal(_fused_decode(b, archives, T), w)
+
+
+@pytest.mark.gpu
+def test_forward_batch_cdf_matches_step_then_cdf(small_gauss_rbin):
+    from conftest import shared_backend
+    from redukt_b200.plugin import PluginError, PluginLibrary
+
+    b = shared_backend(small_gauss_rbin)
+    lib = PluginLibrary()
+    n = 5
+    b.batch_init(n)
+    w = _zipf_windows(n, 3, b.vocab_size, 5)
+    slots = [4, 0, 3, 1, 2]
+    b.batch_reset()
+    logits = b.forward_batch(slots, w[:, 0].tolist())
+    want, wq = lib.cdf(logits, symbols=w[:, 1].astype(np.uint32))
+    b.batch_reset()
+    q, c = b.forward_batch_cdf(slots, w[:, 0], symbols=w[:, 1], want_cdf=True)
+    np.testing.assert_array_equal(c, want)
+    np.testing.assert_array_equal(q, wq)
+    with pytest.raises(PluginError):      # duplicate slot: rejected before any launch
+        b.forward_batch_cdf([0, 0], [1, 2], symbols=[1, 2])
+    with pytest.raises(PluginError):      # token outside the vocabulary
+        b.forward_batch_cdf([0], [b.vocab_size], symbols=[1])
 
 
 @pytest.mark.gpu
@@ -211,3 +276,4 @@ def test_rwkv7_archive_bytes_match_cpu_pipeline(tmp_path):
     assert gpu_bytes == cpu_bytes
     back = _engine_decode(b, lib, gpu_bytes, T)
     np.testing.assert_array_equal(back, w)
+    assert _fused_encode(b, w) == cpu_bytes
