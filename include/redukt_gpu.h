@@ -193,8 +193,10 @@ int32_t redukt_b200_softmax_noalloc(const float* d_logits, uint32_t n_rows, uint
  * d_cum_freqs (decoder), {Cdf::lookup(cum), cdf[sym], cdf[sym + 1]} (coder.rs:100-114); an
  * out-of-range symbol or a cum >= 2^24 gives {.., UINT32_MAX, UINT32_MAX}.  At most one of
  * d_symbols / d_cum_freqs.  Work is enqueued on cuda_stream (NULL = the legacy default stream),
- * not synchronised, and allocates nothing.  INVALID_ARGUMENT when vocab is 0 or >= 2^24 or a
- * stride is too small.  Needs no model loaded. */
+ * not synchronised, and allocates nothing.  The first call on a device sets the kernel's
+ * shared-memory limit (rows of up to 53,248 logits keep their workspace in shared memory): make it
+ * before any stream capture.  INVALID_ARGUMENT when vocab is 0 or >= 2^24 or a stride is too
+ * small.  Needs no model loaded. */
 int32_t redukt_b200_cdf_device(const float* d_logits, uint32_t n_rows, uint32_t vocab, uint32_t ld_logits,
                                uint32_t* d_cdf, uint32_t ld_cdf, const uint32_t* d_symbols,
                                const uint32_t* d_cum_freqs, uint32_t* d_query_out, void* cuda_stream);
