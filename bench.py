@@ -118,22 +118,46 @@ def model_paths(rank: int, world: int, barrier):
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running (read-only queries).
 
-    def __init__(self, index: int):
-        self.path = tempfile.mktemp(suffix=".csv")
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    The GPU is selected by its UUID (the CUDA-visible index need not be nvidia-smi's index).  If the
+    full query is refused (an unknown field on this driver), the sampler retries with only the
+    clocks; nvidia-smi's stderr is kept and reported when no sample was taken."""
+
+    FULL = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+            "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+            "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    BASIC = "index,clocks.sm,clocks.max.sm"
+
+    def __init__(self, local: int):
+        self.sel = str(local)
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                       "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            import torch
+            u = str(torch.cuda.get_device_properties(local).uuid)
+            self.sel = u if u.startswith("GPU-") else f"GPU-{u}"
+        except Exception:
+            pass
+        self.query = self.FULL
+        self.p = self._start(self.FULL)
+        if self.p is not None:
+            time.sleep(0.3)
+            if self.p.poll() is not None:  # exited at once: the query was refused
+                self.p = self._start(self.BASIC)
+                self.query = self.BASIC
+
+    def _start(self, q):
+        self.path = tempfile.mktemp(suffix=".csv")
+        self.err = tempfile.mktemp(suffix=".err")
+        try:
+            return subprocess.Popen(["nvidia-smi", f"--id={self.sel}", f"--query-gpu={q}",
+                                     "--format=csv,noheader,nounits", "-lms", "200"],
+                                    stdout=open(self.path, "w"), stderr=open(self.err, "w"))
         except OSError:
-            self.p = None
+            return None
 
     def stop(self) -> dict:
         if self.p is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "samples": 0, "reasons": ["nvidia-smi unavailable"]}
         self.p.terminate()
         try:
             self.p.wait(timeout=5)
@@ -143,7 +167,7 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in open(self.path):
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
+            if len(f) < 3:
                 continue
             try:
                 sm.append(float(f[1]))
@@ -153,9 +177,17 @@ class ClockSampler:
             for nm, v in zip(names, f[5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
-        os.unlink(self.path)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "samples": len(sm), "reasons": sorted(reasons)}
+        err = open(self.err).read().strip() if os.path.exists(self.err) else ""
+        for f in (self.path, self.err):
+            if os.path.exists(f):
+                os.unlink(f)
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+               "samples": len(sm), "reasons": sorted(reasons), "gpu": self.sel}
+        if self.query != self.FULL:
+            out["note"] = "throttle-reason fields refused by nvidia-smi; clocks only"
+        if not sm and err:
+            out["nvidia_smi_stderr"] = err[-300:]
+        return out
 
 
 def load_peaks() -> dict:
@@ -239,9 +271,21 @@ def run_b200(args, rank, world, local, dist):
         dev_step(t)
         t += 1
     torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+
+    def roll(seconds):
+        """Untimed steps of the same workload around the timed region, so the clock sampler (one
+        sample per 200 ms) sees the clocks under this load even when the timed region is short."""
+        nonlocal t
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            for _ in range(32):
+                dev_step(t)
+                t += 1
+            torch.cuda.synchronize()
+    roll(0.8)
     barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler(local)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(K):
@@ -250,6 +294,7 @@ def run_b200(args, rank, world, local, dist):
     e1.record(stream)
     torch.cuda.synchronize()
     dev_ms = e0.elapsed_time(e1)
+    roll(0.8)
     clk = clocks.stop()
     barrier()
     torch.cuda.synchronize()

@@ -103,9 +103,13 @@ int32_t redukt_backend_forward_batch_probs(uint32_t n_streams, const uint32_t* s
 
 /* forward_batch on device-resident inputs: d_slots/d_tokens/d_out are device pointers and the
  * work is enqueued on `cuda_stream` (a cudaStream_t, NULL = the library's stream) without a host
- * synchronisation.  Slots/tokens are checked on the device; a bad entry sets the error word read by
- * redukt_b200_device_error() and its row is not computed.  Duplicate slots are the caller's
- * responsibility.  probs != 0 writes probabilities instead of logits. */
+ * synchronisation.  Slots/tokens are checked on the device.  A bad entry (slot >= pool or
+ * token >= vocab) sets bit 0 of the error word read by redukt_b200_device_error() and rejects only
+ * its own stream: no state is read or written for it (its slot, if valid, keeps its state and its
+ * periodic-reset counter bit for bit), its output row is all zeros (logits; with probs != 0 the row
+ * is the uniform distribution), and every other stream of the call is computed as if the bad one
+ * were absent.  Duplicate slots are the caller's responsibility.  probs != 0 writes probabilities
+ * instead of logits. */
 int32_t redukt_b200_forward_batch_device(uint32_t n_streams, const uint32_t* d_slots, const uint32_t* d_tokens,
                                          float* d_out, uint32_t vocab_size, int32_t probs, void* cuda_stream);
 
@@ -142,7 +146,6 @@ int32_t redukt_b200_info(uint32_t* out, uint32_t n);
  *   "split_target" CTAs a split-K tensor-core launch may use (0 = never split)
  *   "fused"        0/1 = run Q8 batches of up to 32 streams as one persistent step kernel
  *                  (only with proj_path 0; same bits as the per-kernel step)
- *   "fused_ctas"   1-4 = CTAs per SM the fused step may use (capped by occupancy)
  *   "head_ctas"    1 or 2 = tensor-core head tiles per SM at up to 64 streams (2: a 6-stage pipeline
  *                  so two CTAs share an SM; 1: the 12-stage tile of the other projections)
  * Returns INVALID_ARGUMENT for an unknown key or value. */

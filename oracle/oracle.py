@@ -21,9 +21,21 @@ _lib: Optional[ctypes.CDLL] = None
 PROFILE_F32, PROFILE_Q8 = 0, 1
 
 
+def reference_root() -> Optional[str]:
+    """The redukt source tree used to build and pin the test infrastructure: $REDUKT_REF_ROOT, else a
+    directory named `reference` beside this repository's own directory; None when neither exists
+    (as on a GPU box, which uses the prebuilt files)."""
+    cand = os.environ.get("REDUKT_REF_ROOT") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return cand if os.path.isdir(cand) else None
+
+
 def build(ref: bool = False) -> None:
     target = "all" if ref else "oracle"
-    subprocess.run(["make", "-s", "-C", HERE, target], check=True)
+    cmd = ["make", "-s", "-C", HERE, target]
+    root = reference_root()
+    if ref and root:
+        cmd.append(f"REF_ROOT={root}")
+    subprocess.run(cmd, check=True)
 
 
 def lib() -> ctypes.CDLL:

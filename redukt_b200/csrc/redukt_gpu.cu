@@ -106,6 +106,7 @@ struct Pool {
     size_t part_cap = 0;         // floats in `part`
     uint32_t* counter = nullptr; // split-K tile counters
     uint32_t* rflag = nullptr;   // [cap]
+    uint32_t* vslot = nullptr;   // [cap] validated slot per batch position (k_embed; kRejected = bad entry)
     uint32_t* d_slots = nullptr;
     uint32_t* d_tokens = nullptr;
     uint32_t* h_slots = nullptr;   // pinned
@@ -139,7 +140,6 @@ struct Model {
     // fused small-batch step (rk_fused.cuh)
     bool fused = true;          // option "fused"
     int fused_nc = 0;           // norm chunks of the instantiated kernel, 0 = shape not supported
-    int fused_ctas_per_sm = 2;  // option "fused_ctas"
     int head_ctas = 2;          // option "head_ctas": 2 = the two-CTAs-per-SM head tiles at small batch
     bool q8_payload = false;    // the loaded file stores its Q8 matrices quantised (flag bit 6)
     int num_sms = 0;
@@ -177,7 +177,7 @@ void pool_free(Pool* p) {
     p->graphs.clear();
     p->eager_done.clear();
     void* bufs[] = {p->conv, p->ssm, p->since, p->x, p->act_f, p->act_q, p->act_e, p->conv_out, p->z,
-                    p->logits, p->red, p->part, p->counter, p->rflag, p->d_slots, p->d_tokens,
+                    p->logits, p->red, p->part, p->counter, p->rflag, p->vslot, p->d_slots, p->d_tokens,
                     p->xpart, p->bar, p->zp, p->xcount};
     for (void* b : bufs) cudaFree(b);
     if (p->h_slots) cudaFreeHost(p->h_slots);
@@ -206,7 +206,7 @@ bool pool_alloc(Pool* p, uint32_t cap) {
               dalloc(&p->since, n) && dalloc(&p->x, n * d) && dalloc(&p->conv_out, n * di) &&
               dalloc(&p->z, n * di) && dalloc(&p->xpart, n * ((di + 63) / 64) * G.xr) && dalloc(&p->zp, n * G.xr) &&
               dalloc(&p->xcount, (n + 15) / 16) && dalloc(&p->logits, n * V) &&
-              dalloc(&p->red, n * parts * 2) && dalloc(&p->rflag, n) && dalloc(&p->d_slots, n) &&
+              dalloc(&p->red, n * parts * 2) && dalloc(&p->rflag, n) && dalloc(&p->vslot, n) && dalloc(&p->d_slots, n) &&
               dalloc(&p->d_tokens, n);
     if (ok) {
         if (G.profile == kF32) ok = dalloc(&p->act_f, n * di);
@@ -686,21 +686,23 @@ void launch_scan(const ScanArgs& sc, const ActOut& ao, int n, cudaStream_t st) {
     else launch(k_scan<1>, dim3((G.di + 255) / 256, n), dim3(256), G.xr * sizeof(float), st, sc, ao);
 }
 
-void launch_norm(const Pool& p, int n, const float* w, const float* b, int K_out, cudaStream_t st) {
+// vslot: the final norm's validated slots (rejected streams give zero rows), nullptr for a layer norm.
+void launch_norm(const Pool& p, int n, const float* w, const float* b, int K_out, cudaStream_t st,
+                 const uint32_t* vslot = nullptr) {
     ActOut out{p.act_f, p.act_q, p.act_e, p.cap_pad, K_out};
     if (G.profile != kF32) out.f = nullptr;
     else out.q = nullptr;
     dim3 grid((n + 3) / 4);
     int nc = (G.d + 127) / 128;
     switch (nc) {
-        case 1: launch(k_norm<1>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
-        case 2: launch(k_norm<2>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
-        case 3: launch(k_norm<3>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
-        case 4: launch(k_norm<4>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
-        case 5: launch(k_norm<5>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
-        case 6: launch(k_norm<6>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
-        case 7: launch(k_norm<7>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
-        default: launch(k_norm<8>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out); break;
+        case 1: launch(k_norm<1>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out, vslot); break;
+        case 2: launch(k_norm<2>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out, vslot); break;
+        case 3: launch(k_norm<3>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out, vslot); break;
+        case 4: launch(k_norm<4>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out, vslot); break;
+        case 5: launch(k_norm<5>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out, vslot); break;
+        case 6: launch(k_norm<6>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out, vslot); break;
+        case 7: launch(k_norm<7>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out, vslot); break;
+        default: launch(k_norm<8>, grid, dim3(128), 0, st, n, (const float*)p.x, G.d, w, b, out, vslot); break;
     }
 }
 
@@ -802,12 +804,10 @@ template <int NC>
 void launch_fused_nc(const FusedArgs& fa, size_t smem, cudaStream_t st) {
     auto k = k_step_fused<NC>;
     allow_smem(k, smem);
-    int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kFusedThreads, smem);
-    per_sm = std::min(per_sm, G.fused_ctas_per_sm);
-    if (per_sm < 1) per_sm = 1;  // the launch itself reports a grid that cannot be co-resident
+    // one CTA per SM (the job shapes are sized for that grid); a cooperative launch reports a grid
+    // that cannot be co-resident
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(G.num_sms * per_sm));
+    cfg.gridDim = dim3((unsigned)G.num_sms);
     cfg.blockDim = dim3(kFusedThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -835,7 +835,7 @@ void launch_fused(Pool& p, int n, const uint32_t* d_slots, cudaStream_t st) {
     fa.g_out = G.di / kGroup;
     fa.s_out = q8_splits(fa.g_out);
     fa.mpad_out = round_up(G.d, 128);
-    const int grid = G.num_sms * std::max(1, std::min(G.fused_ctas_per_sm, 1));
+    const int grid = G.num_sms;  // the launch grid: one CTA per SM
     const int nmb = G.di / 64, nt = (n + 7) / 8;
     // phase A: x-half jobs (conv and x_proj work) take 8 streams while they fit; z-half jobs grow
     // to 16 streams first
@@ -877,7 +877,10 @@ void launch_fused(Pool& p, int n, const uint32_t* d_slots, cudaStream_t st) {
 int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_tokens, float* d_out, bool probs,
                  cudaStream_t st) {
     const bool fused = use_fused(n);
-    StepArgs sa{n, (int)p.cap, d_slots, d_tokens, p.rflag, p.since, G.reset_every, G.d_err, fused ? p.bar : nullptr};
+    StepArgs sa{n, (int)p.cap, d_slots, d_tokens, p.rflag, p.since, G.reset_every, G.d_err, p.vslot,
+                fused ? p.bar : nullptr};
+    // every kernel after the embedding reads the validated slots, never the caller's
+    const uint32_t* vs = p.vslot;
     const Mat& emb = G.emb;
     int launches = 0;
     {
@@ -887,7 +890,7 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
         launches++;
     }
     if (fused) {  // every layer and the final norm in one persistent kernel
-        launch_fused(p, n, d_slots, st);
+        launch_fused(p, n, vs, st);
         launches++;
     }
     for (int li = 0; !fused && li < G.nl; li++) {
@@ -899,7 +902,7 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
         }
         {
             KScope k(kKInProj, st);
-            EpiInProj ein{G.di, (int)p.cap, li, d_slots, p.rflag, p.conv, L.conv_t, L.conv_b, p.conv_out, p.z};
+            EpiInProj ein{G.di, (int)p.cap, li, vs, p.rflag, p.conv, L.conv_t, L.conv_b, p.conv_out, p.z};
             project(L.in_proj, p, n, ein, st);
         }
         {
@@ -908,7 +911,7 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
         }
         {
             KScope k(kKScan, st);
-            ScanArgs sc{G.di, G.dr, G.xr, (int)p.cap, li, d_slots, p.rflag, p.zp, p.conv_out, p.z,
+            ScanArgs sc{G.di, G.dr, G.xr, (int)p.cap, li, vs, p.rflag, p.zp, p.conv_out, p.z,
                         L.dt_wt, L.dt_b, L.a_t, L.dvec, p.ssm};
             ActOut ao{p.act_f, p.act_q, p.act_e, p.cap_pad, G.di};
             if (G.profile != kF32) ao.f = nullptr;
@@ -923,7 +926,7 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
     }
     if (!fused) {
         KScope k(kKNorm, st);
-        launch_norm(p, n, G.norm_f_w, G.norm_f_b, G.d, st);
+        launch_norm(p, n, G.norm_f_w, G.norm_f_b, G.d, st, vs);
         launches++;
     }
     float* lo = probs ? p.logits : d_out;
@@ -1150,6 +1153,10 @@ int32_t check_cdf_args(uint32_t n_rows, uint32_t vocab, uint32_t ld_logits, uint
     }
     if (ld_logits < vocab || ld_cdf < vocab + 1) {
         set_err("cdf: strides %u / %u too small for %u logits", ld_logits, ld_cdf, vocab);
+        return BACKEND_INVALID_ARGUMENT;
+    }
+    if (ld_logits > 0x7fffffffu || ld_cdf > 0x7fffffffu) {  // the kernel indexes rows with int strides
+        set_err("cdf: strides %u / %u exceed 2^31 - 1", ld_logits, ld_cdf);
         return BACKEND_INVALID_ARGUMENT;
     }
     if (n_rows > 0x7fffffffu) {
@@ -1436,7 +1443,7 @@ int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* m
     int nn = (int)n;
     int launches = 0;
     auto body = [&]() {
-        StepArgs sa{nn, (int)p.cap, p.d_slots, p.d_tokens, p.rflag, p.since, 0u, G.d_err};
+        StepArgs sa{nn, (int)p.cap, p.d_slots, p.d_tokens, p.rflag, p.since, 0u, G.d_err, p.vslot};
         launches = 0;
         if (cls == kKEmbed) {
             launch(k_embed, dim3(nn), dim3(256), 0, st, sa, (const float*)G.emb.f, (const int8_t*)G.emb.q,
@@ -1547,14 +1554,12 @@ int32_t redukt_b200_set_option(const char* key, int64_t value) {
         clear_dev_graphs();
         return BACKEND_OK;
     }
-    if (!strcmp(key, "fused") || !strcmp(key, "fused_ctas") || !strcmp(key, "head_ctas")) {
+    if (!strcmp(key, "fused") || !strcmp(key, "head_ctas")) {
         if (!strcmp(key, "fused")) G.fused = value != 0;
-        else if (!strcmp(key, "head_ctas")) {
+        else {
             if (value < 1 || value > 2) return BACKEND_INVALID_ARGUMENT;
             G.head_ctas = (int)value;
         }
-        else if (value < 1 || value > 4) return BACKEND_INVALID_ARGUMENT;
-        else G.fused_ctas_per_sm = (int)value;
         for (Pool* p : {&G.v1, &G.batch}) {  // captured graphs hold the old launch sequence
             for (auto& kv : p->graphs) cudaGraphExecDestroy(kv.second);
             p->graphs.clear();

@@ -76,7 +76,7 @@ struct FusedArgs {
     int rz;                      // rows per z-half A job (64 or 128; x-half jobs are 64 rows)
     int pitch_a;                 // bytes per digit-plane row of phase A's planes (d + 16)
     FusedLayout lay;
-    const uint32_t* slots;
+    const uint32_t* slots;  // validated slots of the step (kRejected: a stream that touches no state)
     const uint32_t* rflag;
     float* x;          // [cap][d] residual stream
     float* conv;       // [L][cap][3][di]
@@ -862,6 +862,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_step_fused(FusedArgs a) {
         float4 v[NC];
         load_row_cg<NC>(a.x + (size_t)b * a.d, a.d, lane, v);
         norm_apply<NC>(v, a.d, nw, a.norm_f_b != nullptr, lane);
+        zero_if_rejected<NC>(v, meta.slot[b] == kRejected);  // a rejected stream's logits are zeros
         norm_emit<NC>(b, v, a.d, out, lane);
     }
 }

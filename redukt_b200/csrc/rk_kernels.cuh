@@ -97,12 +97,16 @@ struct StepArgs {
     uint32_t* since;              // [cap] forwards since the slot's last reset
     uint32_t reset_every;         // 0 = never (host-driven resets only)
     uint32_t* err;                // device error word (bad slot/token seen on device)
+    uint32_t* vslot;              // [n] out: the stream's slot, or kRejected for a bad slot/token
     uint32_t* bar = nullptr;      // grid-barrier counter of the fused step, zeroed here
 };
 
 // Embedding row + the periodic reset decision (MambaState::maybe_periodic_reset,
 // src/infrastructure/mamba/model.rs:315-320): reset when since >= every, then since += 1.
 // The state itself is never written here: every conv/scan read of a flagged stream uses zeros.
+// A stream with a bad slot or token is rejected: its validated slot becomes kRejected, which every
+// later kernel of the step treats as "no slot" (no state read or written, no counter change), and
+// the final norm emits zeros for it, so its output row is all zeros.
 __global__ void k_embed(StepArgs a, const float* __restrict__ emb_f, const int8_t* __restrict__ emb_q,
                         const float* __restrict__ emb_s, int d, int vocab, float* __restrict__ x) {
     pdl_wait();
@@ -113,9 +117,10 @@ __global__ void k_embed(StepArgs a, const float* __restrict__ emb_f, const int8_
     uint32_t tok = a.tokens[b], slot = a.slots[b];
     bool bad = tok >= (uint32_t)vocab || slot >= (uint32_t)a.cap;
     if (threadIdx.x == 0) {
+        a.vslot[b] = bad ? kRejected : slot;
         if (bad) {
             atomicOr(a.err, 1u);
-            a.rflag[b] = 1u;
+            a.rflag[b] = 0u;
         } else {
             uint32_t s = a.since[slot];
             uint32_t rf = (a.reset_every > 0 && s >= a.reset_every) ? 1u : 0u;
@@ -276,26 +281,37 @@ __device__ __forceinline__ void norm_emit(int b, const float4 (&o)[NC], int d, c
     });
 }
 
+// A rejected stream's normalised row is replaced by zeros (the final norm: zero logits).
+template <int NC>
+__device__ __forceinline__ void zero_if_rejected(float4 (&v)[NC], bool rejected) {
+    if (!rejected) return;
+#pragma unroll
+    for (int c = 0; c < NC; c++) v[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
 template <int NC>
 __device__ __forceinline__ void norm_row_warp(int b, const float* x, int d, const NormWeights<NC>& nw,
-                                              bool has_bias, const ActOut& out, int lane) {
+                                              bool has_bias, const ActOut& out, int lane, bool rejected) {
     float4 v[NC];
     norm_load<NC>(x + (size_t)b * d, d, lane, v);
     norm_apply<NC>(v, d, nw, has_bias, lane);
+    zero_if_rejected<NC>(v, rejected);
     norm_emit<NC>(b, v, d, out, lane);
 }
 
-// One stream per warp.
+// One stream per warp.  vslot (the step's validated slots, or nullptr for a layer norm): rows of
+// rejected streams come out as zeros.
 template <int NC>
 __global__ void k_norm(int n, const float* __restrict__ x, int d, const float* __restrict__ w,
-                       const float* __restrict__ bias, ActOut out) {
+                       const float* __restrict__ bias, ActOut out, const uint32_t* __restrict__ vslot) {
     NormWeights<NC> nw;
     nw.load(w, bias, d, threadIdx.x & 31);
     pdl_wait();
     pdl_trigger();
     int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (b >= n) return;
-    norm_row_warp<NC>(b, x, d, nw, bias != nullptr, out, threadIdx.x & 31);
+    const bool rejected = vslot && vslot[b] == kRejected;
+    norm_row_warp<NC>(b, x, d, nw, bias != nullptr, out, threadIdx.x & 31, rejected);
 }
 
 // ------------------------------------------------------------------------------------------

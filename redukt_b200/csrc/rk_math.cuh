@@ -228,6 +228,10 @@ __host__ __device__ __forceinline__ int round_up(int x, int m) { return (x + m -
 // another stream's entries.  Every Q8 projection has at most 32 groups.
 constexpr int kEStride = 32;
 
+// Validated slot of a stream whose slot or token failed the device-side check: no slot at all,
+// at least as large as every pool capacity, so every `slot < cap` test skips the stream.
+constexpr uint32_t kRejected = 0xffffffffu;
+
 // Programmatic dependent launch: wait for the preceding kernel of the stream (and its memory)
 // before touching anything it wrote, then let the next kernel start its own prologue.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

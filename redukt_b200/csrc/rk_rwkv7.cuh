@@ -156,6 +156,8 @@ struct RwStep {
     uint32_t* since;        // [cap] tokens since the last reset
     uint32_t reset_every;   // 0 = off
     uint32_t* err;          // bit 0: bad slot/token on the device path, bit 1: pipeline timeout
+    uint32_t* vslot;        // [n] validated slots, written by the step's first kernel (kRejected = bad
+                            // slot or token); every later kernel gets them as `slots`
 };
 
 // ---- Load-time embedding normalisation (Rwkv7Model::load, model.rs:266-275) -----------------
@@ -263,14 +265,18 @@ __global__ void __launch_bounds__(1024) k_rw_ln_mix(RwStep sa, LnMixArgs a) {
     pdl_wait();
     pdl_trigger();
     const uint32_t slot = sa.slots[b];
-    const bool slot_ok = slot < (uint32_t)sa.cap;
+    bool slot_ok = slot < (uint32_t)sa.cap;
     float* xb = a.x + (size_t)b * D;
     float4 x;
     if (a.emb) {
+        // the step's first kernel: a bad slot or token rejects the stream for the whole step (no
+        // state read or written, no counter change, zero logits)
         const uint32_t tok = sa.tokens[b];
         const bool bad = tok >= (uint32_t)sa.vocab || !slot_ok;
+        slot_ok = !bad;
         if (t == 0) {
-            uint32_t rf = 1u;
+            sa.vslot[b] = bad ? kRejected : slot;
+            uint32_t rf = 0u;
             if (bad) {
                 atomicOr(sa.err, 1u);
             } else {
@@ -310,7 +316,7 @@ __global__ void __launch_bounds__(1024) k_rw_ln_mix(RwStep sa, LnMixArgs a) {
     float4 q[3];
     int nq = 1;
     if (a.mode == kLnFinal) {
-        q[0] = ln;
+        q[0] = slot_ok ? ln : make_float4(0.f, 0.f, 0.f, 0.f);  // a rejected stream's logits are zeros
     } else {
         if (s_rf || !slot_ok) xp = make_float4(0.f, 0.f, 0.f, 0.f);
         if (slot_ok) st4(xp_row + i0, ln);  // state.x_prev_* = ln_buf (model.rs:668, 681)

@@ -52,7 +52,7 @@ struct Pool {
     float *x = nullptr, *lora_in = nullptr, *rkv = nullptr, *h1 = nullptr, *gated = nullptr, *ffn = nullptr;
     float *logits = nullptr, *red = nullptr, *as = nullptr;
     int8_t *aq0 = nullptr, *aq1 = nullptr, *aq2 = nullptr;
-    uint32_t *rflag = nullptr, *d_slots = nullptr, *d_tokens = nullptr;
+    uint32_t *rflag = nullptr, *vslot = nullptr, *d_slots = nullptr, *d_tokens = nullptr;
     uint32_t *h_slots = nullptr, *h_tokens = nullptr, *h_err = nullptr;
     std::vector<uint8_t> seen;
     std::map<uint64_t, cudaGraphExec_t> graphs;
@@ -75,7 +75,7 @@ Model M;
 void pool_free(Pool* p) {
     for (auto& kv : p->graphs) cudaGraphExecDestroy(kv.second);
     void* bufs[] = {p->x_att, p->x_ffn, p->wkv, p->v_first, p->since, p->x, p->lora_in, p->rkv, p->h1, p->gated,
-                    p->ffn, p->logits, p->red, p->as, p->aq0, p->aq1, p->aq2, p->rflag, p->d_slots, p->d_tokens};
+                    p->ffn, p->logits, p->red, p->as, p->aq0, p->aq1, p->aq2, p->rflag, p->vslot, p->d_slots, p->d_tokens};
     for (void* b : bufs) cudaFree(b);
     if (p->h_slots) cudaFreeHost(p->h_slots);
     if (p->h_tokens) cudaFreeHost(p->h_tokens);
@@ -95,7 +95,7 @@ bool pool_alloc(Pool* p, uint32_t cap) {
               dalloc(&p->h1, n * (size_t)M.R) && dalloc(&p->gated, n * D) && dalloc(&p->ffn, n * F) &&
               dalloc(&p->logits, n * V) && dalloc(&p->red, n * parts * 2) && dalloc(&p->as, 3 * n) &&
               dalloc(&p->aq0, std::max(D, F) * cp) && dalloc(&p->aq1, D * cp) && dalloc(&p->aq2, D * cp) &&
-              dalloc(&p->rflag, n) && dalloc(&p->d_slots, n) && dalloc(&p->d_tokens, n);
+              dalloc(&p->rflag, n) && dalloc(&p->vslot, n) && dalloc(&p->d_slots, n) && dalloc(&p->d_tokens, n);
     ok = ok && cudaHostAlloc(reinterpret_cast<void**>(&p->h_slots), n * 4, cudaHostAllocDefault) == cudaSuccess &&
          cudaHostAlloc(reinterpret_cast<void**>(&p->h_tokens), n * 4, cudaHostAllocDefault) == cudaSuccess &&
          cudaHostAlloc(reinterpret_cast<void**>(&p->h_err), 4, cudaHostAllocDefault) == cudaSuccess;
@@ -301,7 +301,9 @@ W8Args w8args(int K, int n, const Pool& p) {
 
 int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_tokens, float* d_out, bool probs,
                  cudaStream_t st) {
-    const RwStep sa{n, (int)p.cap, p.cap_pad, M.V, d_slots, d_tokens, p.rflag, p.since, G.reset_every, G.d_err};
+    // the first kernel checks the caller's slots and tokens; every later one reads the validated slots
+    const RwStep sa0{n, (int)p.cap, p.cap_pad, M.V, d_slots, d_tokens, p.rflag, p.since, G.reset_every, G.d_err, p.vslot};
+    const RwStep sa{n, (int)p.cap, p.cap_pad, M.V, p.vslot, d_tokens, p.rflag, p.since, G.reset_every, G.d_err, p.vslot};
     const int D = M.D, F = M.F;
     const size_t cap = p.cap;
     const size_t ln_smem = (size_t)D * sizeof(float);
@@ -320,7 +322,7 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
             KScope k(kKNorm, st);
             LnMixArgs la{D, kLnTime, li == 0 ? M.emb : nullptr, p.x, Y.ln1_w, Y.ln1_b, x_att, Y.mix6,
                          p.aq0, p.aq1, p.aq2, p.as, p.lora_in};
-            launch(k_rw_ln_mix, dim3(n), ln_block, ln_smem, st, sa, la);
+            launch(k_rw_ln_mix, dim3(n), ln_block, ln_smem, st, li == 0 ? sa0 : sa, la);
         }
         {
             KScope k(kKInProj, st);

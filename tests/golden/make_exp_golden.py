@@ -16,7 +16,14 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def main(ref_root="/root/reference"):
+def main(ref_root=None):
+    """ref_root: the redukt source tree (default: $REDUKT_REF_ROOT, else `reference` beside the repo)."""
+    if ref_root is None:
+        sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+        from oracle.oracle import reference_root
+        ref_root = reference_root()
+        if ref_root is None:
+            raise SystemExit("the redukt source tree was not found: set REDUKT_REF_ROOT")
     src = open(os.path.join(ref_root, "src", "domain", "fmath.rs")).read()
     body = re.search(r"const EXP_GOLDEN: \[\(f64, u64\); \d+\] = \[(.*?)\];", src, re.S).group(1)
     pairs = re.findall(r"f64::from_bits\(0x([0-9a-f]+)\), 0x([0-9a-f]+)\)", body)

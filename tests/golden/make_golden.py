@@ -55,7 +55,14 @@ def sha256(path):
     return h.hexdigest()
 
 
-def main(ref_root="/root/reference"):
+def main(ref_root=None):
+    """ref_root: the redukt source tree (default: $REDUKT_REF_ROOT, else `reference` beside the repo)."""
+    if ref_root is None:
+        sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+        from oracle.oracle import reference_root
+        ref_root = reference_root()
+        if ref_root is None:
+            raise SystemExit("the redukt source tree was not found: set REDUKT_REF_ROOT")
     RefMamba = load_refmamba(ref_root)
     tmp = tempfile.mkdtemp()
     for name, (dims, kind, seed, flags, steps) in CASES.items():

@@ -199,6 +199,8 @@ def test_cdf_entry_points_reject_bad_shapes_without_a_gpu():
     assert lib.cdf_device(1, 1, 10, 9, 1, 11) == BackendResult.INVALID_ARGUMENT      # ld_logits < vocab
     assert lib.cdf_device(1, 1, 10, 10, 1, 10) == BackendResult.INVALID_ARGUMENT     # ld_cdf < vocab + 1
     assert lib.cdf_device(1, 1, TOTAL, TOTAL, 1, TOTAL + 1) == BackendResult.INVALID_ARGUMENT
+    assert lib.cdf_device(1, 1, 10, 2**31, 1, 11) == BackendResult.INVALID_ARGUMENT   # int stride overflow
+    assert lib.cdf_device(1, 1, 10, 10, 1, 2**32 - 1) == BackendResult.INVALID_ARGUMENT
 
 
 # ----------------------------------------------------------------------------------------------
