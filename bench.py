@@ -41,7 +41,7 @@ WINDOW = 2700          # tokens per stream window (configs[0-1])
 STREAMS = 32           # lockstep streams per GPU
 L2_BYTES = 126 * 2**20
 METRIC = "Mamba-130M decode tok/s (Q8, 32 lockstep streams per GPU)"
-SWEEP_N = (1, 128, 1024)
+SWEEP_N = (1, 32, 128, 1024)
 FUSED_MAX_N = 32       # Q8 batches up to this size run the fused step kernel (rk_fused.cuh)
 RWKV_N = (1, 32, 256)  # configs[3] is 256 lockstep streams of uniform byte tokens
 
@@ -211,11 +211,23 @@ def load_traffic() -> dict:
 # CPU baseline: the reference CPU path (restated in C, oracle/) on this host's cores
 # ---------------------------------------------------------------------------------------------
 
-def cpu_baseline(q8_path: str, n: int, budget_s: float, min_steps: int = 2):
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_time(path: str, profile: str, n: int, budget_s: float, min_steps: int = 2, reset_every: int = 4096):
+    """tok/s of the C restatement of the reference CPU path (oracle/) on all host threads: n lockstep
+    streams of Zipf(1.1) windows, timed for about budget_s after one warm-up step."""
     from oracle import oracle as O
-    m = O.Model(q8_path, O.PROFILE_Q8, 64)
+    m = O.Model(path, O.PROFILE_Q8 if profile == "q8" else O.PROFILE_F32, 64)
     toks = zipf_tokens(n, WINDOW, vocab=m.vocab)
-    states = [m.new_state(4096) for _ in range(n)]
+    states = [m.new_state(reset_every) for _ in range(n)]
     m.forward_multi(toks[:, 0].tolist(), states)  # warm-up (page in weights, start the pool)
     t0 = time.perf_counter()
     steps = 0
@@ -223,10 +235,28 @@ def cpu_baseline(q8_path: str, n: int, budget_s: float, min_steps: int = 2):
         m.forward_multi(toks[:, (1 + steps) % WINDOW].tolist(), states)
         steps += 1
     dt = time.perf_counter() - t0
-    return {"value": round(n * steps / dt, 2), "unit": "tok/s", "cores": O.get_threads(), "kind": "port",
+    m.close()
+    return n * steps / dt, steps, dt, O.get_threads()
+
+
+def cpu_baseline(q8_path: str, n: int, budget_s: float, min_steps: int = 2):
+    v, steps, dt, thr = cpu_time(q8_path, "q8", n, budget_s, min_steps)
+    return {"value": round(v, 2), "unit": "tok/s", "cores": thr, "kind": "port",
             "sample": f"{steps} lockstep steps x {n} streams (Q8 group 64, Mamba-130M, {dt:.1f} s), "
                       f"C restatement of the reference CPU path (oracle/mamba_oracle.c, AVX2 lane order), "
-                      f"{O.get_threads()} threads on {os.cpu_count()} host CPUs"}
+                      f"{thr} threads on {os.cpu_count()} host CPUs ({cpu_model()})"}
+
+
+def cpu_rows(f32_path: str, q8_path: str, budget_s: float) -> dict:
+    """The reference CPU path's rows of the north star's baseline plan: F32 and Q8 single stream,
+    lockstep N=32 in Q8 and F32, each on all host threads."""
+    out = {"cpu_model": cpu_model(), "nproc": os.cpu_count(),
+           "impl": "C restatement of the reference CPU path (oracle/mamba_oracle.c, AVX2 lane order)"}
+    for prof, path in (("f32", f32_path), ("q8", q8_path)):
+        for n in (1, 32):
+            v, steps, dt, thr = cpu_time(path, prof, n, budget_s)
+            out[f"{prof}_n{n}"] = {"tok_s": round(v, 2), "steps": steps, "seconds": round(dt, 2), "threads": thr}
+    return out
 
 
 # ---------------------------------------------------------------------------------------------
@@ -368,28 +398,115 @@ def run_b200(args, rank, world, local, dist):
     if world == 1 and not args.no_cdf:   # before the sweep, which replaces the loaded model
         res["coder_cdf"] = coder_cdf(b.libobj, n, V, dev, with_cpu=rank == 0 and not args.no_cpu_baseline,
                                      backend=b, windows=windows)
+    res["archive_batch"] = archive_batch(b, rank, world, dev, stream, max_over_ranks, barrier, K, W)
+    res["determinism"] = determinism(b, rank, world, n, dev, dist)
+    with_cpu = rank == 0 and world == 1 and not args.no_cpu_baseline
     if world == 1 and not args.no_sweep:
-        res["sweep"] = sweep(b, f32_path, q8_path, dims, args, dev, peaks)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        b.close()
-        res["cpu_baseline"] = cpu_baseline(q8_path, n, args.cpu_seconds)
+        res["sweep"] = sweep(b, f32_path, q8_path, dims, args, dev, peaks, with_cpu)
     else:
         b.close()
+    if with_cpu:
+        res["cpu_baseline"] = cpu_baseline(q8_path, n, args.cpu_seconds)
+        res["cpu_baselines"] = cpu_rows(f32_path, q8_path, args.cpu_seconds / 4)
     return res
 
 
-def sweep(b, f32_path, q8_path, dims, args, dev, peaks):
-    """Device tok/s at 1/128/1024 streams, Q8 and F32 (each from fresh zero state)."""
+def archive_batch(b, rank, world, dev, stream, max_over_ranks, barrier, K, W) -> dict:
+    """configs[4]'s per-GPU batch: 512 lockstep streams per GPU (device-resident step, CUDA-graph
+    replay), timed with CUDA events and taken as the max over ranks; whole-job tok/s."""
+    import torch
+    n = 512
+    V = b.vocab_size
+    b.batch_init(n)
+    b.set_reset_every(4096)
+    toks = torch.from_numpy(zipf_tokens(n, W + K, vocab=V, seed_base=ZIPF_SEED_BASE + 7 * 4096 + rank * n).T.copy()
+                            .astype(np.int32)).to(dev)
+    slots = torch.arange(n, dtype=torch.int32, device=dev)
+    tok = torch.empty(n, dtype=torch.int32, device=dev)
+    o = torch.empty((n, V), dtype=torch.float32, device=dev)
+
+    def step(i):
+        tok.copy_(toks[i])
+        b.forward_batch_device(n, slots.data_ptr(), tok.data_ptr(), o.data_ptr(), stream=stream.cuda_stream)
+    for i in range(W):
+        step(i)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(K):
+        step(W + i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / K
+    b.set_reset_every(0)
+    if b.device_error():
+        raise RuntimeError("archive batch: device error word set")
+    del o, toks
+    return {"streams_per_gpu": n, "n_gpus": world, "ms_per_step": round(ms, 4),
+            "tok_s": round(world * n / ms * 1e3, 1), "steps": K, "scaling": "weak"}
+
+
+def window_hash(b, window: int, steps: int = 8) -> str:
+    """sha256 (first 16 hex digits) of the logits of global window `window` (its Zipf seed), run as
+    the only stream of slot 0 from zero state for `steps` tokens."""
+    import hashlib
+    toks = zipf_tokens(1, steps, vocab=b.vocab_size, seed_base=ZIPF_SEED_BASE + window)
+    b.batch_reset([0])
+    h = hashlib.sha256()
+    for t in range(steps):
+        h.update(b.forward_batch([0], toks[:, t]).tobytes())
+    return h.hexdigest()[:16]
+
+
+def determinism(b, rank, world, n, dev, dist) -> dict:
+    """Same window, same bits on every GPU and for every GPU count.  Rank r owns global windows
+    r*n .. r*n+n-1; it hashes the logits of its first window.  Rank 0 gathers the hashes and
+    recomputes every rank's window on its own GPU; the single-GPU line carries the hashes of the
+    first windows of the ranks of an 8-GPU run, so lines of different GPU counts can be compared."""
+    import torch
+    b.batch_init(max(n, 1))
+    mine = window_hash(b, rank * n)
+    got = {rank * n: mine}
+    if dist is not None:
+        t = torch.tensor([int(mine, 16) >> 1], dtype=torch.int64, device=dev)  # 63 bits
+        allv = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(allv, t)
+        got = {r * n: format(int(v.item()) << 1, "016x") for r, v in enumerate(allv)}
+    if rank != 0:
+        return {}
+    want = {w: window_hash(b, w) for w in sorted(set(list(got) + [r * n for r in range(8)]))}
+    match = all((int(got[w], 16) >> 1) == (int(want[w], 16) >> 1) for w in got)
+    return {"steps": 8, "window_hashes": want, "ranks_agree_with_rank0": match,
+            "what": "sha256 prefix of 8 steps of logits of one window (slot 0, fresh state)"}
+
+
+def sweep(b, f32_path, q8_path, dims, args, dev, peaks, with_cpu: bool):
+    """device tok/s at 1/32/128/1024 streams, Q8 and F32.  Each stream runs a Zipf(1.1)
+    window with the device-side reset every 4,096 tokens; the slots' reset counters are set so the
+    timed steps are the window positions around 4,096 and one reset falls inside the timed region.
+    Q8 at 128 and 1024 streams also gets the per-kernel breakdown (each class replayed in isolation
+    after an L2 flush).  With with_cpu, the reference CPU path (C restatement, all host threads) is
+    timed on a bounded sample of the same configuration beside it."""
     import torch
     from redukt_b200.plugin import PluginBackend
     out = {}
+    classes = ("embed", "norm", "in_proj", "x_proj", "scan", "out_proj", "head")
+    per_step = {"embed": 1, "norm": dims.n_layer + 1, "in_proj": dims.n_layer, "x_proj": dims.n_layer,
+                "scan": dims.n_layer, "out_proj": dims.n_layer, "head": 1}
     for prof, path in (("q8", q8_path), ("f32", f32_path)):
         if prof == "f32":
             b.close()
             b = PluginBackend(path, device_id=dev.index)
         for n in SWEEP_N:
+            W = max(3, args.warmup)
+            K = max(6, min(args.steps, int(2000 / max(1, n))))
+            first = 4096 - W - K // 2          # window position of the first warm-up step
+            win = zipf_tokens(n, first + W + K, vocab=b.vocab_size)
+            toks = torch.from_numpy(win[:, first:].T.copy().astype(np.int32)).to(dev)
             b.batch_init(n)
-            toks = torch.from_numpy(zipf_tokens(n, 64, vocab=b.vocab_size).T.copy().astype(np.int32)).to(dev)
+            b.set_reset_every(4096)
+            b.set_option("reset_counters", first)
             slots = torch.arange(n, dtype=torch.int32, device=dev)
             tok = torch.empty(n, dtype=torch.int32, device=dev)
             o = torch.empty((n, b.vocab_size), dtype=torch.float32, device=dev)
@@ -397,23 +514,40 @@ def sweep(b, f32_path, q8_path, dims, args, dev, peaks):
             assert sh != 0, "the sweep must run on a non-default stream"
 
             def step(i):
-                tok.copy_(toks[i % 64])
+                tok.copy_(toks[i])
                 b.forward_batch_device(n, slots.data_ptr(), tok.data_ptr(), o.data_ptr(), stream=sh)
-            for i in range(max(3, args.warmup)):
+            for i in range(W):
                 step(i)
             torch.cuda.synchronize()
-            K = max(5, min(args.steps, int(2000 / max(1, n))))
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(torch.cuda.current_stream(dev))
             for i in range(K):
-                step(i)
+                step(W + i)
             e1.record(torch.cuda.current_stream(dev))
             torch.cuda.synchronize()
+            if b.device_error():
+                raise RuntimeError(f"sweep {prof} n={n}: device error word set")
+            b.set_reset_every(0)
             ms = e0.elapsed_time(e1) / K
             wb, ps = dims_bytes(dims, prof)
             by = wb + n * ps
-            out[f"{prof}_n{n}"] = {"tok_s": round(n / ms * 1e3, 1), "ms_per_step": round(ms, 4), "steps": K,
-                                   "hbm_frac": round(by / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)}
+            e = {"tok_s": round(n / ms * 1e3, 1), "ms_per_step": round(ms, 4), "steps": K,
+                 "positions": f"{first + W}-{first + W + K - 1} of a 4,352-token window (reset before 4,096)",
+                 "bytes_per_step": by, "hbm_frac": round(by / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)}
+            if prof == "q8" and n in (128, 1024):
+                ks = {}
+                for c in classes:
+                    us = b.time_kernel(c, n, reps=3) * 1e3
+                    kb = kernel_bytes(c, n, dims, prof)
+                    ks[c] = {"avg_us": round(us, 2), "step_us": round(us * per_step[c], 1),
+                             "gbs": round(kb / (us / 1e6) / 1e9, 1)}
+                e["kernels"] = ks
+            if with_cpu:
+                v, st, dt, thr = cpu_time(path, prof, n, budget_s=1.5, min_steps=1)
+                e["cpu_tok_s"] = round(v, 2)
+                e["cpu_sample"] = f"{st} steps x {n} streams, {thr} threads, {dt:.1f} s"
+                e["vs_cpu"] = round(e["tok_s"] / v, 1)
+            out[f"{prof}_n{n}"] = e
             del o, toks
     b.close()
     out.update(sweep_rwkv7(args, dev, peaks))

@@ -148,6 +148,16 @@ int32_t redukt_b200_info(uint32_t* out, uint32_t n);
  *                  (only with proj_path 0; same bits as the per-kernel step)
  *   "head_ctas"    1 or 2 = tensor-core head tiles per SM at up to 64 streams (2: a 6-stage pipeline
  *                  so two CTAs share an SM; 1: the 12-stage tile of the other projections)
+ *   "reset_counters" sets every batch slot's periodic-reset counter to `value` (forwards since its
+ *                  last reset), e.g. to time the steps around a reset boundary without running the
+ *                  window up to it; for benchmarks
+ *   "wait_limit_us" limit of every bounded device wait in microseconds (0 = the defaults: 200 ms for
+ *                  the fused step, about 2 s for the tensor-core pipelines); for tests
+ *   "wait_test"    1 or 2 = make one bounded wait of the next step run out (1: the fused step's first
+ *                  grid barrier misses one arrival; 2: a tensor-core projection tile misses one
+ *                  activation copy); the step then returns FORWARD_FAILED with error-word bit 2
+ *                  (fused) or bit 1 (tensor core) set and the device stays usable.  One-shot; for
+ *                  tests of the error path
  * Returns INVALID_ARGUMENT for an unknown key or value. */
 int32_t redukt_b200_set_option(const char* key, int64_t value);
 

@@ -1034,7 +1034,8 @@ int pool_forward(Pool& p, uint32_t n, const uint32_t* slots, const uint32_t* tok
     CK(cudaMemcpyAsync(p.h_err, G.d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, G.stream), BACKEND_FORWARD_FAILED);
     CK(cudaStreamSynchronize(G.stream), BACKEND_FORWARD_FAILED);
     if (*p.h_err) {
-        set_err("device error word 0x%x (2 = a tensor-core pipeline wait timed out)", *p.h_err);
+        set_err("device error word 0x%x (1 = bad slot/token, 2 = a tensor-core pipeline wait ran out, "
+                "4 = a fused-step wait ran out)", *p.h_err);
         cudaMemset(G.d_err, 0, sizeof(uint32_t));
         if (p.counter) cudaMemset(p.counter, 0, kSplitMaxTiles * sizeof(uint32_t));  // an aborted tile keeps its count
         return BACKEND_FORWARD_FAILED;
@@ -1544,6 +1545,29 @@ int32_t redukt_b200_set_option(const char* key, int64_t value) {
         G.use_graphs = value != 0;
         return BACKEND_OK;
     }
+    if (!strcmp(key, "wait_limit_us")) {  // test setting: limit of every bounded device wait (0 = default)
+        if (value < 0 || value > 10 * 1000 * 1000) return BACKEND_INVALID_ARGUMENT;
+        long long cyc = value ? (long long)value * 2000 : tc::kWaitLimitCycles;  // ~2 cycles per ns
+        unsigned long long ns = value ? (unsigned long long)value * 1000 : 200ull * 1000 * 1000;
+        CK(cudaMemcpyToSymbol(tc::g_wait_cycles, &cyc, sizeof(cyc)), BACKEND_FORWARD_FAILED);
+        CK(cudaMemcpyToSymbol(tc::g_wait_ns, &ns, sizeof(ns)), BACKEND_FORWARD_FAILED);
+        return BACKEND_OK;
+    }
+    if (!strcmp(key, "reset_counters")) {  // bench setting: every batch slot has run `value` forwards
+        if (value < 0 || value > 0xffffffffll || batch_cap() == 0) return BACKEND_INVALID_ARGUMENT;
+        uint32_t* since = G.rwkv ? rwe::M.batch.since : G.batch.since;
+        std::vector<uint32_t> h(batch_cap(), (uint32_t)value);
+        CK(cudaMemcpyAsync(since, h.data(), h.size() * sizeof(uint32_t), cudaMemcpyHostToDevice, G.stream),
+           BACKEND_FORWARD_FAILED);
+        CK(cudaStreamSynchronize(G.stream), BACKEND_FORWARD_FAILED);
+        return BACKEND_OK;
+    }
+    if (!strcmp(key, "wait_test")) {  // test setting: one bounded wait of the next step runs out
+        if (value < 0 || value > 2) return BACKEND_INVALID_ARGUMENT;
+        int v = (int)value;
+        CK(cudaMemcpyToSymbol(tc::g_wait_test, &v, sizeof(v)), BACKEND_FORWARD_FAILED);
+        return BACKEND_OK;
+    }
     if (!strcmp(key, "split_target")) {
         if (value < 0 || value > 4096) return BACKEND_INVALID_ARGUMENT;
         g_split_target = (int)value;
@@ -1725,7 +1749,8 @@ int32_t redukt_b200_forward_batch_cdf(uint32_t n, const uint32_t* slots, const u
     CK(cudaMemcpyAsync(B.h_err, G.d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, st), BACKEND_FORWARD_FAILED);
     CK(cudaStreamSynchronize(st), BACKEND_FORWARD_FAILED);
     if (*B.h_err) {
-        set_err("forward_batch_cdf: device error word 0x%x (2 = a tensor-core pipeline wait timed out)", *B.h_err);
+        set_err("forward_batch_cdf: device error word 0x%x (2 = a tensor-core pipeline wait ran out, "
+                "4 = a fused-step wait ran out)", *B.h_err);
         cudaMemset(G.d_err, 0, sizeof(uint32_t));
         return BACKEND_FORWARD_FAILED;
     }

@@ -41,7 +41,6 @@ namespace rk {
 constexpr int kFusedMaxN = 32;           // streams handled by the fused step
 constexpr int kFusedThreads = 256;
 constexpr uint32_t kErrGridWait = 4u;    // error-word bit: a fused-step wait ran out
-constexpr unsigned long long kGridWaitNs = 200ull * 1000 * 1000;
 
 struct FusedLayer {
     const float* norm_w;
@@ -175,7 +174,10 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 __device__ __forceinline__ void grid_arrive(uint32_t* bar, uint32_t& target) {
     __syncthreads();
     target += gridDim.x;
-    if (threadIdx.x == 0) red_release_gpu_add(bar, 1u);
+    // wait test: CTA 0 withholds its first arrival, so this barrier never fills and every CTA's
+    // bounded wait runs out
+    if (threadIdx.x == 0 && !(blockIdx.x == 0 && target == gridDim.x && tc::take_wait_test(1)))
+        red_release_gpu_add(bar, 1u);
 }
 
 __device__ __forceinline__ bool grid_wait(uint32_t* bar, uint32_t target, uint32_t* err, int* s_ok) {
@@ -189,7 +191,7 @@ __device__ __forceinline__ bool grid_wait(uint32_t* bar, uint32_t target, uint32
                     ok = 0;
                     break;
                 }
-                if (globaltimer_ns() - t0 > kGridWaitNs) {
+                if (globaltimer_ns() - t0 > *(volatile unsigned long long*)&tc::g_wait_ns) {
                     atomicOr(err, kErrGridWait);
                     ok = 0;
                     break;
@@ -227,7 +229,7 @@ __device__ __forceinline__ bool copies_wait(uint64_t* bar, uint32_t par, uint32_
         if (!tc::mbar_try_wait(bar, par)) {
             const unsigned long long t0 = globaltimer_ns();
             while (!tc::mbar_try_wait(bar, par)) {
-                if (globaltimer_ns() - t0 > kGridWaitNs) {
+                if (globaltimer_ns() - t0 > *(volatile unsigned long long*)&tc::g_wait_ns) {
                     atomicOr(err, kErrGridWait);
                     ok = 0;
                     break;

@@ -33,6 +33,26 @@ constexpr int kAutoMinStreams = 1;   // the tensor-core kernel serves every batc
 // clock is lower): far beyond any legitimate wait.  clock64 is a cheap per-SM counter.
 constexpr long long kWaitLimitCycles = 4000000000ll;
 
+// Test settings of the bounded waits (option "wait_limit_us" / "wait_test"; device globals of the
+// library, read only on a wait's slow path):
+//   g_wait_cycles  limit of every tensor-core mbarrier wait, in SM cycles
+//   g_wait_ns      limit of every fused-step wait (grid barrier, bulk copies), in ns
+//   g_wait_test    one-shot: 1 = CTA 0 of the next fused step skips its first grid-barrier arrival,
+//                  2 = CTA 0 of the next tensor-core projection never issues its first activation
+//                  copy.  Either makes one bounded wait run out (nothing faults or hangs: every wait
+//                  gives up at its limit); the CTA that acts on it clears it.
+__device__ long long g_wait_cycles = kWaitLimitCycles;
+__device__ unsigned long long g_wait_ns = 200ull * 1000 * 1000;
+__device__ int g_wait_test = 0;
+
+__device__ __forceinline__ long long wait_limit_cycles() { return *(volatile long long*)&g_wait_cycles; }
+
+// True once for the CTA that takes a pending one-shot wait test of kind `kind`.
+__device__ __forceinline__ bool take_wait_test(int kind) {
+    if (*(volatile int*)&g_wait_test != kind) return false;
+    return atomicCAS(&g_wait_test, kind, 0) == kind;
+}
+
 template <int BN, int ST = stages_for<BN>(), int MB = 1>
 struct TileCfg {
     static constexpr int kBufs = BN == 16 ? 4 : 2;          // TMEM accumulator sets in flight
@@ -101,7 +121,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 255) == 0) {
             if (*abort) return false;
-            if (clock64() - t0 > kWaitLimitCycles) {
+            if (clock64() - t0 > wait_limit_cycles()) {
                 *abort = 1;
                 return false;
             }
@@ -112,7 +132,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // Bounded wait that ignores the abort flag (used to drain work already in flight).
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
     const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity) && clock64() - t0 < kWaitLimitCycles) {
+    const long long lim = wait_limit_cycles();
+    while (!mbar_try_wait(bar, parity) && clock64() - t0 < lim) {
     }
 }
 
@@ -279,6 +300,9 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
             pdl_wait();  // the activation digits come from the preceding kernel
             pdl_trigger();
             int issued = 0;
+            // wait test: stage 0 never receives its activation bytes, so its full barrier never
+            // completes and the MMA warp's bounded wait runs out
+            const bool skip0 = blockIdx.x == 0 && blockIdx.y == 0 && take_wait_test(2);
             for (int g = 0; g < GL; g++) {
                 int s = g % kStages;
                 uint32_t ph = (g / kStages) & 1;
@@ -287,8 +311,9 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
                     mbar_expect_tx(&S.full[s], kStageBytes);
                     bulk_load(S.a[s], wtile + (size_t)g * m_pad * 64, kBM * kBK, &S.full[s]);
                 }
-                bulk_load(S.b[s], dq + ((size_t)(gb + g) * (cap_pad >> 4) + (n0 >> 4)) * 3 * 16 * 64, 3 * BN * kBK,
-                          &S.full[s]);
+                if (!(skip0 && g == 0))
+                    bulk_load(S.b[s], dq + ((size_t)(gb + g) * (cap_pad >> 4) + (n0 >> 4)) * 3 * 16 * 64,
+                              3 * BN * kBK, &S.full[s]);
                 issued = g + 1;
             }
             if (*abort) {  // drain the copies this CTA started before its shared memory goes away
