@@ -417,7 +417,7 @@ __device__ __forceinline__ void prefetch_a(const FusedArgs& a, const StepMeta& m
         for (int i = threadIdx.x; i < ns * 3 * 16; i += kFusedThreads) {
             const int c4 = i & 15, kk = (i >> 4) % 3, s = i / 48;
             const uint32_t slot = live_slot(a, m, jb.g0 + s);
-            cp_async16(cv + (s * 3 + kk) * 64 + c4 * 4, a.conv + (((size_t)l * a.cap + slot) * 3 + kk) * a.di + c0 + c4 * 4);
+            cp_async16(cv + (s * 3 + kk) * 64 + c4 * 4, a.conv + conv_off(l, a.cap, slot, a.di, kk, c0 + c4 * 4));
         }
     }
     cp_async_commit();
@@ -451,7 +451,7 @@ __device__ __forceinline__ void prefetch_b(const FusedArgs& a, const StepMeta& m
     for (int i = threadIdx.x; i < ns * 16 * 16; i += kFusedThreads) {
         const int c4 = i & 15, kk = (i >> 4) & 15, s = i >> 8;
         const uint32_t slot = live_slot(a, m, jb.b0 + s);
-        cp_async16(st + (s * 16 + kk) * 64 + c4 * 4, a.ssm + (((size_t)l * a.cap + slot) * kDState + kk) * a.di + c0 + c4 * 4);
+        cp_async16(st + (s * 16 + kk) * 64 + c4 * 4, a.ssm + ssm_off(l, a.cap, slot, a.di, kk, c0 + c4 * 4));
     }
     cp_async_commit();
     issue_copies(bar, (a.dr + 18) * 64 * 4, 1, [&](int) {
@@ -582,10 +582,10 @@ __device__ __forceinline__ bool run_a(const FusedArgs& a, const StepMeta& m, con
                 s1 = cv[(s * 3 + 1) * 64 + rl];
                 s2 = cv[(s * 3 + 2) * 64 + rl];
             }
-            float* st = a.conv + (((size_t)l * a.cap + slot) * 3) * a.di + j;
+            float* st = a.conv + conv_off(l, a.cap, slot, a.di, 0, j);
             st[0] = s1;
-            st[a.di] = s2;
-            st[2 * a.di] = tot;
+            st[64] = s2;
+            st[128] = tot;
             co = conv_silu_taps(s0, s1, s2, tot, ct[rl], ct[64 + rl], ct[128 + rl], ct[192 + rl], ct[256 + rl]);
             a.conv_out[(size_t)b * a.di + j] = co;
         }
@@ -717,9 +717,9 @@ __device__ __forceinline__ bool run_b(const FusedArgs& a, const StepMeta& m, int
                 }
             }
             if (ok && (update || fresh)) {
-                float* sp = a.ssm + (((size_t)l * a.cap + slot) * kDState) * a.di + j;
+                float* sp = a.ssm + ssm_off(l, a.cap, slot, a.di, 0, j);
 #pragma unroll
-                for (int k = 0; k < kDState; k++) sp[(size_t)k * a.di] = st[k];
+                for (int k = 0; k < kDState; k++) sp[k * 64] = st[k];
             }
             const float y = __fadd_rn(ssm_out16(st, C), __fmul_rn(dv, xv));
             gated = ok ? __fmul_rn(y, __fmul_rn(zv, lane_sigmoid(zv))) : 0.0f;

@@ -15,8 +15,9 @@
 //
 // Layouts in HBM (all row-major):
 //   weights      f32 [rows][K] or int8 [rows][K] + f32 scales [rows][K/64]
-//   conv state   f32 [layer][slot][dc-1][d_inner]   (channel fastest: coalesced per tap)
-//   ssm state    f32 [layer][slot][d_state][d_inner]
+//   conv state   f32 [layer][slot][d_inner/64][dc-1][64]   (64-channel blocks, channel fastest:
+//   ssm state    f32 [layer][slot][d_inner/64][d_state][64]  coalesced per tap / state index, and
+//                one (slot, channel block) is one contiguous piece: 768 B conv, 4 KiB ssm)
 //   activations  f32 [stream][K], or int8 digit planes [3][stream][K] + f32 2^e [stream][K/64]
 #pragma once
 #include "rk_math.cuh"
@@ -26,6 +27,16 @@ namespace rk {
 constexpr int kDState = 16;
 constexpr int kDConv = 4;
 constexpr int kGroup = 64;
+
+// Offsets of state element (tap or state index k, channel j) of a (layer, slot) in the
+// channel-blocked state layout above; d_inner is padded to whole 64-channel blocks.
+__host__ __device__ __forceinline__ int state_blocks(int di) { return (di + 63) >> 6; }
+__host__ __device__ __forceinline__ size_t conv_off(int layer, int cap, uint32_t slot, int di, int k, int j) {
+    return ((((size_t)layer * cap + slot) * state_blocks(di) + (j >> 6)) * (kDConv - 1) + k) * 64 + (j & 63);
+}
+__host__ __device__ __forceinline__ size_t ssm_off(int layer, int cap, uint32_t slot, int di, int k, int j) {
+    return ((((size_t)layer * cap + slot) * state_blocks(di) + (j >> 6)) * kDState + k) * 64 + (j & 63);
+}
 
 // ------------------------------------------------------------------------------------------
 // Load-time kernels
@@ -406,16 +417,16 @@ struct EpiInProj {
         int j = row;
         uint32_t slot = slots[b];
         if (slot >= (uint32_t)cap) return;  // rejected stream (device-side check in k_embed)
-        float* st = conv_state + (((size_t)layer * cap + slot) * 3) * di + j;
+        float* st = conv_state + conv_off(layer, cap, slot, di, 0, j);
         float s0 = 0.f, s1 = 0.f, s2 = 0.f;
         if (!rflag[b]) {
             s0 = st[0];
-            s1 = st[di];
-            s2 = st[2 * di];
+            s1 = st[64];
+            s2 = st[128];
         }
         st[0] = s1;
-        st[di] = s2;
-        st[2 * di] = v;
+        st[64] = s2;
+        st[128] = v;
         conv_out[(size_t)b * di + j] = conv_silu(j, s0, s1, s2, v);
     }
 
@@ -449,21 +460,21 @@ struct EpiInProj {
             uint32_t slot = i < nb ? meta.slot[t0 + i] : 0xffffffffu;
             live[i] = slot < (uint32_t)cap;
             rd[i] = live[i] && meta.fresh[t0 + i] == 0;
-            st[i] = conv_state + (((size_t)layer * cap + (live[i] ? slot : 0)) * 3) * di + j;
+            st[i] = conv_state + conv_off(layer, cap, live[i] ? slot : 0u, di, 0, j);
         }
         float s0[CH], s1[CH], s2[CH];
 #pragma unroll
         for (int i = 0; i < CH; i++) {
             s0[i] = rd[i] ? st[i][0] : 0.0f;
-            s1[i] = rd[i] ? st[i][di] : 0.0f;
-            s2[i] = rd[i] ? st[i][2 * di] : 0.0f;
+            s1[i] = rd[i] ? st[i][64] : 0.0f;
+            s2[i] = rd[i] ? st[i][128] : 0.0f;
         }
 #pragma unroll
         for (int i = 0; i < CH; i++) {
             if (!live[i]) continue;
             st[i][0] = s1[i];
-            st[i][di] = s2[i];
-            st[i][2 * di] = v[i];
+            st[i][64] = s2[i];
+            st[i][128] = v[i];
             conv_out[(size_t)(b0 + i) * di + j] = conv_silu(j, s0[i], s1[i], s2[i], v[i]);
         }
     }
@@ -484,22 +495,22 @@ struct EpiInProj {
             uint32_t slot = i < nb ? slots[b0 + i] : 0xffffffffu;
             live[i] = slot < (uint32_t)cap;
             fresh[i] = live[i] && rflag[b0 + i] != 0;
-            st[i] = conv_state + (((size_t)layer * cap + (live[i] ? slot : 0)) * 3) * di + j;
+            st[i] = conv_state + conv_off(layer, cap, live[i] ? slot : 0u, di, 0, j);
         }
         float s0[CH], s1[CH], s2[CH];
 #pragma unroll
         for (int i = 0; i < CH; i++) {
             bool rd = live[i] && !fresh[i];
             s0[i] = rd ? st[i][0] : 0.0f;
-            s1[i] = rd ? st[i][di] : 0.0f;
-            s2[i] = rd ? st[i][2 * di] : 0.0f;
+            s1[i] = rd ? st[i][64] : 0.0f;
+            s2[i] = rd ? st[i][128] : 0.0f;
         }
 #pragma unroll
         for (int i = 0; i < CH; i++) {
             if (!live[i]) continue;
             st[i][0] = s1[i];
-            st[i][di] = s2[i];
-            st[i][2 * di] = v[i];
+            st[i][64] = s2[i];
+            st[i][128] = v[i];
             conv_out[(size_t)(b0 + i) * di + j] = conv_silu(j, s0[i], s1[i], s2[i], v[i]);
         }
     }
@@ -944,14 +955,14 @@ __device__ __forceinline__ void scan_block(const ScanArgs& a, const ActOut& out,
     const uint32_t slot = a.slots[b];
     const bool ok = j < a.di && slot < (uint32_t)a.cap;
     const bool fresh = a.rflag[b] != 0;
-    float* st = a.ssm + (((size_t)a.layer * a.cap + (ok ? slot : 0)) * kDState) * a.di + j;
+    float* st = a.ssm + ssm_off(a.layer, a.cap, ok ? slot : 0u, a.di, 0, ok ? j : 0);
     // Everything except x_proj's (dt_raw, B, C) is read before the dependency wait: the state and
     // the reset flag come from earlier steps and kernels, conv_out and z from the in_proj two
     // launches back (complete, since every kernel waits for its predecessor before it lets the
     // next one start), the weights are constant.
     float s[kSt];
 #pragma unroll
-    for (int k = 0; k < kSt; k++) s[k] = (ok && !fresh) ? st[(size_t)(t + TPC * k) * a.di] : 0.0f;
+    for (int k = 0; k < kSt; k++) s[k] = (ok && !fresh) ? st[(t + TPC * k) * 64] : 0.0f;
     const int jj = ok ? j : 0;
     const float xv = a.conv_out[(size_t)b * a.di + jj];
     const float zv = a.z[(size_t)b * a.di + jj];
@@ -1012,7 +1023,7 @@ __device__ __forceinline__ void scan_block(const ScanArgs& a, const ActOut& out,
     }
     if (ok && (update || fresh)) {
 #pragma unroll
-        for (int k = 0; k < kSt; k++) st[(size_t)(t + TPC * k) * a.di] = s[k];
+        for (int k = 0; k < kSt; k++) st[(t + TPC * k) * 64] = s[k];
     }
     // y = hsum_ssm(lanes) + D x, lanes[l] = s[l] C[l] + s[l+8] C[l+8],
     // hsum_ssm = ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7))
@@ -1069,16 +1080,16 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
 // Zero the conv and SSM state of the listed slots in every layer, and their reset counters.
 __global__ void k_zero_slots(const uint32_t* __restrict__ slots, int n_slots, int cap, int layers, int di,
                              float* __restrict__ conv, float* __restrict__ ssm, uint32_t* __restrict__ since) {
-    int per = (3 + kDState) * di;
+    const int cb = state_blocks(di) * 64 * (kDConv - 1), sb = state_blocks(di) * 64 * kDState;
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     int k = blockIdx.y;
     int layer = blockIdx.z;
     if (k >= n_slots) return;
     uint32_t slot = slots[k];
     if (slot >= (uint32_t)cap) return;
-    if (i < per) {
-        if (i < 3 * di) conv[((size_t)layer * cap + slot) * 3 * di + i] = 0.0f;
-        else ssm[((size_t)layer * cap + slot) * kDState * di + (i - 3 * di)] = 0.0f;
+    if (i < cb + sb) {  // a (layer, slot)'s conv and ssm state are each one contiguous block
+        if (i < cb) conv[conv_off(layer, cap, slot, di, 0, 0) + i] = 0.0f;
+        else ssm[ssm_off(layer, cap, slot, di, 0, 0) + (i - cb)] = 0.0f;
     }
     if (i == 0 && layer == 0) since[slot] = 0u;
 }

@@ -1,6 +1,8 @@
-"""The fused small-batch step (one persistent kernel per step for up to 32 streams) against the
-per-kernel step: logits and both state tensors must agree bit for bit, for every batch size the
-fused kernel covers, with slot resets and the device-side periodic reset.
+"""The one-kernel small-batch steps against the per-kernel step: logits and both state tensors must
+agree bit for bit, for every batch size the kernels cover, with slot resets and the device-side
+periodic reset.  Option "fused" selects the step: 1 the clustered step (rk_cluster.cuh: clusters
+of 16 CTAs, up to 8 streams each), 2 the grid-barrier step (rk_fused.cuh, up to 32 streams), 0 the
+per-kernel step.
 
 The per-kernel path is itself checked against the CPU oracle and against the reference's own
 golden vectors (test_gpu_parity.py), and the fused path runs all of those tests too (it is the
@@ -30,24 +32,29 @@ def run(b, fused, n, toks, slots, cap, resets):
     return np.stack(out, 1), states
 
 
+@pytest.mark.parametrize("fused", [1, 2])
 @pytest.mark.parametrize("quant", ["q8", "q8row"])
 @pytest.mark.parametrize("model", ["reftest", "gauss_small", "mamba130m"])
-def test_fused_step_bit_identical_to_kernel_path(ref_test_rbin, small_gauss_rbin, mamba130m_rbin, model, quant):
+def test_fused_step_bit_identical_to_kernel_path(ref_test_rbin, small_gauss_rbin, mamba130m_rbin, model, quant,
+                                                 fused):
     base = {"reftest": ref_test_rbin, "gauss_small": small_gauss_rbin, "mamba130m": mamba130m_rbin}[model]
     b = shared_backend(q8(base, quant == "q8row"))
     V = b.vocab_size
+    sizes = (1, 3, 8, 9, 17, 32) if model != "mamba130m" else (1, 5, 32)
+    if fused == 1:
+        sizes = sizes + (40, 56)  # the clustered step covers up to 8 streams x the co-resident clusters
     try:
-        for n in ((1, 3, 8, 9, 17, 32) if model != "mamba130m" else (1, 5, 32)):
+        for n in sizes:
             steps = 4
             toks = zipf_tokens(n, steps, vocab=V, seed_base=31 * n)
             cap = n + 5
             slots = [(3 * s + 2) % cap for s in range(n)]
             resets = {2: [s for s in range(n) if s % 4 == 1]}
-            got, st_f = run(b, 1, n, toks, slots, cap, resets)
+            got, st_f = run(b, fused, n, toks, slots, cap, resets)
             want, st_k = run(b, 0, n, toks, slots, cap, resets)
-            assert np.array_equal(bits(got), bits(want)), (model, quant, n)
+            assert np.array_equal(bits(got), bits(want)), (model, quant, n, fused)
             for (cf, sf), (ck, sk) in zip(st_f, st_k):
-                assert np.array_equal(bits(cf), bits(ck)) and np.array_equal(bits(sf), bits(sk)), (model, quant, n)
+                assert np.array_equal(bits(cf), bits(ck)) and np.array_equal(bits(sf), bits(sk)), (model, quant, n, fused)
             assert b.device_error() == 0
     finally:
         b.set_option("fused", 1)
@@ -60,7 +67,7 @@ def test_fused_step_device_periodic_reset(small_gauss_rbin):
     toks = zipf_tokens(n, steps, vocab=V, seed_base=5)
     outs = {}
     try:
-        for fused in (1, 0):
+        for fused in (2, 1, 0):
             b.set_option("fused", fused)
             b.batch_init(8)
             b.set_reset_every(4)
@@ -70,6 +77,7 @@ def test_fused_step_device_periodic_reset(small_gauss_rbin):
         b.set_option("fused", 1)
         b.set_reset_every(0)
     assert np.array_equal(bits(outs[1]), bits(outs[0]))
+    assert np.array_equal(bits(outs[2]), bits(outs[0]))
 
 
 def test_fused_step_probs_and_device_path(small_gauss_rbin):
