@@ -7,6 +7,8 @@ per-kernel step.
 The per-kernel path is itself checked against the CPU oracle and against the reference's own
 golden vectors (test_gpu_parity.py), and the fused path runs all of those tests too (it is the
 default for Q8 batches of up to 32 streams)."""
+import math
+
 import numpy as np
 import pytest
 
@@ -48,7 +50,8 @@ def test_fused_step_bit_identical_to_kernel_path(ref_test_rbin, small_gauss_rbin
             steps = 4
             toks = zipf_tokens(n, steps, vocab=V, seed_base=31 * n)
             cap = n + 5
-            slots = [(3 * s + 2) % cap for s in range(n)]
+            mult = next(m for m in range(3, cap + 3) if math.gcd(m, cap) == 1)  # a permutation of the slots
+            slots = [(mult * s + 2) % cap for s in range(n)]
             resets = {2: [s for s in range(n) if s % 4 == 1]}
             got, st_f = run(b, fused, n, toks, slots, cap, resets)
             want, st_k = run(b, 0, n, toks, slots, cap, resets)
