@@ -638,7 +638,7 @@ __global__ void __launch_bounds__(kClThreads, 1) k_step_cluster(ClArgs a) {
                 for (int sp = warp; sp < a.s_out; sp += kClThreads / 32) {
                     const int g0 = G_out * sp / a.s_out, g1 = G_out * (sp + 1) / a.s_out;
                     float acc[4];
-                    q8_tile16_split(reinterpret_cast<const int8_t*>(cw) - (size_t)g0 * 16 * 64, 16, 0,
+                    q8_tile16_split(reinterpret_cast<const int8_t*>(cw), 16, 0,  // the item holds every group
                                     reinterpret_cast<const float*>(cw + G_out * 1024), G_out, g0, g1,
                                     [&](int p, int g, int cc) {
                                         return *reinterpret_cast<const uint32_t*>(brow + (g * 3 + p) * 512 +
