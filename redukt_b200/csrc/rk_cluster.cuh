@@ -62,6 +62,7 @@ struct ClLayout {
     int gq;      // int8 [G_out][3][8][64] out_proj digit planes (64-byte swizzle), all groups
     int ge;      // f32 [8][kEStride] their exponents
     int xn;      // f32 [kClMaxT][8][16] new residual rows of the owned tiles
+    int layers;  // FusedLayer [nl]: the layer table, read by the copy issuer without a global load
     int ring;    // the operand ring
     int total;
 };
@@ -103,6 +104,7 @@ inline ClLayout cluster_layout(const ClArgs& a, int smem_max) {
     L.gq = o;     o += align16(a.g_out * 3 * 512);
     L.ge = o;     o += align16(kClMaxNS * kEStride * 4);
     L.xn = o;     o += align16(kClMaxT * kClMaxNS * 16 * 4);
+    L.layers = o; o += align16(a.nl * (int)sizeof(FusedLayer));
     o = (o + 127) & ~127;
     L.ring = o;
     L.total = smem_max;
@@ -180,13 +182,14 @@ __device__ __forceinline__ int cl_tile(const ClCtx& c, int ti) { return c.rank +
 // Copies of item k: emit(byte offset in the item, source, bytes) for each piece; returns the item's
 // size.  Pieces are 16-byte multiples at 16-byte offsets.
 template <class Emit>
-__device__ __forceinline__ int cl_item(const ClArgs& a, const ClCtx& c, const StepMeta& m, int k, Emit emit) {
+__device__ __forceinline__ int cl_item(const ClArgs& a, const ClCtx& c, const StepMeta& m, const FusedLayer* layers,
+                                       int k, Emit emit) {
     const int l = k / c.per_layer;
     int j = k - l * c.per_layer;
-    const FusedLayer& L = a.layers[l];
-    int o = 0;
+    const FusedLayer& L = layers[l];
+    int o = 0, part = 0;
     auto put = [&](const void* src, int bytes) {
-        emit(o, src, bytes);
+        emit(part++, o, src, bytes);
         o += align16(bytes);
     };
     auto state_slot = [&](int s) -> uint32_t {
@@ -231,32 +234,44 @@ __device__ __forceinline__ int cl_item(const ClArgs& a, const ClCtx& c, const St
     return o;
 }
 
-// Thread 0: issue items while a barrier slot and ring space are free.
-__device__ __forceinline__ void cl_refill(const ClArgs& a, const ClCtx& c, const StepMeta& m, ClRing& R, char* ring) {
+// Warp 0 (all lanes, converged): issue items while a barrier slot and ring space are free.  Lane 0
+// keeps the ring's books and arms the item's barrier with its total size before any lane issues one
+// of the item's copies (piece i by lane i % 32).
+__device__ __forceinline__ void cl_refill(const ClArgs& a, const ClCtx& c, const StepMeta& m, const FusedLayer* layers,
+                                          ClRing& R, char* ring) {
+    const int lane = threadIdx.x & 31;
     const long long RB = a.ring;
-    while (R.issued < c.total && !R.abort) {
-        const int k = R.issued;
-        if (k - R.released >= kClItems) return;
-        const int size = cl_item(a, c, m, k, [](int, const void*, int) {});
-        long long pos = R.head;
-        long long off = pos % RB;
-        if (off + size > RB) {  // items never wrap: skip to the ring's start
-            pos += RB - off;
-            off = 0;
+    for (;;) {
+        int k = -1, off = 0;
+        if (lane == 0 && R.issued < c.total && !R.abort && R.issued - R.released < kClItems) {
+            const int kk = R.issued;
+            const int size = cl_item(a, c, m, layers, kk, [](int, int, const void*, int) {});
+            long long pos = R.head;
+            long long o = pos % RB;
+            if (o + size > RB) {  // items never wrap: skip to the ring's start
+                pos += RB - o;
+                o = 0;
+            }
+            if (pos + size - R.tail <= RB) {
+                const int slot = kk % kClItems;
+                R.start[slot] = (int)o;
+                R.endpos[slot] = pos + size;
+                R.head = pos + size;
+                R.issued = kk + 1;
+                tc::mbar_expect_tx(&R.bar[slot], (uint32_t)size);
+                // wait test: the step's very first item never receives its bytes
+                k = (kk == 0 && blockIdx.x == 0 && tc::take_wait_test(1)) ? -2 : kk;
+                off = (int)o;
+            }
         }
-        if (pos + size - R.tail > RB) return;
-        const int slot = k % kClItems;
-        R.start[slot] = (int)off;
-        R.endpos[slot] = pos + size;
-        R.head = pos + size;
-        tc::mbar_expect_tx(&R.bar[slot], (uint32_t)size);
-        // wait test: the step's very first item never receives its bytes
-        const bool skip = k == 0 && blockIdx.x == 0 && tc::take_wait_test(1);
-        if (!skip)
-            cl_item(a, c, m, k, [&](int o, const void* src, int bytes) {
-                tc::bulk_load(ring + off + o, src, (uint32_t)bytes, &R.bar[slot]);
+        k = __shfl_sync(0xffffffffu, k, 0);
+        off = __shfl_sync(0xffffffffu, off, 0);
+        if (k == -1) return;
+        if (k >= 0)
+            cl_item(a, c, m, layers, k, [&](int i, int o, const void* src, int bytes) {
+                if ((i & 31) == lane) tc::bulk_load(ring + off + o, src, (uint32_t)bytes, &R.bar[k % kClItems]);
             });
-        R.issued = k + 1;
+        __syncwarp();
     }
 }
 
@@ -274,11 +289,11 @@ __device__ __forceinline__ bool cl_wait_one(ClRing& R, int k) {
 
 // Every thread: items [k0, k1) have landed (or the CTA has aborted).  Returns nothing: after an
 // abort the CTA computes on whatever the ring holds and only its error word matters.
-__device__ __forceinline__ void cl_wait_items(const ClArgs& a, const ClCtx& c, const StepMeta& m, ClRing& R,
-                                              char* ring, int k0, int k1) {
+__device__ __forceinline__ void cl_wait_items(const ClArgs& a, const ClCtx& c, const StepMeta& m,
+                                              const FusedLayer* layers, ClRing& R, char* ring, int k0, int k1) {
+    if (threadIdx.x < 32 && R.issued < k1) cl_refill(a, c, m, layers, R, ring);
     if (threadIdx.x == 0) {
         for (int k = k0; k < k1 && !R.abort; k++) {
-            if (k >= R.issued) cl_refill(a, c, m, R, ring);
             if (k >= R.issued) {  // the ring cannot hold the item: a layout error, never a wait
                 R.abort = 1;
                 atomicOr(a.err, kErrGridWait);
@@ -297,15 +312,18 @@ __device__ __forceinline__ void cl_wait_items(const ClArgs& a, const ClCtx& c, c
     __syncthreads();
 }
 
-// Thread 0, after a __syncthreads that ends every read of items < k1: release them and refill.
-__device__ __forceinline__ void cl_release(const ClArgs& a, const ClCtx& c, const StepMeta& m, ClRing& R, char* ring,
-                                           int k1) {
-    if (threadIdx.x != 0) return;
-    while (R.released < k1 && R.released < R.issued) {
-        R.tail = R.endpos[R.released % kClItems];
-        R.released++;
+// Warp 0, after a __syncthreads that ends every read of items < k1: release them and refill.
+__device__ __forceinline__ void cl_release(const ClArgs& a, const ClCtx& c, const StepMeta& m, const FusedLayer* layers,
+                                           ClRing& R, char* ring, int k1) {
+    if (threadIdx.x >= 32) return;
+    if (threadIdx.x == 0) {
+        while (R.released < k1 && R.released < R.issued) {
+            R.tail = R.endpos[R.released % kClItems];
+            R.released++;
+        }
     }
-    cl_refill(a, c, m, R, ring);
+    __syncwarp();
+    cl_refill(a, c, m, layers, R, ring);
 }
 
 __device__ __forceinline__ const char* cl_ptr(const ClRing& R, const char* ring, int k) {
@@ -372,14 +390,16 @@ __global__ void __launch_bounds__(kClThreads, 1) k_step_cluster(ClArgs a) {
     int8_t* gq = reinterpret_cast<int8_t*>(sm + a.lay.gq);
     float* ge = reinterpret_cast<float*>(sm + a.lay.ge);
     float* xn = reinterpret_cast<float*>(sm + a.lay.xn);
+    FusedLayer* lt = reinterpret_cast<FusedLayer*>(sm + a.lay.layers);
 
     // ---- set-up: stream metadata, zeroed exchange buffers, residual rows, the first copies ----
     if (tid < ns) {
         meta.slot[tid] = a.slots[b0 + tid];
         meta.fresh[tid] = a.rflag[b0 + tid];
     }
-    for (int i = tid; i < (a.lay.ring - a.lay.bq) / 16; i += kClThreads)
+    for (int i = tid; i < (a.lay.layers - a.lay.bq) / 16; i += kClThreads)
         reinterpret_cast<uint4*>(sm + a.lay.bq)[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = tid; i < a.nl; i += kClThreads) lt[i] = a.layers[i];
     for (int i = tid; i < kClMaxNS * d; i += kClThreads) {
         const int s = i / d;
         xs[i] = s < ns ? __ldcg(a.x + (size_t)(b0 + s) * d + (i - s * d)) : 0.0f;
@@ -392,7 +412,7 @@ __global__ void __launch_bounds__(kClThreads, 1) k_step_cluster(ClArgs a) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    if (tid == 0) cl_refill(a, c, meta, R, ring);
+    if (tid < 32) cl_refill(a, c, meta, lt, R, ring);
     cl_sync();  // every CTA of the cluster is set up before any exchange writes into it
 
     const int G_out = a.g_out, xr = a.xr;
@@ -400,9 +420,9 @@ __global__ void __launch_bounds__(kClThreads, 1) k_step_cluster(ClArgs a) {
     for (int l = 0; l < a.nl; l++) {
         int k = l * c.per_layer;
         // ---- A: norm of every stream into digit planes (warp w: stream w) ----
-        cl_wait_items(a, c, meta, R, ring, k, k + 1);
+        cl_wait_items(a, c, meta, lt, R, ring, k, k + 1);
         {
-            const FusedLayer& L = a.layers[l];
+            const FusedLayer& L = lt[l];
             const float* nws = reinterpret_cast<const float*>(cl_ptr(R, ring, k));
             if (warp < ns) {
                 NormWeights<NC> nw;
@@ -430,18 +450,18 @@ __global__ void __launch_bounds__(kClThreads, 1) k_step_cluster(ClArgs a) {
             }
         }
         __syncthreads();
-        cl_release(a, c, meta, R, ring, k + 1);
+        cl_release(a, c, meta, lt, R, ring, k + 1);
         k += 1;
         // ---- A: the owned groups' in_proj jobs ----
         for (int gi = 0; gi < c.ng; gi++) {
             const int g = cl_group(c, gi);
             const int kx = k + gi * per_g;
             // x half: MMA, then conv/SiLU + conv state + x_proj chains
-            cl_wait_items(a, c, meta, R, ring, kx, kx + a.s_in);
+            cl_wait_items(a, c, meta, lt, R, ring, kx, kx + a.s_in);
             cl_job_mma(a, R, ring, sm, kx);
             __syncthreads();
-            cl_release(a, c, meta, R, ring, kx + a.s_in);
-            cl_wait_items(a, c, meta, R, ring, kx + a.s_in, kx + a.s_in + 1);
+            cl_release(a, c, meta, lt, R, ring, kx + a.s_in);
+            cl_wait_items(a, c, meta, lt, R, ring, kx + a.s_in, kx + a.s_in + 1);
             {
                 const char* xe = cl_ptr(R, ring, kx + a.s_in);
                 const float* xw = reinterpret_cast<const float*>(xe);
@@ -510,10 +530,10 @@ __global__ void __launch_bounds__(kClThreads, 1) k_step_cluster(ClArgs a) {
                 }
             }
             __syncthreads();
-            cl_release(a, c, meta, R, ring, kx + a.s_in + 1);
+            cl_release(a, c, meta, lt, R, ring, kx + a.s_in + 1);
             // z half: MMA, then z kept locally
             const int kz = kx + a.s_in + 1;
-            cl_wait_items(a, c, meta, R, ring, kz, kz + a.s_in);
+            cl_wait_items(a, c, meta, lt, R, ring, kz, kz + a.s_in);
             cl_job_mma(a, R, ring, sm, kz);
             __syncthreads();
             for (int o = tid; o < ns * 64; o += kClThreads) {
@@ -522,7 +542,7 @@ __global__ void __launch_bounds__(kClThreads, 1) k_step_cluster(ClArgs a) {
                     sum_splits(part + (size_t)(rl >> 4) * a.s_in * 128, a.s_in, (rl & 15) * 8 + s);
             }
             __syncthreads();
-            cl_release(a, c, meta, R, ring, kz + a.s_in);
+            cl_release(a, c, meta, lt, R, ring, kz + a.s_in);
         }
         k += c.ng * per_g;
         cl_sync();
@@ -545,7 +565,7 @@ __global__ void __launch_bounds__(kClThreads, 1) k_step_cluster(ClArgs a) {
         for (int gi = 0; gi < c.ng; gi++) {
             const int g = cl_group(c, gi);
             const int kb = k + gi;
-            cl_wait_items(a, c, meta, R, ring, kb, kb + 1);
+            cl_wait_items(a, c, meta, lt, R, ring, kb, kb + 1);
             const char* sbi = cl_ptr(R, ring, kb);
             const float* sb = reinterpret_cast<const float*>(sbi);  // [dr + 18][64]
             const float* pst = reinterpret_cast<const float*>(sbi + align16((a.dr + 18) * 64 * 4));  // [ns][16][64]
@@ -607,7 +627,7 @@ __global__ void __launch_bounds__(kClThreads, 1) k_step_cluster(ClArgs a) {
                 }
             }
             __syncthreads();
-            cl_release(a, c, meta, R, ring, kb + 1);
+            cl_release(a, c, meta, lt, R, ring, kb + 1);
         }
         // the owned groups' planes (3 x 8 rows x 64 B) and exponents to the other CTAs
         for (int gi = 0; gi < c.ng; gi++) {
@@ -632,7 +652,7 @@ __global__ void __launch_bounds__(kClThreads, 1) k_step_cluster(ClArgs a) {
             const uint32_t bsw = ((uint32_t)gid >> 1) & 3u;
             const int8_t* brow = gq + gid * 64 + tig * 4;
             for (int ti = 0; ti < c.nt; ti++) {  // one tile at a time: its item, its splits over the warps
-                cl_wait_items(a, c, meta, R, ring, k + ti, k + ti + 1);
+                cl_wait_items(a, c, meta, lt, R, ring, k + ti, k + ti + 1);
                 const char* cw = cl_ptr(R, ring, k + ti);
                 float* pt = part + (size_t)ti * a.s_out * 128;
                 for (int sp = warp; sp < a.s_out; sp += kClThreads / 32) {
@@ -648,7 +668,7 @@ __global__ void __launch_bounds__(kClThreads, 1) k_step_cluster(ClArgs a) {
                     store_split(pt + (size_t)sp * 128, lane, acc);
                 }
                 __syncthreads();
-                cl_release(a, c, meta, R, ring, k + ti + 1);
+                cl_release(a, c, meta, lt, R, ring, k + ti + 1);
                 if (tid < 128) {  // residual: (row rr, stream s) of the tile
                     const int rr = tid >> 3, s = tid & 7;
                     if (s < ns) {
