@@ -144,10 +144,8 @@ int32_t redukt_b200_info(uint32_t* out, uint32_t n);
  *   "graphs"       0/1 = replay each batch size's launch sequence from a captured CUDA graph
  *   "pdl"          0/1 = programmatic dependent launch between the step's kernels
  *   "split_target" CTAs a split-K tensor-core launch may use (0 = never split)
- *   "fused"        1 = run small Q8 batches as one clustered step kernel (clusters of 16 CTAs, up
- *                  to 8 streams each, as many clusters as fit the GPU at once), 2 = as the grid-barrier
- *                  step kernel (up to 32 streams), 0 = the per-kernel step; only with proj_path 0;
- *                  every choice gives the same bits
+ *   "fused"        0/1 = run Q8 batches of up to 32 streams as one persistent step kernel
+ *                  (only with proj_path 0; same bits as the per-kernel step)
  *   "head_ctas"    1 or 2 = tensor-core head tiles per SM at up to 64 streams (2: a 6-stage pipeline
  *                  so two CTAs share an SM; 1: the 12-stage tile of the other projections)
  *   "reset_counters" sets every batch slot's periodic-reset counter to `value` (forwards since its
@@ -155,12 +153,11 @@ int32_t redukt_b200_info(uint32_t* out, uint32_t n);
  *                  window up to it; for benchmarks
  *   "wait_limit_us" limit of every bounded device wait in microseconds (0 = the defaults: 200 ms for
  *                  the fused step, about 2 s for the tensor-core pipelines); for tests
- *   "wait_test"    1 or 2 = make one bounded wait of the next step run out (1: the clustered step's
- *                  first operand copy never lands, or the grid-barrier step's first barrier misses one
- *                  arrival; 2: a tensor-core projection tile misses one activation copy); the step
- *                  then returns FORWARD_FAILED with error-word bit 2 (one-kernel steps) or bit 1
- *                  (tensor core) set and the device stays usable.  One-shot; for tests of the error
- *                  path
+ *   "wait_test"    1 or 2 = make one bounded wait of the next step run out (1: the fused step's first
+ *                  grid barrier misses one arrival; 2: a tensor-core projection tile misses one
+ *                  activation copy); the step then returns FORWARD_FAILED with error-word bit 2
+ *                  (fused) or bit 1 (tensor core) set and the device stays usable.  One-shot; for
+ *                  tests of the error path
  * Returns INVALID_ARGUMENT for an unknown key or value. */
 int32_t redukt_b200_set_option(const char* key, int64_t value);
 

@@ -9,7 +9,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libredukt_gpu.so")
 SOURCES = ["redukt_gpu.cu"]
-HEADERS = ["rk_math.cuh", "rk_kernels.cuh", "rk_fused.cuh", "rk_cluster.cuh", "rk_tc.cuh", "rk_rwkv7.cuh", "rwkv7_engine.cuh", "rk_cdf.cuh", "rk_exp_table.h"]
+HEADERS = ["rk_math.cuh", "rk_kernels.cuh", "rk_fused.cuh", "rk_tc.cuh", "rk_rwkv7.cuh", "rwkv7_engine.cuh", "rk_cdf.cuh", "rk_exp_table.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -21,7 +21,6 @@
 #include "../../include/redukt_gpu.h"
 #include "rk_kernels.cuh"
 #include "rk_fused.cuh"
-#include "rk_cluster.cuh"
 #include "rk_rwkv7.cuh"
 #include "rk_tc.cuh"
 #include "rk_cdf.cuh"
@@ -139,10 +138,7 @@ struct Model {
     bool rwkv = false;     // an RWKV-7 model is loaded (rwkv7_engine.cuh) instead of Mamba
     bool ready = false;
     // fused small-batch step (rk_fused.cuh)
-    int fused = 1;              // option "fused": 1 clustered step (rk_cluster.cuh), 2 grid-barrier step
-                                //   (rk_fused.cuh), 0 the per-kernel step
-    int cl_max = 0;             // clusters of the clustered step that fit the GPU at once (0 = unavailable)
-    int cl_smem = 0;            // its dynamic shared memory per CTA
+    bool fused = true;          // option "fused"
     int fused_nc = 0;           // norm chunks of the instantiated kernel, 0 = shape not supported
     int head_ctas = 2;          // option "head_ctas": 2 = the two-CTAs-per-SM head tiles at small batch
     bool q8_payload = false;    // the loaded file stores its Q8 matrices quantised (flag bit 6)
@@ -152,7 +148,6 @@ struct Model {
 
 Model G;
 bool prepare_fused();
-void cluster_setup();
 
 // ------------------------------------------------------------------------------------------
 // Allocation helpers
@@ -530,7 +525,6 @@ bool prepare_fused() {
     if (cudaMemcpy(G.d_fused, h.data(), h.size() * sizeof(FusedLayer), cudaMemcpyHostToDevice) != cudaSuccess) return false;
     cudaDeviceGetAttribute(&G.num_sms, cudaDevAttrMultiProcessorCount, G.device);
     if (shape_ok && G.num_sms > 0) G.fused_nc = nc;
-    cluster_setup();
     return true;
 }
 
@@ -802,13 +796,7 @@ int g_launches_per_step = 0;
 
 // ---- fused small-batch step (rk_fused.cuh) ----
 
-bool use_cluster(int n) {
-    return G.profile != kF32 && G.fused == 1 && G.fused_nc > 0 && G.cl_max > 0 && G.proj_path == 0 && !g_kt.on &&
-           n >= 1 && n <= kClMaxNS * G.cl_max;
-}
-
 bool use_fused(int n) {
-    if (use_cluster(n)) return true;
     return G.profile != kF32 && G.fused && G.fused_nc > 0 && G.proj_path == 0 && !g_kt.on && n >= 1 &&
            n <= kFusedMaxN;
 }
@@ -886,134 +874,6 @@ void launch_fused(Pool& p, int n, const uint32_t* d_slots, cudaStream_t st) {
     }
 }
 
-// ---- clustered small-batch step (rk_cluster.cuh) ----
-
-ClArgs cluster_args(Pool& p, int n, const uint32_t* d_slots) {
-    ClArgs ca{};
-    ca.n = n;
-    ca.cap = (int)p.cap;
-    ca.cap_pad = p.cap_pad;
-    ca.d = G.d;
-    ca.di = G.di;
-    ca.dr = G.dr;
-    ca.xr = G.xr;
-    ca.nl = G.nl;
-    ca.g_in = G.d / kGroup;
-    ca.s_in = q8_splits(ca.g_in);
-    ca.g_out = G.di / kGroup;
-    ca.s_out = q8_splits(ca.g_out);
-    ca.n_clusters = std::min(n, G.cl_max);
-    ca.pitch_a = G.d + 16;
-    ca.lay = cluster_layout(ca, G.cl_smem);
-    ca.ring = G.cl_smem - ca.lay.ring;
-    ca.slots = d_slots;
-    ca.rflag = p.rflag;
-    ca.x = p.x;
-    ca.conv = p.conv;
-    ca.ssm = p.ssm;
-    ca.act_q = p.act_q;
-    ca.act_e = p.act_e;
-    ca.layers = G.d_fused;
-    ca.norm_f_w = G.norm_f_w;
-    ca.norm_f_b = G.norm_f_b;
-    ca.err = G.d_err;
-    return ca;
-}
-
-// Ring bytes one CTA needs for streams_per_cluster streams: the largest set of items it waits for
-// at once, plus the largest item (the space an item that does not fit at the ring's end skips).
-int cluster_ring_need(int ns) {
-    const int gi = G.d / kGroup, go = G.di / kGroup;
-    const int xw = align16(64 * gi * 4) + gi * 4096;
-    const int xe = align16(G.xr * 68 * 4) + align16(5 * 64 * 4) + ns * 768;
-    const int sb = align16((G.dr + 18) * 64 * 4) + ns * 4096;
-    const int cw = go * 1024 + align16(16 * go * 4);
-    const int nw = G.d * 4 * (G.layers[0].norm_b ? 2 : 1);
-    const int big = std::max(std::max(xw, xe), std::max(std::max(sb, cw), nw));
-    return big + big;
-}
-
-template <int NC>
-void cluster_setup_nc() {
-    auto k = k_step_cluster<NC>;
-    cudaFuncAttributes fa{};
-    int optin = 0;
-    if (cudaFuncGetAttributes(&fa, k) != cudaSuccess ||
-        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, G.device) != cudaSuccess) {
-        cudaGetLastError();
-        return;
-    }
-    const int smem = optin - (int)fa.sharedSizeBytes;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
-        cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
-        cudaGetLastError();
-        return;
-    }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kClCTAs);
-    cfg.blockDim = dim3(kClThreads);
-    cfg.dynamicSmemBytes = smem;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kClCTAs;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, k, &cfg) != cudaSuccess) {
-        cudaGetLastError();
-        return;
-    }
-    Pool dummy;
-    G.cl_smem = smem;
-    const ClArgs ca = cluster_args(dummy, 1, nullptr);
-    if (ca.ring < cluster_ring_need(kClMaxNS) || G.di / 64 > kClMaxG * kClCTAs || G.d / 16 > kClMaxT * kClCTAs) {
-        G.cl_smem = 0;
-        return;
-    }
-    G.cl_max = clusters;
-}
-
-void cluster_setup() {
-    G.cl_max = 0;
-    G.cl_smem = 0;
-    switch (G.fused_nc) {
-        case 1: cluster_setup_nc<1>(); break;
-        case 2: cluster_setup_nc<2>(); break;
-        case 6: cluster_setup_nc<6>(); break;
-        case 8: cluster_setup_nc<8>(); break;
-        default: break;
-    }
-}
-
-template <int NC>
-void launch_cluster_nc(const ClArgs& ca, cudaStream_t st) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(ca.n_clusters * kClCTAs));
-    cfg.blockDim = dim3(kClThreads);
-    cfg.dynamicSmemBytes = (size_t)G.cl_smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kClCTAs;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, k_step_cluster<NC>, ca);
-}
-
-void launch_cluster(Pool& p, int n, const uint32_t* d_slots, cudaStream_t st) {
-    const ClArgs ca = cluster_args(p, n, d_slots);
-    switch (G.fused_nc) {
-        case 1: launch_cluster_nc<1>(ca, st); break;
-        case 2: launch_cluster_nc<2>(ca, st); break;
-        case 6: launch_cluster_nc<6>(ca, st); break;
-        default: launch_cluster_nc<8>(ca, st); break;
-    }
-}
-
 // Enqueues one decode step for n streams whose slots/tokens are already on the device.
 int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_tokens, float* d_out, bool probs,
                  cudaStream_t st) {
@@ -1031,8 +891,7 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
         launches++;
     }
     if (fused) {  // every layer and the final norm in one kernel
-        if (use_cluster(n)) launch_cluster(p, n, vs, st);
-        else launch_fused(p, n, vs, st);
+        launch_fused(p, n, vs, st);
         launches++;
     }
     for (int li = 0; !fused && li < G.nl; li++) {
@@ -1600,8 +1459,7 @@ int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* m
             launches = 1;
         } else if (cls == kKStep) {  // every layer + the final norm in the fused kernel
             cudaMemsetAsync(p.bar, 0, sizeof(uint32_t), st);
-            if (use_cluster(nn)) launch_cluster(p, nn, p.d_slots, st);
-            else launch_fused(p, nn, p.d_slots, st);
+            launch_fused(p, nn, p.d_slots, st);
             launches = 1;
         } else {
             for (int li = 0; li < G.nl; li++) {
@@ -1725,10 +1583,7 @@ int32_t redukt_b200_set_option(const char* key, int64_t value) {
         return BACKEND_OK;
     }
     if (!strcmp(key, "fused") || !strcmp(key, "head_ctas")) {
-        if (!strcmp(key, "fused")) {
-            if (value < 0 || value > 2) return BACKEND_INVALID_ARGUMENT;
-            G.fused = (int)value;
-        }
+        if (!strcmp(key, "fused")) G.fused = value != 0;
         else {
             if (value < 1 || value > 2) return BACKEND_INVALID_ARGUMENT;
             G.head_ctas = (int)value;

@@ -4,8 +4,8 @@ Every wait in the engine's kernels (the fused step's grid barriers and copy wait
 tensor-core pipelines' mbarrier waits) gives up after a time limit, sets a bit of the device error
 word and lets the kernel return; the host turns the word into FORWARD_FAILED.  These tests make one
 wait run out on purpose with the engine's test settings: the limit is shortened to 2 ms and one
-copy (clustered step, tensor-core tile) or one grid-barrier arrival (grid-barrier step) is withheld,
-so the waiting side sees a flag that nothing sets.  Nothing faults: the waits simply give up.  The next normal step must then return the
+arrival (fused step) or one copy (tensor-core tile) is withheld, so the waiting side sees a flag that
+nothing sets.  Nothing faults: the waits simply give up.  The next normal step must then return the
 same bits as a step that never saw the failure.
 """
 import numpy as np
@@ -22,7 +22,7 @@ def bits(a):
     return np.ascontiguousarray(a).view(np.uint32)
 
 
-@pytest.mark.parametrize("kind,n,fused,word", [(1, 8, 1, 0x4), (1, 8, 2, 0x4), (2, 40, 0, 0x2)])
+@pytest.mark.parametrize("kind,n,fused,word", [(1, 8, 1, 0x4), (2, 40, 0, 0x2)])
 def test_wait_runs_out_then_next_step_is_correct(small_gauss_rbin, kind, n, fused, word):
     b = shared_backend(q8(small_gauss_rbin))
     V = b.vocab_size
