@@ -148,6 +148,8 @@ int32_t redukt_b200_info(uint32_t* out, uint32_t n);
  *                  (only with proj_path 0; same bits as the per-kernel step)
  *   "head_ctas"    1 or 2 = tensor-core head tiles per SM at up to 64 streams (2: a 6-stage pipeline
  *                  so two CTAs share an SM; 1: the 12-stage tile of the other projections)
+ *   "scan_blk"     0/1 = above 64 streams, scan blocks of 16-32 streams per CTA with the channel
+ *                  group's weights staged once (1, default) or one stream per CTA (0); same bits
  *   "reset_counters" sets every batch slot's periodic-reset counter to `value` (forwards since its
  *                  last reset), e.g. to time the steps around a reset boundary without running the
  *                  window up to it; for benchmarks

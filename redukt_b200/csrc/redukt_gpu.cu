@@ -139,6 +139,7 @@ struct Model {
     bool ready = false;
     // fused small-batch step (rk_fused.cuh)
     bool fused = true;          // option "fused"
+    bool scan_blk = true;       // option "scan_blk": stream-blocked scan above 64 streams
     int fused_nc = 0;           // norm chunks of the instantiated kernel, 0 = shape not supported
     int head_ctas = 2;          // option "head_ctas": 2 = the two-CTAs-per-SM head tiles at small batch
     bool q8_payload = false;    // the loaded file stores its Q8 matrices quantised (flag bit 6)
@@ -682,9 +683,24 @@ void project_head(const Pool& p, int n, float* out, cudaStream_t st) {
 
 // Four threads per channel while the batch is small (latency), one when it is large (no repeated
 // per-channel work); both give the same bits.
+// Above 64 streams, stream blocks of 16 or 32 per CTA with the group's weights staged once
+// (k_scan_blk, same bits) where d_inner is a multiple of 64.
 void launch_scan(const ScanArgs& sc, const ActOut& ao, int n, cudaStream_t st) {
-    if (n <= 64) launch(k_scan<4>, dim3(G.di / 64, n), dim3(256), G.xr * sizeof(float), st, sc, ao);
-    else launch(k_scan<1>, dim3((G.di + 255) / 256, n), dim3(256), G.xr * sizeof(float), st, sc, ao);
+    if (n <= 64) {
+        launch(k_scan<4>, dim3(G.di / 64, n), dim3(256), G.xr * sizeof(float), st, sc, ao);
+    } else if (G.di % 64 == 0 && G.scan_blk) {
+        const int sb = n >= 512 ? 32 : 16;
+        const size_t smem = ((size_t)(G.dr + kDState + 2) * 64 + (size_t)sb * G.xr) * sizeof(float);
+        if (sb == 32) {
+            allow_smem(k_scan_blk<32>, smem);
+            launch(k_scan_blk<32>, dim3(G.di / 64, (n + 31) / 32), dim3(256), smem, st, sc, ao, n);
+        } else {
+            allow_smem(k_scan_blk<16>, smem);
+            launch(k_scan_blk<16>, dim3(G.di / 64, (n + 15) / 16), dim3(256), smem, st, sc, ao, n);
+        }
+    } else {
+        launch(k_scan<1>, dim3((G.di + 255) / 256, n), dim3(256), G.xr * sizeof(float), st, sc, ao);
+    }
 }
 
 // vslot: the final norm's validated slots (rejected streams give zero rows), nullptr for a layer norm.
@@ -1578,6 +1594,16 @@ int32_t redukt_b200_set_option(const char* key, int64_t value) {
         for (Pool* p : {&G.v1, &G.batch}) {  // captured graphs hold the old grids
             for (auto& kv : p->graphs) cudaGraphExecDestroy(kv.second);
             p->graphs.clear();
+        }
+        clear_dev_graphs();
+        return BACKEND_OK;
+    }
+    if (!strcmp(key, "scan_blk")) {
+        G.scan_blk = value != 0;
+        for (Pool* p : {&G.v1, &G.batch}) {
+            for (auto& kv : p->graphs) cudaGraphExecDestroy(kv.second);
+            p->graphs.clear();
+            p->eager_done.clear();
         }
         clear_dev_graphs();
         return BACKEND_OK;

@@ -1077,6 +1077,111 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
     });
 }
 
+// Large-batch scan: one CTA per (64-channel group, block of SB streams), thread = (channel, stream
+// lane of 4), SB / 4 passes.  The group's dt_proj columns, A, dt bias and D are staged in shared
+// memory once per CTA instead of being re-read from L2 for every stream (the one-stream CTAs of
+// k_scan), and the next pass's state, conv output and z are loaded while the current pass
+// computes.  The arithmetic is scan_block<1>'s (same bits); d_inner must be a multiple of 64.
+template <int SB>
+__global__ void __launch_bounds__(256) k_scan_blk(ScanArgs a, ActOut out, int n) {
+    extern __shared__ float4 smem_f4[];
+    float* w = reinterpret_cast<float*>(smem_f4);   // [dr][64] dt_proj, [16][64] A, [64] dt bias, [64] D
+    float* zs = w + (a.dr + kDState + 2) * 64;       // [SB][xr]
+    __shared__ float s_max[2][8];
+    const int g = blockIdx.x, b0 = blockIdx.y * SB;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ch = tid & 63, sl = tid >> 6, j = g * 64 + ch;
+    // constant operands (before the dependency wait): the group's columns, coalesced
+    for (int i = tid; i < a.dr * 64; i += 256) w[i] = __ldg(a.dt_wt + (size_t)(i >> 6) * a.di + g * 64 + (i & 63));
+    for (int i = tid; i < kDState * 64; i += 256)
+        w[a.dr * 64 + i] = __ldg(a.a_t + (size_t)(i >> 6) * a.di + g * 64 + (i & 63));
+    if (tid < 64) {
+        w[(a.dr + kDState) * 64 + tid] = __ldg(a.dt_b + j);
+        w[(a.dr + kDState + 1) * 64 + tid] = __ldg(a.dvec + j);
+    }
+    // one pass's per-thread operands: state, conv output, z (written by earlier kernels)
+    struct Op {
+        float s[kDState];
+        float xv, zv;
+        bool ok, fresh;
+        uint32_t slot;
+    };
+    auto load = [&](int pass, Op& o) {
+        const int b = b0 + pass * 4 + sl;
+        o.ok = false;
+        o.fresh = false;
+        o.slot = 0;
+        o.xv = o.zv = 0.0f;
+        if (b < n) {
+            o.slot = a.slots[b];
+            o.ok = o.slot < (uint32_t)a.cap;
+            o.fresh = a.rflag[b] != 0;
+            o.xv = a.conv_out[(size_t)b * a.di + j];
+            o.zv = a.z[(size_t)b * a.di + j];
+        }
+        const float* st = a.ssm + ssm_off(a.layer, a.cap, o.ok ? o.slot : 0u, a.di, 0, j);
+#pragma unroll
+        for (int k = 0; k < kDState; k++) o.s[k] = (o.ok && !o.fresh) ? st[k * 64] : 0.0f;
+    };
+    Op cur;
+    load(0, cur);
+    pdl_wait();
+    pdl_trigger();
+    for (int i = tid; i < SB * a.xr; i += 256) {
+        const int s = i / a.xr, b = b0 + s;
+        zs[i] = b < n ? a.zp[(size_t)b * a.xr + (i - s * a.xr)] : 0.0f;
+    }
+    __syncthreads();
+    const float* at = w + a.dr * 64;
+    const float dtb = w[(a.dr + kDState) * 64 + ch], dv = w[(a.dr + kDState + 1) * 64 + ch];
+    const int body = a.dr & ~7;
+    for (int pass = 0; pass < SB / 4; pass++) {
+        Op nxt;
+        if (pass + 1 < SB / 4) load(pass + 1, nxt);
+        const int s = pass * 4 + sl, b = b0 + s;
+        const float* zb = zs + s * a.xr;
+        float dt = dt_dot8_body(zb, body, [&](int c) { return w[c * 64 + ch]; });
+        for (int c = body; c < a.dr; c++) dt = __fadd_rn(dt, __fmul_rn(w[c * 64 + ch], zb[c]));
+        dt = softplus(__fadd_rn(dt, dtb));
+        const float* B = zb + a.dr;
+        const float* C = zb + a.dr + kDState;
+        const bool update = !(fabsf(dt) < 1e-6f);
+        if (update) {
+            const float dtx = __fmul_rn(dt, cur.xv);
+#pragma unroll
+            for (int k = 0; k < kDState; k++) {
+                const float da = lane_expf(__fsub_rn(0.0f, __fmul_rn(dt, at[k * 64 + ch])));
+                cur.s[k] = __fadd_rn(__fmul_rn(da, cur.s[k]), __fmul_rn(dtx, B[k]));
+            }
+        }
+        if (cur.ok && (update || cur.fresh)) {
+            float* st = a.ssm + ssm_off(a.layer, a.cap, cur.slot, a.di, 0, j);
+#pragma unroll
+            for (int k = 0; k < kDState; k++) st[k * 64] = cur.s[k];
+        }
+        const float y = __fadd_rn(ssm_out16(cur.s, C), __fmul_rn(dv, cur.xv));
+        const float gated = cur.ok ? __fmul_rn(y, __fmul_rn(cur.zv, lane_sigmoid(cur.zv))) : 0.0f;
+        if (out.f) {
+            if (cur.ok) out.f[(size_t)b * out.K + j] = gated;
+        } else {
+            // digit planes over the stream's 64 channels (warps 2 sl, 2 sl + 1)
+            float m = warp_allmax(fabsf(gated));
+            if (lane == 0) s_max[pass & 1][warp] = m;
+            __syncthreads();
+            m = fmaxf(s_max[pass & 1][warp & ~1], s_max[pass & 1][warp | 1]);
+            if (cur.ok) {
+                float ginv, gs = group_scale(m, &ginv);
+                const Digits3 dg = split_digits(gated, ginv);
+                out.q[dq_off(out.cap_pad, 0, b, j)] = (int8_t)dg.d1;
+                out.q[dq_off(out.cap_pad, 1, b, j)] = (int8_t)dg.d2;
+                out.q[dq_off(out.cap_pad, 2, b, j)] = (int8_t)dg.d3;
+                if (ch == 0) out.e[(size_t)b * kEStride + g] = gs;
+            }
+        }
+        if (pass + 1 < SB / 4) cur = nxt;
+    }
+}
+
 // Zero the conv and SSM state of the listed slots in every layer, and their reset counters.
 __global__ void k_zero_slots(const uint32_t* __restrict__ slots, int n_slots, int cap, int layers, int di,
                              float* __restrict__ conv, float* __restrict__ ssm, uint32_t* __restrict__ since) {
