@@ -202,7 +202,7 @@ bool pool_alloc(Pool* p, uint32_t cap) {
     *p = Pool();
     p->cap = cap;
     size_t n = cap, L = G.nl, d = G.d, di = G.di, V = G.V;
-    size_t parts = (V + kSoftmaxTile - 1) / kSoftmaxTile;
+    size_t parts = std::max((V + kSoftmaxTile - 1) / kSoftmaxTile, (V + tc::kBM - 1) / tc::kBM);  // softmax partials
     const size_t dib = (size_t)state_blocks((int)di) * 64;  // d_inner in whole 64-channel blocks
     bool ok = dalloc(&p->conv, L * n * (kDConv - 1) * dib) && dalloc(&p->ssm, L * n * kDState * dib) &&
               dalloc(&p->since, n) && dalloc(&p->x, n * d) && dalloc(&p->conv_out, n * di) &&
@@ -652,7 +652,8 @@ void project_tc_bn(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st)
     allow_smem(k, smem);
     const int gx = (n + BN - 1) / BN, gy = (m.rows + tc::kBM - 1) / tc::kBM;
     tc::SplitK sk{1, p.part, p.counter};
-    if (BN == 16 && p.part) sk.splits = split_for(gx * gy, m.rows, m.cols / kGroup, n, p.part_cap);
+    // the head's softmax partials need every CTA to hold its whole tile: never split it
+    if (BN == 16 && p.part && !TileSoftmax<Epi>::value) sk.splits = split_for(gx * gy, m.rows, m.cols / kGroup, n, p.part_cap);
     dim3 grid(gx, gy, sk.splits);
     launch(k, grid, dim3(tc::TileCfg<BN, ST, MB>::kThreads), smem, st, (const int8_t*)m.q, (const int8_t*)p.act_q, m.rows, m.cols,
            p.cap_pad, n, (const float*)m.s, (const float*)p.act_e, G.d_err, epi, sk);
@@ -679,6 +680,20 @@ void project_head(const Pool& p, int n, float* out, cudaStream_t st) {
         project_tc_bn<16, EpiStore, 6, 2>(G.head, p, n, EpiStore{out, G.V}, st);
     else
         project(G.head, p, n, EpiStore{out, G.V}, st);
+}
+
+// The head with the softmax partials of its 128-row tiles (EpiStoreSoftmax); the tile shapes are
+// project_head's, so the logits are the same bits.
+void project_head_softmax(const Pool& p, int n, float* out, int tiles, cudaStream_t st) {
+    EpiStoreSoftmax e{};
+    e.out = out;
+    e.ld = G.V;
+    e.red = p.red;
+    e.parts = tiles;
+    if (n <= 64 && G.head_ctas == 2) project_tc_bn<16, EpiStoreSoftmax, 6, 2>(G.head, p, n, e, st);
+    else if (n <= 64) project_tc_bn<16>(G.head, p, n, e, st);
+    else if (n <= 256) project_tc_bn<32>(G.head, p, n, e, st);
+    else project_tc_bn<64>(G.head, p, n, e, st);
 }
 
 // Four threads per channel while the batch is small (latency), one when it is large (no repeated
@@ -723,8 +738,12 @@ void launch_norm(const Pool& p, int n, const float* w, const float* b, int K_out
     }
 }
 
-// Softmax over each row of `logits` written to `out` (may alias): partial (max, sum exp) per
-// 2048-logit tile, then a fixed-order combine.  exp is the reference's Cephes polynomial.
+// Softmax over each row of `logits` written to `out` (may alias), softmax_into's semantics
+// (src/domain/tensor.rs:1917-1933): p = exp(l - max) / max(sum, FLT_EPSILON) with the reference's
+// Cephes exp, and a row whose logits are all -inf becomes uniform.  Two passes: a (max, sum of
+// exp(l - max)) partial per tile of logits (k_softmax_partial over 2048-logit tiles, or the
+// tensor-core head's own 128-row tiles, EpiStoreSoftmax), then k_softmax_final combines the
+// partials in a fixed order (lane-strided, then a butterfly) and normalises.
 __global__ void k_softmax_partial(const float* __restrict__ logits, int V, float* __restrict__ red, int parts) {
     pdl_wait();
     pdl_trigger();
@@ -741,7 +760,8 @@ __global__ void k_softmax_partial(const float* __restrict__ logits, int V, float
     m = s_m[0];
     for (int i = 1; i < (int)(blockDim.x >> 5); i++) m = fmaxf(m, s_m[i]);
     float s = 0.0f;
-    for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) s = __fadd_rn(s, portable_expf(__fsub_rn(l[v], m)));
+    if (m != -INFINITY)
+        for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) s = __fadd_rn(s, portable_expf(__fsub_rn(l[v], m)));
     s = warp_allsum(s);
     if (lane == 0) s_s[w] = s;
     __syncthreads();
@@ -757,16 +777,33 @@ __global__ void k_softmax_final(const float* __restrict__ logits, int V, const f
                                 float* __restrict__ out) {
     pdl_wait();
     pdl_trigger();
-    int b = blockIdx.y;
+    __shared__ float s_ms[2];
+    const int b = blockIdx.y;
     const float* rb = red + (size_t)b * parts * 2;
-    float M = -INFINITY;
-    for (int t = 0; t < parts; t++) M = fmaxf(M, rb[2 * t]);
-    float S = 0.0f;
-    for (int t = 0; t < parts; t++) S = __fadd_rn(S, __fmul_rn(rb[2 * t + 1], portable_expf(__fsub_rn(rb[2 * t], M))));
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        float M = -INFINITY;
+        for (int t = lane; t < parts; t += 32) M = fmaxf(M, rb[2 * t]);
+        M = warp_allmax(M);
+        float S = 0.0f;
+        if (M != -INFINITY)
+            for (int t = lane; t < parts; t += 32) {
+                const float mt = rb[2 * t];
+                if (mt != -INFINITY) S = __fadd_rn(S, __fmul_rn(rb[2 * t + 1], portable_expf(__fsub_rn(mt, M))));
+            }
+        S = warp_allsum(S);
+        if (lane == 0) {
+            s_ms[0] = M;
+            s_ms[1] = fmaxf(S, 1.1920928955078125e-07f);  // sum.max(f32::EPSILON)
+        }
+    }
+    __syncthreads();
+    const float M = s_ms[0], D = s_ms[1];
     const float* l = logits + (size_t)b * V;
     float* o = out + (size_t)b * V;
+    const float uni = __fdiv_rn(1.0f, (float)V);
     for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < V; v += gridDim.x * blockDim.x)
-        o[v] = __fdiv_rn(portable_expf(__fsub_rn(l[v], M)), S);
+        o[v] = M == -INFINITY ? uni : __fdiv_rn(portable_expf(__fsub_rn(l[v], M)), D);
 }
 
 // Kernel classes for the optional per-launch CUDA-event timing (redukt_b200_kernel_times).
@@ -947,18 +984,25 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
         launches++;
     }
     float* lo = probs ? p.logits : d_out;
+    const bool fused_softmax = probs && G.profile != kF32 && use_tc(n);
+    const int head_tiles = (G.V + tc::kBM - 1) / tc::kBM;
     {
         KScope k(kKHead, st);
-        project_head(p, n, lo, st);
+        if (fused_softmax) project_head_softmax(p, n, lo, head_tiles, st);
+        else project_head(p, n, lo, st);
     }
     launches += 1;
     if (probs) {
         KScope k(kKSoftmax, st);
-        int parts = (G.V + kSoftmaxTile - 1) / kSoftmaxTile;
-        launch(k_softmax_partial, dim3(parts, n), dim3(256), 0, st, (const float*)lo, G.V, p.red, parts);
+        int parts = head_tiles;
+        if (!fused_softmax) {
+            parts = (G.V + kSoftmaxTile - 1) / kSoftmaxTile;
+            launch(k_softmax_partial, dim3(parts, n), dim3(256), 0, st, (const float*)lo, G.V, p.red, parts);
+            launches++;
+        }
         launch(k_softmax_final, dim3(std::max(1, std::min(64, G.V / 1024)), n), dim3(256), 0, st, (const float*)lo, G.V,
                (const float*)p.red, parts, d_out);
-        launches += 2;
+        launches++;
     }
     g_launches_per_step = launches;
     CK(cudaGetLastError(), BACKEND_FORWARD_FAILED);

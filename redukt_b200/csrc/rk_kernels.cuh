@@ -357,6 +357,23 @@ struct EpiStore {  // out[b][row] = v
     }
 };
 
+// The LM head's store when probabilities follow: the logits are stored as EpiStore does, and the
+// tensor-core tile kernel also writes, for each of its streams, the (max, sum of exp(l - max)) of
+// its 128 rows to red[stream][tile] (k_proj_q8_tc), so one normalising pass finishes the softmax
+// without reading the logits twice.
+struct EpiStoreSoftmax : EpiStore {
+    float* red;  // [stream][parts][2]
+    int parts;   // row tiles of the head
+};
+template <class E>
+struct TileSoftmax {
+    static constexpr bool value = false;
+};
+template <>
+struct TileSoftmax<EpiStoreSoftmax> {
+    static constexpr bool value = true;
+};
+
 struct EpiResidual {  // x[b][row] += v (src/infrastructure/mamba/model.rs:716-719)
     float* x;
     int ld;

@@ -556,6 +556,45 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
                 if (b0 < n) epi.template apply<kCH>(row, b0, min(kCH, n - b0), v, TileMeta{S.slot, S.fresh}, tb);
             }
         }
+        if constexpr (TileSoftmax<Epi>::value) {
+            // The tile's softmax partials: for each of this warpgroup's kSPT streams, the max over
+            // the tile's 128 rows and the sum of exp(l - max) over them (the reference's Cephes exp),
+            // each reduced in a fixed order (warp butterfly, then the 4 warps in order), so the
+            // result depends only on the stream's own logits.  Rows past M count as -inf / 0.  The
+            // head never runs split (every CTA emits its whole tile).
+            __shared__ float s_part[kEG][4][kSPT];
+            const int bar_id = 2 + half;
+            const bool valid = emit && !*abort && row_ok;
+            float mx[kSPT];
+#pragma unroll
+            for (int b = 0; b < kSPT; b++) mx[b] = warp_allmax(valid ? acc[b] : -INFINITY);
+            if (lane == 0)
+#pragma unroll
+                for (int b = 0; b < kSPT; b++) s_part[half][quad][b] = mx[b];
+            asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+#pragma unroll
+            for (int b = 0; b < kSPT; b++)
+                mx[b] = fmaxf(fmaxf(s_part[half][0][b], s_part[half][1][b]), fmaxf(s_part[half][2][b], s_part[half][3][b]));
+            asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+#pragma unroll
+            for (int b = 0; b < kSPT; b++) {
+                const float e = (valid && mx[b] != -INFINITY) ? portable_expf(__fsub_rn(acc[b], mx[b])) : 0.0f;
+                const float w = warp_allsum(e);
+                if (lane == 0) s_part[half][quad][b] = w;
+            }
+            asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+            if (quad == 0 && lane < kSPT) {
+                const int b = n0 + half * kSPT + lane;
+                if (b < n && !*abort) {
+                    const float tot = __fadd_rn(__fadd_rn(__fadd_rn(s_part[half][0][lane], s_part[half][1][lane]),
+                                                          s_part[half][2][lane]),
+                                                s_part[half][3][lane]);
+                    float* r = epi.red + ((size_t)b * epi.parts + blockIdx.y) * 2;
+                    r[0] = mx[lane];
+                    r[1] = tot;
+                }
+            }
+        }
     }
     if (threadIdx.x == 64 && S.last) mbar_drain(&S.gather, 0);  // a gather copy never outlives the CTA
     tc_fence_before();

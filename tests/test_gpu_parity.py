@@ -9,7 +9,7 @@ Tolerance against the oracle: max |delta log p| <= 1e-3 nats per token (the engi
 import numpy as np
 import pytest
 
-from conftest import max_dlogp, q8, shared_backend
+from conftest import logsoftmax64, max_dlogp, q8, shared_backend
 from oracle import oracle as O
 from redukt_b200.plugin import BackendResult, PluginBackend
 from redukt_b200.workload import zipf_tokens
@@ -282,3 +282,50 @@ def test_tensor_core_and_cuda_core_projections_bit_identical(small_gauss_rbin, m
             b.set_option("proj_path", 0)
             assert np.array_equal(bits(outs[1]), bits(outs[2])), (path, n)
             assert np.array_equal(bits(outs[(1, "state")][1]), bits(outs[(2, "state")][1])), (path, n)
+
+
+@pytest.mark.parametrize("n", [1, 5, 33, 70, 300])
+def test_fused_head_softmax_matches_softmax_of_logits(small_gauss_rbin, n):
+    """Q8 probabilities come from the tensor-core head's own 128-row tile partials (max and sum of
+    exp) plus one normalising pass; they must agree with the softmax of the same step's logits for
+    every head tile shape (16-, 32- and 64-stream tiles)."""
+    b = backend(q8(small_gauss_rbin))
+    V = b.vocab_size
+    toks = zipf_tokens(n, 2, vocab=V, seed_base=4242)
+    b.batch_init(2 * n)
+    a_slots, p_slots = list(range(n)), list(range(n, 2 * n))
+    for t in range(2):
+        lg = b.forward_batch(a_slots, toks[:, t])
+        pr = b.forward_batch_probs(p_slots, toks[:, t])
+        assert np.all(np.isfinite(pr))
+        assert np.allclose(pr.sum(axis=1, dtype=np.float64), 1.0, atol=1e-5)
+        want = np.exp(logsoftmax64(lg))
+        got = pr.astype(np.float64)
+        assert np.max(np.abs(np.log(got) - np.log(want))) < 1e-5, (n, t)
+    assert b.device_error() == 0
+
+
+def test_softmax_edge_rows_follow_softmax_into(ref_test_rbin):
+    """The normalising pass keeps softmax_into's edge semantics (src/domain/tensor.rs:1917-1933):
+    a row of all -inf is uniform, a row with one finite logit puts all mass on it, and the
+    denominator is max(sum, FLT_EPSILON)."""
+    import torch
+    b = backend(ref_test_rbin)
+    V = 5000
+    rows = np.zeros((4, V), np.float32)
+    rows[0] = -np.inf                                   # all -inf: uniform
+    rows[1] = -np.inf
+    rows[1, 1234] = 3.0                                 # one finite logit
+    rows[2] = np.random.default_rng(1).standard_normal(V).astype(np.float32) * 4
+    rows[3] = -np.inf
+    rows[3, :3] = [-1e30, -1e30, -1e30]                 # finite but tiny: still normalised by its own max
+    d = torch.from_numpy(rows).cuda()
+    o = torch.full_like(d, float("nan"))
+    assert b.libobj.softmax_noalloc(d.data_ptr(), 4, V, o.data_ptr(), 0) == BackendResult.OK
+    torch.cuda.synchronize()
+    p = o.cpu().numpy()
+    assert np.all(p[0] == np.float32(1.0) / np.float32(V))
+    assert p[1, 1234] == 1.0 and np.count_nonzero(p[1]) == 1
+    want = O.softmax(rows[2])
+    assert np.max(np.abs(np.log(p[2].astype(np.float64)) - np.log(want.astype(np.float64)))) < 1e-5
+    assert np.allclose(p[3, :3], 1.0 / 3, rtol=1e-6) and np.count_nonzero(p[3]) == 3
