@@ -28,7 +28,27 @@ def _stale() -> bool:
     return any(os.path.exists(p) and os.path.getmtime(p) > t for p in deps)
 
 
+ARC_LIB = os.path.join(HERE, "libredukt_archive.so")
+ARC_SOURCES = ["rk_archive.cpp"]
+
+
+def build_archive(force: bool = False) -> str:
+    """libredukt_archive.so: the host range coder, CRC-32, container and text workload (C++)."""
+    srcs = [os.path.join(CSRC, s) for s in ARC_SOURCES] + [os.path.join(HERE, "..", "include", "redukt_archive.h")]
+    if not force and os.path.exists(ARC_LIB) and all(os.path.getmtime(p) <= os.path.getmtime(ARC_LIB) for p in srcs):
+        return ARC_LIB
+    cxx = os.environ.get("CXX", "g++")
+    cmd = [cxx, "-O3", "-std=c++17", "-shared", "-fPIC", "-Wall", "-o", ARC_LIB + ".tmp", srcs[0]]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        sys.stderr.write(r.stdout + r.stderr)
+        raise RuntimeError("g++ failed building libredukt_archive.so")
+    os.replace(ARC_LIB + ".tmp", ARC_LIB)
+    return ARC_LIB
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
+    build_archive(force)
     if not force and not _stale():
         return LIB
     nvcc = os.environ.get("NVCC", "nvcc")

@@ -33,3 +33,37 @@ def uniform_tokens(n_streams: int, length: int, vocab: int, seed_base: int = ZIP
     for i in range(n_streams):
         out[i] = np.random.Generator(np.random.PCG64(seed_base + i)).integers(0, vocab, length)
     return out
+
+
+# ---- archive workload: windows of synthetic order-3 Markov text -------------------
+
+ARCHIVE_SEED_BASE = 0x0A4C0000  # window i is sample ARCHIVE_SEED_BASE + i of the Markov source
+ARCHIVE_WINDOW = 10240          # bytes per window
+VOCAB_TRAIN_SEED = 12345        # the sample the archive vocabulary is learned from
+VOCAB_TRAIN_BYTES = 1_000_000
+VOCAB_MAX_LEN = 5               # bytes per vocabulary entry: about 3.6 bytes per token on this source
+
+
+def archive_windows(n: int, first: int = 0, size: int = ARCHIVE_WINDOW):
+    """Windows first .. first + n - 1 of the archive workload (bytes each)."""
+    from redukt_b200.archive import markov_text
+    return [markov_text(ARCHIVE_SEED_BASE + first + i, size) for i in range(n)]
+
+
+def archive_tokenizer(vocab: int, cache_dir: str = None):
+    """The workload's byte-level vocabulary (learned once from a fixed sample; cached as .npz)."""
+    import os
+    from redukt_b200.archive import Tokenizer, markov_text
+    path = os.path.join(cache_dir, f"archive_vocab_{vocab}.npz") if cache_dir else None
+    if path and os.path.exists(path):
+        z = np.load(path)
+        blob, offs = z["blob"].tobytes(), z["offs"]
+        return Tokenizer([blob[offs[i]:offs[i + 1]] for i in range(vocab)])
+    tok = Tokenizer.learn(markov_text(VOCAB_TRAIN_SEED, VOCAB_TRAIN_BYTES), vocab, per_round=2048,
+                          max_len=VOCAB_MAX_LEN)
+    if path:
+        os.makedirs(cache_dir, exist_ok=True)
+        offs = np.zeros(vocab + 1, np.uint64)
+        offs[1:] = np.cumsum([len(t) for t in tok.tokens])
+        np.savez(path, blob=np.frombuffer(b"".join(tok.tokens), np.uint8), offs=offs)
+    return tok

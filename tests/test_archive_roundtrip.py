@@ -277,3 +277,42 @@ def test_rwkv7_archive_bytes_match_cpu_pipeline(tmp_path):
     back = _engine_decode(b, lib, gpu_bytes, T)
     np.testing.assert_array_equal(back, w)
     assert _fused_encode(b, w) == cpu_bytes
+
+
+# ----------------------------------------------------------------------------------------------
+# GPU: the configs[4] workload through the native host side (libredukt_archive.so)
+# ----------------------------------------------------------------------------------------------
+
+@pytest.mark.gpu
+def test_markov_windows_round_trip_with_crc(mamba130m_rbin, model_dir):
+    """16 windows of 10 KB of the synthetic order-3 Markov text, Mamba-130M Q8 with the reset every
+    4096 forwards: compressed in lockstep (device step + CDF, native range coder, RDKT v5 with
+    CRC-32), decompressed in lockstep on the GPU, byte-equal.  A byte flipped inside one window's
+    coded stream is caught: that window fails its size or CRC-32 check, the other windows of the
+    batch still decode exactly."""
+    from conftest import q8, shared_backend
+    from redukt_b200 import archive as A
+    from redukt_b200.workload import archive_tokenizer, archive_windows
+
+    b = shared_backend(q8(mamba130m_rbin))
+    tok = archive_tokenizer(b.vocab_size, model_dir)
+    wins = archive_windows(16)
+    b.batch_init(16)
+    arcs = A.compress_windows(b, wins, tok)
+    assert all(a[:8] == b"RDKT\x05\x00\x00\x00" for a in arcs)
+    for a, w in zip(arcs, wins):
+        h, stream, crc = A.unpack(a)
+        assert h.total_bytes == len(w) and crc == A.crc32(w) and h.reset_log2 == 12
+    back = A.decompress_windows(b, arcs, tok)
+    assert back == wins
+    # the same windows again: the archive is deterministic
+    assert A.compress_windows(b, wins, tok) == arcs
+    # corrupt one byte in the middle of window 5's coded stream
+    bad = bytearray(arcs[5])
+    bad[16 + len(bad) // 3] ^= 0x5A
+    arcs2 = list(arcs)
+    arcs2[5] = bytes(bad)
+    back2 = A.decompress_windows(b, arcs2, tok)
+    assert isinstance(back2[5], A.ArchiveError)
+    assert "CRC-32 mismatch" in str(back2[5]) or "size mismatch" in str(back2[5]) or "corrupt" in str(back2[5])
+    assert [x for i, x in enumerate(back2) if i != 5] == [w for i, w in enumerate(wins) if i != 5]
