@@ -399,6 +399,8 @@ def run_b200(args, rank, world, local, dist):
         res["coder_cdf"] = coder_cdf(b.libobj, n, V, dev, with_cpu=rank == 0 and not args.no_cpu_baseline,
                                      backend=b, windows=windows)
     res["archive_batch"] = archive_batch(b, rank, world, dev, stream, max_over_ranks, barrier, K, W)
+    if not args.no_archive:
+        res["archive"] = archive_run(b, rank, world, args.archive_windows, max_over_ranks, barrier)
     res["determinism"] = determinism(b, rank, world, n, dev, dist)
     with_cpu = rank == 0 and world == 1 and not args.no_cpu_baseline
     if world == 1 and not args.no_sweep:
@@ -445,6 +447,40 @@ def archive_batch(b, rank, world, dev, stream, max_over_ranks, barrier, K, W) ->
     del o, toks
     return {"streams_per_gpu": n, "n_gpus": world, "ms_per_step": round(ms, 4),
             "tok_s": round(world * n / ms * 1e3, 1), "steps": K, "scaling": "weak"}
+
+
+def archive_run(b, rank, world, n, max_over_ranks, barrier) -> dict:
+    """configs[4] on this rank's share: n windows of 10 KB of the synthetic order-3 Markov text
+    (global windows rank*n .. rank*n + n - 1), Mamba-130M Q8, reset every 4096 forwards, compressed
+    in lockstep (device step + coder CDF per token, native range coder, RDKT v5 + CRC-32) and
+    decompressed in lockstep on the GPU; every window must come back byte-exact with its CRC-32
+    passing.  Times are wall clock around each pass (the host coder is part of it), max over ranks."""
+    from redukt_b200 import archive as A
+    from redukt_b200.workload import archive_tokenizer, archive_windows
+    cache = os.environ.get("REDUKT_B200_MODEL_CACHE", os.path.join(tempfile.gettempdir(), "redukt_b200_models"))
+    tok = archive_tokenizer(b.vocab_size, cache)
+    wins = archive_windows(n, first=rank * n)
+    tokens = sum(len(tok.encode(w)) for w in wins)
+    b.batch_init(n)
+    barrier()
+    t0 = time.perf_counter()
+    arcs = A.compress_windows(b, wins, tok)
+    t_enc = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    t0 = time.perf_counter()
+    back = A.decompress_windows(b, arcs, tok)
+    t_dec = max_over_ranks(time.perf_counter() - t0)
+    ok = sum(1 for x, w in zip(back, wins) if x == w)
+    raw = sum(len(w) for w in wins)
+    comp = sum(len(a) for a in arcs)
+    return {"windows_per_gpu": n, "window_bytes": len(wins[0]) if wins else 0, "n_gpus": world,
+            "tokens_per_gpu": tokens, "bytes_per_token": round(raw / max(1, tokens), 3),
+            "compress_tok_s": round(world * tokens / t_enc, 1), "decompress_tok_s": round(world * tokens / t_dec, 1),
+            "compress_s": round(t_enc, 2), "decompress_s": round(t_dec, 2),
+            "round_trip_exact_windows": ok, "crc_checked": True,
+            "bits_per_byte": round(8.0 * comp / max(1, raw), 4),
+            "what": "lockstep archive: redukt_b200_forward_batch_cdf per token + native range coder "
+                    "(libredukt_archive.so), RDKT v5 with CRC-32; no CM ensemble"}
 
 
 def window_hash(b, window: int, steps: int = 8) -> str:
@@ -788,6 +824,8 @@ def main():
     ap.add_argument("--profile-fused", type=int, default=1, choices=[0, 1],
                     help="0: the per-kernel Mamba step even at n <= 32")
     ap.add_argument("--no-cdf", action="store_true", help="skip the coder-CDF measurement")
+    ap.add_argument("--no-archive", action="store_true", help="skip the configs[4] archive round trip")
+    ap.add_argument("--archive-windows", type=int, default=512, help="10 KB windows per GPU for the archive")
     ap.add_argument("--profile-cdf", type=int, default=0,
                     help="run two launches of the CDF kernel over N rows and exit (small case for ncu)")
     args = ap.parse_args()
