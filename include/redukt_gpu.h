@@ -150,6 +150,8 @@ int32_t redukt_b200_info(uint32_t* out, uint32_t n);
  *                  so two CTAs share an SM; 1: the 12-stage tile of the other projections)
  *   "scan_blk"     0/1 = above 64 streams, scan blocks of 16-32 streams per CTA with the channel
  *                  group's weights staged once (1, default) or one stream per CTA (0); same bits
+ *   "large_tile"   0/1 = above 256 streams, tensor-core tiles of 64 streams, one CTA per SM (0) or
+ *                  of 32 streams, two CTAs per SM (1); same bits
  *   "reset_counters" sets every batch slot's periodic-reset counter to `value` (forwards since its
  *                  last reset), e.g. to time the steps around a reset boundary without running the
  *                  window up to it; for benchmarks

@@ -140,6 +140,8 @@ struct Model {
     // fused small-batch step (rk_fused.cuh)
     bool fused = true;          // option "fused"
     bool scan_blk = true;       // option "scan_blk": stream-blocked scan above 64 streams
+    int large_tile = 0;         // option "large_tile": above 256 streams, 0 = 64-stream tensor-core
+                                //   tiles (one CTA per SM), 1 = 32-stream tiles, two CTAs per SM
     int fused_nc = 0;           // norm chunks of the instantiated kernel, 0 = shape not supported
     int head_ctas = 2;          // option "head_ctas": 2 = the two-CTAs-per-SM head tiles at small batch
     bool q8_payload = false;    // the loaded file stores its Q8 matrices quantised (flag bit 6)
@@ -667,6 +669,7 @@ void project(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st) {
         // narrow stream tiles at small n put more CTAs on the weights (re-reads hit L2)
         if (n <= 64) project_tc_bn<16>(m, p, n, epi, st);
         else if (n <= 256) project_tc_bn<32>(m, p, n, epi, st);
+        else if (G.large_tile == 1) project_tc_bn<32, Epi, 6, 2>(m, p, n, epi, st);  // two CTAs per SM
         else project_tc_bn<64>(m, p, n, epi, st);
     } else {
         gemv_q8(m, p.act_q, p.act_e, p.cap_pad, n, epi, st);
@@ -693,6 +696,7 @@ void project_head_softmax(const Pool& p, int n, float* out, int tiles, cudaStrea
     if (n <= 64 && G.head_ctas == 2) project_tc_bn<16, EpiStoreSoftmax, 6, 2>(G.head, p, n, e, st);
     else if (n <= 64) project_tc_bn<16>(G.head, p, n, e, st);
     else if (n <= 256) project_tc_bn<32>(G.head, p, n, e, st);
+    else if (G.large_tile == 1) project_tc_bn<32, EpiStoreSoftmax, 6, 2>(G.head, p, n, e, st);
     else project_tc_bn<64>(G.head, p, n, e, st);
 }
 
@@ -1642,8 +1646,10 @@ int32_t redukt_b200_set_option(const char* key, int64_t value) {
         clear_dev_graphs();
         return BACKEND_OK;
     }
-    if (!strcmp(key, "scan_blk")) {
-        G.scan_blk = value != 0;
+    if (!strcmp(key, "scan_blk") || !strcmp(key, "large_tile")) {
+        if (!strcmp(key, "scan_blk")) G.scan_blk = value != 0;
+        else if (value < 0 || value > 1) return BACKEND_INVALID_ARGUMENT;
+        else G.large_tile = (int)value;
         for (Pool* p : {&G.v1, &G.batch}) {
             for (auto& kv : p->graphs) cudaGraphExecDestroy(kv.second);
             p->graphs.clear();

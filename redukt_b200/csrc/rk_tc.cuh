@@ -426,7 +426,7 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
             send = (G * (sp + 1)) / NS;
         };
         // TMEM column of (stream block u, digit plane p, stream j of the block) = 48u + 16p + j
-        if constexpr (kSPT > 16) {
+        if constexpr (kSPT > 16 || (MB > 1 && kSPT >= 16)) {
             // one group at a time (a double buffer would not fit in registers)
             for (int gl = 0; gl < GL; gl++) {
                 const int g = gb + gl;
