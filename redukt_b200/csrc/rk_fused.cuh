@@ -500,7 +500,41 @@ __device__ __forceinline__ bool run_a(const FusedArgs& a, const StepMeta& m, con
     float* ae = reinterpret_cast<float*>(sm + a.lay.ae);
     float* part = reinterpret_cast<float*>(sm + a.lay.part);
     float* xc = reinterpret_cast<float*>(sm + a.lay.xc);
-    {
+    if (ns == 1) {
+        // one stream (batch 1): every warp computes the stream's norm and emits every eighth
+        // 128-column chunk of its digit planes, so the per-chunk maxima and digit splits run on
+        // eight warps instead of one; the other stream rows of the tile are zero
+        float4 v[NC];
+        load_row_cg<NC>(a.x + (size_t)jb.g0 * a.d, a.d, lane, v);
+        if (!pf.wait(a.err, s_ok)) return false;
+        NormWeights<NC> nw;
+        const float* nws = reinterpret_cast<const float*>(sm + a.lay.a_nw);
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            const int k = c * 128 + lane * 4;
+            nw.w[c] = k < a.d ? *reinterpret_cast<const float4*>(nws + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+            nw.b[c] = (L.norm_b && k < a.d) ? *reinterpret_cast<const float4*>(nws + a.d + k)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        norm_apply<NC>(v, a.d, nw, L.norm_b != nullptr, lane);
+        int8_t* rows = bq;  // stream 0: tile 0, row 0
+        norm_emit_q<NC>(v, a.d, lane, [&](int k, int p1, int p2, int p3, float gs, bool lead) {
+            *reinterpret_cast<int*>(rows + k) = p1;
+            *reinterpret_cast<int*>(rows + 8 * pitch + k) = p2;
+            *reinterpret_cast<int*>(rows + 16 * pitch + k) = p3;
+            if (lead) ae[k / kGroup] = gs;
+        }, 8, warp);
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int s = warp + 8 * u;
+            if (s == 0 || s >= jb.sg) continue;
+            int8_t* zr = bq + (s >> 3) * tile_bytes + (s & 7) * pitch;
+            for (int k = lane * 4; k < a.d; k += 128)
+#pragma unroll
+                for (int p = 0; p < 3; p++) *reinterpret_cast<int*>(zr + p * 8 * pitch + k) = 0;
+            ae[s * kEStride + lane] = 0.0f;
+        }
+    } else {
         // this warp's rows (sga <= 16) are requested before anything waits
         float4 v2[2][NC];
 #pragma unroll
@@ -741,6 +775,109 @@ __device__ __forceinline__ bool run_b(const FusedArgs& a, const StepMeta& m, int
     return true;
 }
 
+// B for a job of one stream (the batch-1 case): four threads per channel, each owning states
+// t, t + 4, t + 8, t + 12, with the dt_proj lanes and the state-output lanes finished by quad
+// shuffles in the trees of the one-thread form (scan_block<4>'s arithmetic), so the 16
+// exponentials of a channel run on four threads.  Same bits as run_b.
+__device__ __forceinline__ bool run_b1(const FusedArgs& a, const StepMeta& m, int l, int job, char* sm,
+                                       float (*s_max)[8], CopyBatch& pf, int* s_ok) {
+    const JobB jb = job_b(a, job);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    float* zs = reinterpret_cast<float*>(sm + a.lay.zs);
+    const int nmb = a.di / 64;
+    const int t = lane & 3, ch = warp * 8 + (lane >> 2), j = jb.g * 64 + ch;
+    const int b = jb.b0;
+    const float xv = __ldcg(a.conv_out + (size_t)b * a.di + j);
+    const float zv = __ldcg(a.z + (size_t)b * a.di + j);
+    {
+        const int nq = a.xr >> 2;
+        if (tid < nq) {  // x_proj sums of the stream, group order
+            const int r4 = tid * 4;
+            const float4* pp = reinterpret_cast<const float4*>(a.xpart + ((size_t)b * nmb) * a.xr + r4);
+            float4 v[kEStride];
+#pragma unroll
+            for (int q = 0; q < kEStride; q++)
+                v[q] = q < nmb ? __ldcg(pp + (size_t)q * (a.xr >> 2)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 tt = v[0];
+#pragma unroll
+            for (int q = 1; q < kEStride; q++) {
+                if (q < nmb) {
+                    tt.x = __fadd_rn(tt.x, v[q].x);
+                    tt.y = __fadd_rn(tt.y, v[q].y);
+                    tt.z = __fadd_rn(tt.z, v[q].z);
+                    tt.w = __fadd_rn(tt.w, v[q].w);
+                }
+            }
+            *reinterpret_cast<float4*>(zs + r4) = tt;
+        }
+    }
+    if (!pf.wait(a.err, s_ok)) return false;  // also publishes zs to the CTA
+    const float* sb = reinterpret_cast<const float*>(sm + a.lay.b_sb);  // [dr + 18][64]
+    const float* dtw = sb;
+    const float* at = sb + a.dr * 64;
+    const float dtb = sb[(a.dr + 16) * 64 + ch], dv = sb[(a.dr + 17) * 64 + ch];
+    const float* pst = reinterpret_cast<const float*>(sm + a.lay.b_ssm);  // stream 0's [16][64]
+    const uint32_t slot = m.slot[b];
+    const bool ok = slot < (uint32_t)a.cap;
+    const bool fresh = m.fresh[b] != 0;
+    float st[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) st[k] = (ok && !fresh) ? pst[(t + 4 * k) * 64 + ch] : 0.0f;
+    // dt_proj: this thread holds 8-lane lanes t and t + 4 of dt_dot8_body's tree
+    const int body = a.dr & ~7;
+    float la = 0.0f, lb = 0.0f;
+    for (int c = 0; c < body; c += 8) {
+        la = __fadd_rn(la, __fmul_rn(dtw[(c + t) * 64 + ch], zs[c + t]));
+        lb = __fadd_rn(lb, __fmul_rn(dtw[(c + t + 4) * 64 + ch], zs[c + t + 4]));
+    }
+    float pr = __fadd_rn(la, lb);
+    pr = __fadd_rn(pr, __shfl_xor_sync(0xffffffffu, pr, 2));
+    float dt = __fadd_rn(pr, __shfl_xor_sync(0xffffffffu, pr, 1));
+    for (int c = body; c < a.dr; c++) dt = __fadd_rn(dt, __fmul_rn(dtw[c * 64 + ch], zs[c]));
+    dt = softplus(__fadd_rn(dt, dtb));
+    const float* B = zs + a.dr;
+    const float* C = zs + a.dr + kDState;
+    const bool update = !(fabsf(dt) < 1e-6f);
+    if (update) {
+        const float dtx = __fmul_rn(dt, xv);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int n2 = t + 4 * k;
+            const float da = lane_expf(__fsub_rn(0.0f, __fmul_rn(dt, at[n2 * 64 + ch])));
+            st[k] = __fadd_rn(__fmul_rn(da, st[k]), __fmul_rn(dtx, B[n2]));
+        }
+    }
+    if (ok && (update || fresh)) {
+        float* sp = a.ssm + ssm_off(l, a.cap, slot, a.di, 0, j);
+#pragma unroll
+        for (int k = 0; k < 4; k++) sp[(t + 4 * k) * 64] = st[k];
+    }
+    // hsum_ssm: lanes t and t + 4 here, then xor 1 and xor 2 across the quad
+    const float l0 = __fadd_rn(__fmul_rn(st[0], C[t]), __fmul_rn(st[2], C[t + 8]));
+    const float l4 = __fadd_rn(__fmul_rn(st[1], C[t + 4]), __fmul_rn(st[3], C[t + 12]));
+    float h = __fadd_rn(l0, l4);
+    h = __fadd_rn(h, __shfl_xor_sync(0xffffffffu, h, 1));
+    h = __fadd_rn(h, __shfl_xor_sync(0xffffffffu, h, 2));
+    const float y = __fadd_rn(h, __fmul_rn(dv, xv));
+    const float gated = ok ? __fmul_rn(y, __fmul_rn(zv, lane_sigmoid(zv))) : 0.0f;
+    // digit planes over the group's 64 channels (all eight warps)
+    float mx = warp_allmax(fabsf(gated));
+    if (lane == 0) s_max[0][warp] = mx;
+    __syncthreads();
+    mx = s_max[0][0];
+#pragma unroll
+    for (int w = 1; w < 8; w++) mx = fmaxf(mx, s_max[0][w]);
+    if (ok && t == 0) {
+        float ginv, gs = group_scale(mx, &ginv);
+        const Digits3 dg = split_digits(gated, ginv);
+        a.act_q[dq_off(a.cap_pad, 0, b, j)] = (int8_t)dg.d1;
+        a.act_q[dq_off(a.cap_pad, 1, b, j)] = (int8_t)dg.d2;
+        a.act_q[dq_off(a.cap_pad, 2, b, j)] = (int8_t)dg.d3;
+        if (ch == 0) a.act_e[(size_t)b * kEStride + jb.g] = gs;
+    }
+    return true;
+}
+
 // C: out_proj + residual for mc rows x 8 streams; one (16-row tile, split) per warp task.  The
 // streams' digit planes arrive as the scan wrote them (8-row halves of the tiled layout, 64-byte
 // swizzled rows), one bulk copy per (group, plane).
@@ -839,7 +976,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_step_fused(FusedArgs a) {
                 __syncthreads();
                 prefetch_b(a, meta, L, l, job, sm, pf);
             }
-            if (!run_b(a, meta, l, job, sm, s_max, pf, &s_ok)) return drain();
+            const bool one = min(a.sgb, a.n - job_b(a, job).b0) == 1;
+            if (!(one ? run_b1(a, meta, l, job, sm, s_max, pf, &s_ok) : run_b(a, meta, l, job, sm, s_max, pf, &s_ok)))
+                return drain();
         }
         grid_arrive(a.bar, target);
         if (first < jc) prefetch_c(a, L, first, sm, pf);

@@ -255,10 +255,13 @@ __device__ __forceinline__ void norm_apply(float4 (&v)[NC], int d, const NormWei
 // Digit planes of a normalised row over 64-column groups: lanes 0-15 hold group 2c, lanes 16-31
 // group 2c+1.  sink(k, d1x4, d2x4, d3x4, gs, lead) receives lane-packed digits of columns
 // k .. k+3 (k < d only); `lead` marks the group's first lane, which also passes the exponent.
+// (cmod, crem): emit only the chunks c with c % cmod == crem (several warps sharing one stream).
 template <int NC, class Sink>
-__device__ __forceinline__ void norm_emit_q(const float4 (&o)[NC], int d, int lane, Sink sink) {
+__device__ __forceinline__ void norm_emit_q(const float4 (&o)[NC], int d, int lane, Sink sink, int cmod = 1,
+                                            int crem = 0) {
 #pragma unroll
     for (int c = 0; c < NC; c++) {
+        if (c % cmod != crem) continue;
         int k = c * 128 + lane * 4;
         float m = fmaxf(fmaxf(fabsf(o[c].x), fabsf(o[c].y)), fmaxf(fabsf(o[c].z), fabsf(o[c].w)));
         m = warp_allmax(m, 16);
