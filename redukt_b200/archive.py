@@ -314,9 +314,10 @@ def decompress_windows(backend, archives: Sequence[bytes], tok: Tokenizer) -> Li
             bad = q[:, 1] == 0xFFFFFFFF
             if bad.any():
                 failed[act[bad]] = True
-            _check(L.rk_dec_update_batch(cod.h, int((~bad).sum()), act[~bad].ctypes.data,
-                                         np.ascontiguousarray(q[~bad]).ctypes.data, TOTAL), "decode step")
-            for s, y in zip(act[~bad], q[~bad, 0]):
+            ok_s = np.ascontiguousarray(act[~bad])  # kept alive across the native call
+            ok_q = np.ascontiguousarray(q[~bad])
+            _check(L.rk_dec_update_batch(cod.h, len(ok_s), ok_s.ctypes.data, ok_q.ctypes.data, TOTAL), "decode step")
+            for s, y in zip(ok_s, ok_q[:, 0]):
                 toks[s].append(int(y))
                 got[s] += lengths[y]
         for s in range(n):
