@@ -206,7 +206,7 @@ bool pool_alloc(Pool* p, uint32_t cap) {
     size_t n = cap, L = G.nl, d = G.d, di = G.di, V = G.V;
     size_t parts = std::max((V + kSoftmaxTile - 1) / kSoftmaxTile, (V + tc::kBM - 1) / tc::kBM);  // softmax partials
     const size_t dib = (size_t)state_blocks((int)di) * 64;  // d_inner in whole 64-channel blocks
-    bool ok = dalloc(&p->conv, L * n * (kDConv - 1) * dib) && dalloc(&p->ssm, L * n * kDState * dib) &&
+    bool ok = dalloc(&p->conv, L * n * (kDConv - 1) * di) && dalloc(&p->ssm, L * n * kDState * dib) &&
               dalloc(&p->since, n) && dalloc(&p->x, n * d) && dalloc(&p->conv_out, n * di) &&
               dalloc(&p->z, n * di) && dalloc(&p->xpart, n * ((di + 63) / 64) * G.xr) && dalloc(&p->zp, n * G.xr) &&
               dalloc(&p->xcount, (n + 15) / 16) && dalloc(&p->logits, n * V) &&
@@ -1112,7 +1112,7 @@ int pool_reset(Pool& p, const uint32_t* slots, uint32_t n) {
     if (!slots) {
         size_t L = G.nl, cap = p.cap, di = G.di;
         const size_t dib = (size_t)state_blocks((int)di) * 64;
-        CK(cudaMemsetAsync(p.conv, 0, L * cap * (kDConv - 1) * dib * sizeof(float), G.stream), BACKEND_FORWARD_FAILED);
+        CK(cudaMemsetAsync(p.conv, 0, L * cap * (kDConv - 1) * di * sizeof(float), G.stream), BACKEND_FORWARD_FAILED);
         CK(cudaMemsetAsync(p.ssm, 0, L * cap * kDState * dib * sizeof(float), G.stream), BACKEND_FORWARD_FAILED);
         CK(cudaMemsetAsync(p.since, 0, cap * sizeof(uint32_t), G.stream), BACKEND_FORWARD_FAILED);
         CK(cudaStreamSynchronize(G.stream), BACKEND_FORWARD_FAILED);
@@ -1125,7 +1125,7 @@ int pool_reset(Pool& p, const uint32_t* slots, uint32_t n) {
     if (n == 0) return BACKEND_OK;
     CK(cudaMemcpyAsync(p.d_slots, p.h_slots, (size_t)n * sizeof(uint32_t), cudaMemcpyHostToDevice, G.stream),
        BACKEND_FORWARD_FAILED);
-    int per = (3 + kDState) * state_blocks(G.di) * 64;
+    int per = 3 * G.di + kDState * state_blocks(G.di) * 64;
     k_zero_slots<<<dim3((per + 255) / 256, n, G.nl), 256, 0, G.stream>>>(p.d_slots, (int)n, (int)p.cap, G.nl, G.di,
                                                                          p.conv, p.ssm, p.since);
     CK(cudaGetLastError(), BACKEND_FORWARD_FAILED);
@@ -1436,7 +1436,7 @@ int32_t redukt_b200_get_state(uint32_t slot, float* conv, float* ssm) {
     std::vector<float> tmp((size_t)kDState * dib);
     for (int l = 0; l < G.nl; l++) {  // channel-blocked device layout -> the reference's [di][k]
         if (conv) {
-            CK(cudaMemcpy(tmp.data(), p->conv + conv_off(l, cap, slot, di, 0, 0), (kDConv - 1) * dib * sizeof(float),
+            CK(cudaMemcpy(tmp.data(), p->conv + conv_off(l, cap, slot, di, 0, 0), (size_t)(kDConv - 1) * di * sizeof(float),
                           cudaMemcpyDeviceToHost), BACKEND_FORWARD_FAILED);
             for (int j = 0; j < di; j++)
                 for (int k = 0; k < kDConv - 1; k++)

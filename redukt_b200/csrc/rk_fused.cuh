@@ -618,8 +618,8 @@ __device__ __forceinline__ bool run_a(const FusedArgs& a, const StepMeta& m, con
             }
             float* st = a.conv + conv_off(l, a.cap, slot, a.di, 0, j);
             st[0] = s1;
-            st[64] = s2;
-            st[128] = tot;
+            st[a.di] = s2;
+            st[2 * a.di] = tot;
             co = conv_silu_taps(s0, s1, s2, tot, ct[rl], ct[64 + rl], ct[128 + rl], ct[192 + rl], ct[256 + rl]);
             a.conv_out[(size_t)b * a.di + j] = co;
         }

@@ -15,9 +15,9 @@
 //
 // Layouts in HBM (all row-major):
 //   weights      f32 [rows][K] or int8 [rows][K] + f32 scales [rows][K/64]
-//   conv state   f32 [layer][slot][d_inner/64][dc-1][64]   (64-channel blocks, channel fastest:
-//   ssm state    f32 [layer][slot][d_inner/64][d_state][64]  coalesced per tap / state index, and
-//                one (slot, channel block) is one contiguous piece: 768 B conv, 4 KiB ssm)
+//   conv state   f32 [layer][slot][dc-1][d_inner]          (channel fastest: coalesced per tap)
+//   ssm state    f32 [layer][slot][d_inner/64][d_state][64]  (64-channel blocks, channel fastest:
+//                coalesced per state index, and one (slot, channel block) is 4 KiB contiguous)
 //   activations  f32 [stream][K], or int8 digit planes [3][stream][K] + f32 2^e [stream][K/64]
 #pragma once
 #include "rk_math.cuh"
@@ -28,11 +28,12 @@ constexpr int kDState = 16;
 constexpr int kDConv = 4;
 constexpr int kGroup = 64;
 
-// Offsets of state element (tap or state index k, channel j) of a (layer, slot) in the
-// channel-blocked state layout above; d_inner is padded to whole 64-channel blocks.
+// Offsets of state element (tap or state index k, channel j) of a (layer, slot) in the layouts
+// above; the SSM state pads d_inner to whole 64-channel blocks.  (A channel-blocked conv state was
+// measured: the F32 path's per-(row, stream) epilogue ran 2.3x slower on it.)
 __host__ __device__ __forceinline__ int state_blocks(int di) { return (di + 63) >> 6; }
 __host__ __device__ __forceinline__ size_t conv_off(int layer, int cap, uint32_t slot, int di, int k, int j) {
-    return ((((size_t)layer * cap + slot) * state_blocks(di) + (j >> 6)) * (kDConv - 1) + k) * 64 + (j & 63);
+    return (((size_t)layer * cap + slot) * (kDConv - 1) + k) * di + j;
 }
 __host__ __device__ __forceinline__ size_t ssm_off(int layer, int cap, uint32_t slot, int di, int k, int j) {
     return ((((size_t)layer * cap + slot) * state_blocks(di) + (j >> 6)) * kDState + k) * 64 + (j & 63);
@@ -441,12 +442,12 @@ struct EpiInProj {
         float s0 = 0.f, s1 = 0.f, s2 = 0.f;
         if (!rflag[b]) {
             s0 = st[0];
-            s1 = st[64];
-            s2 = st[128];
+            s1 = st[di];
+            s2 = st[2 * di];
         }
         st[0] = s1;
-        st[64] = s2;
-        st[128] = v;
+        st[di] = s2;
+        st[2 * di] = v;
         conv_out[(size_t)b * di + j] = conv_silu(j, s0, s1, s2, v);
     }
 
@@ -486,15 +487,15 @@ struct EpiInProj {
 #pragma unroll
         for (int i = 0; i < CH; i++) {
             s0[i] = rd[i] ? st[i][0] : 0.0f;
-            s1[i] = rd[i] ? st[i][64] : 0.0f;
-            s2[i] = rd[i] ? st[i][128] : 0.0f;
+            s1[i] = rd[i] ? st[i][di] : 0.0f;
+            s2[i] = rd[i] ? st[i][2 * di] : 0.0f;
         }
 #pragma unroll
         for (int i = 0; i < CH; i++) {
             if (!live[i]) continue;
             st[i][0] = s1[i];
-            st[i][64] = s2[i];
-            st[i][128] = v[i];
+            st[i][di] = s2[i];
+            st[i][2 * di] = v[i];
             conv_out[(size_t)(b0 + i) * di + j] = conv_silu(j, s0[i], s1[i], s2[i], v[i]);
         }
     }
@@ -522,15 +523,15 @@ struct EpiInProj {
         for (int i = 0; i < CH; i++) {
             bool rd = live[i] && !fresh[i];
             s0[i] = rd ? st[i][0] : 0.0f;
-            s1[i] = rd ? st[i][64] : 0.0f;
-            s2[i] = rd ? st[i][128] : 0.0f;
+            s1[i] = rd ? st[i][di] : 0.0f;
+            s2[i] = rd ? st[i][2 * di] : 0.0f;
         }
 #pragma unroll
         for (int i = 0; i < CH; i++) {
             if (!live[i]) continue;
             st[i][0] = s1[i];
-            st[i][64] = s2[i];
-            st[i][128] = v[i];
+            st[i][di] = s2[i];
+            st[i][2 * di] = v[i];
             conv_out[(size_t)(b0 + i) * di + j] = conv_silu(j, s0[i], s1[i], s2[i], v[i]);
         }
     }
@@ -1205,7 +1206,7 @@ __global__ void __launch_bounds__(256) k_scan_blk(ScanArgs a, ActOut out, int n)
 // Zero the conv and SSM state of the listed slots in every layer, and their reset counters.
 __global__ void k_zero_slots(const uint32_t* __restrict__ slots, int n_slots, int cap, int layers, int di,
                              float* __restrict__ conv, float* __restrict__ ssm, uint32_t* __restrict__ since) {
-    const int cb = state_blocks(di) * 64 * (kDConv - 1), sb = state_blocks(di) * 64 * kDState;
+    const int cb = (kDConv - 1) * di, sb = state_blocks(di) * 64 * kDState;
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     int k = blockIdx.y;
     int layer = blockIdx.z;
