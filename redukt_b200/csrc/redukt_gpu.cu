@@ -590,12 +590,21 @@ void gemv_f32(int M, int K, const float* W, const float* act, int ld, int n, Epi
 }
 
 // x_proj of every profile: group chains into p.xpart[b][g][r], summed in group order into p.zp.
+// Above 128 streams, 64-stream tiles (the group's weights staged once per 64 streams, 4 x 8
+// register blocks); the chains and their group-order sums are the same either way.
 void launch_xproj(const float* W, const Pool& p, int n, cudaStream_t st) {
     const int ng = (G.di + kXGroup - 1) / kXGroup;
+    if (n > 128) {
+        const size_t smem = ((size_t)G.xr * 68 + 64 * 68) * sizeof(float);
+        allow_smem(k_xproj_part<64, 4, 8>, smem);
+        launch(k_xproj_part<64, 4, 8>, dim3(ng, (n + 63) / 64), dim3(256), smem, st, G.xr, G.di, W,
+               (const float*)p.conv_out, n, p.xpart, p.zp, p.xcount);
+        return;
+    }
     const size_t smem = ((size_t)G.xr * 68 + 16 * 68) * sizeof(float);
-    allow_smem(k_xproj_part, smem);
-    launch(k_xproj_part, dim3(ng, (n + 15) / 16), dim3(256), smem, st, G.xr, G.di, W, (const float*)p.conv_out, n,
-           p.xpart, p.zp, p.xcount);
+    allow_smem(k_xproj_part<16, 2, 4>, smem);
+    launch(k_xproj_part<16, 2, 4>, dim3(ng, (n + 15) / 16), dim3(256), smem, st, G.xr, G.di, W,
+           (const float*)p.conv_out, n, p.xpart, p.zp, p.xcount);
 }
 
 template <int NS, int GI, class Epi>

@@ -690,17 +690,21 @@ __device__ __forceinline__ void xproj_sum_groups(const float* pb, int G, int M, 
     }
 }
 
-// Group chains of x_proj for one 64-channel group and up to 16 streams: part[b][g][r].  Grid
-// (groups, stream tiles of 16).  The group's weights [M][64] and activations [16][64] are staged in
-// shared memory (rows padded to 68 floats), and each thread runs a 2-row x 4-stream block of chains
-// with 16-byte shared loads.  The last of a stream tile's G CTAs (a per-tile arrival counter, reset
-// by that CTA) adds each (stream, row)'s chains in group order into zp[b][r].
+// Group chains of x_proj for one 64-channel group and a tile of SPB streams: part[b][g][r].  Grid
+// (groups, stream tiles).  The group's weights [M][64] and activations [SPB][64] are staged in
+// shared memory (rows padded to 68 floats), and each thread runs an RB-row x SK-stream block of
+// chains with 16-byte shared loads (each weight and activation load feeds several chains); large
+// batches use 64-stream tiles with 4 x 8 blocks, so the weights are staged once per 64 streams.
+// The last of a stream tile's G CTAs (a per-tile arrival counter, reset by that CTA) adds each
+// (stream, row)'s chains in group order into zp[b][r].
+template <int SPB, int RB, int SK>
 __global__ void __launch_bounds__(256) k_xproj_part(int M, int K, const float* __restrict__ W, const float* act,
                                                     int n, float* part, float* zp, uint32_t* tile_count) {
+    static_assert(SPB % SK == 0, "stream blocks tile the stream tile");
     extern __shared__ float4 smem_f4[];
     float* xw = reinterpret_cast<float*>(smem_f4);  // [M][68]
-    float* xc = xw + M * 68;                         // [16][68]
-    const int g = blockIdx.x, G = gridDim.x, b0 = blockIdx.y * 16, ns = min(16, n - b0);
+    float* xc = xw + M * 68;                         // [SPB][68]
+    const int g = blockIdx.x, G = gridDim.x, b0 = blockIdx.y * SPB, ns = min(SPB, n - b0);
     const int c0 = g * kXGroup, len = min(kXGroup, K - c0);
     const int tid = threadIdx.x;
     // the weights are constant: staged before the dependency wait, eight loads in flight per
@@ -720,60 +724,60 @@ __global__ void __launch_bounds__(256) k_xproj_part(int M, int K, const float* _
     }
     pdl_wait();
     pdl_trigger();
-    {
+    for (int base = 0; base < SPB * 64; base += 4 * 256) {
         float v[4];
 #pragma unroll
         for (int u = 0; u < 4; u++) {
-            const int i = u * 256 + tid, sidx = i >> 6, c = i & 63;
-            v[u] = (sidx < ns && c < len) ? act[(size_t)(b0 + sidx) * K + c0 + c] : 0.0f;
+            const int i = base + u * 256 + tid, sidx = i >> 6, c = i & 63;
+            v[u] = (i < SPB * 64 && sidx < ns && c < len) ? act[(size_t)(b0 + sidx) * K + c0 + c] : 0.0f;
         }
 #pragma unroll
         for (int u = 0; u < 4; u++) {
-            const int i = u * 256 + tid;
-            xc[(i >> 6) * 68 + (i & 63)] = v[u];
+            const int i = base + u * 256 + tid;
+            if (i < SPB * 64) xc[(i >> 6) * 68 + (i & 63)] = v[u];
         }
     }
     __syncthreads();
-    const int nsb = (ns + 3) >> 2, nblk = ((M + 1) >> 1) * nsb;
+    const int nsb = (ns + SK - 1) / SK, nblk = ((M + RB - 1) / RB) * nsb;
     for (int t = tid; t < nblk; t += 256) {
-        const int r0 = (t / nsb) * 2, s0 = (t % nsb) * 4;
-        const float* w0 = xw + r0 * 68;
-        const float* w1 = xw + min(r0 + 1, M - 1) * 68;
-        float acc[2][4];
+        const int r0 = (t / nsb) * RB, s0 = (t % nsb) * SK;
+        const float* wr[RB];
 #pragma unroll
-        for (int i = 0; i < 2; i++)
+        for (int i = 0; i < RB; i++) wr[i] = xw + min(r0 + i, M - 1) * 68;
+        float acc[RB][SK];
 #pragma unroll
-            for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+        for (int i = 0; i < RB; i++)
+#pragma unroll
+            for (int j = 0; j < SK; j++) acc[i][j] = 0.0f;
         if (len == kXGroup) {
-#pragma unroll 4
+#pragma unroll 2
             for (int c = 0; c < 64; c += 4) {
-                const float4 wa = *reinterpret_cast<const float4*>(w0 + c);
-                const float4 wb = *reinterpret_cast<const float4*>(w1 + c);
+                float4 w4[RB];
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
+                for (int i = 0; i < RB; i++) w4[i] = *reinterpret_cast<const float4*>(wr[i] + c);
+#pragma unroll
+                for (int j = 0; j < SK; j++) {
                     const float4 xv = *reinterpret_cast<const float4*>(xc + (s0 + j) * 68 + c);
-                    acc[0][j] = __fmaf_rn(wa.x, xv.x, acc[0][j]);
-                    acc[0][j] = __fmaf_rn(wa.y, xv.y, acc[0][j]);
-                    acc[0][j] = __fmaf_rn(wa.z, xv.z, acc[0][j]);
-                    acc[0][j] = __fmaf_rn(wa.w, xv.w, acc[0][j]);
-                    acc[1][j] = __fmaf_rn(wb.x, xv.x, acc[1][j]);
-                    acc[1][j] = __fmaf_rn(wb.y, xv.y, acc[1][j]);
-                    acc[1][j] = __fmaf_rn(wb.z, xv.z, acc[1][j]);
-                    acc[1][j] = __fmaf_rn(wb.w, xv.w, acc[1][j]);
+#pragma unroll
+                    for (int i = 0; i < RB; i++) {
+                        acc[i][j] = __fmaf_rn(w4[i].x, xv.x, acc[i][j]);
+                        acc[i][j] = __fmaf_rn(w4[i].y, xv.y, acc[i][j]);
+                        acc[i][j] = __fmaf_rn(w4[i].z, xv.z, acc[i][j]);
+                        acc[i][j] = __fmaf_rn(w4[i].w, xv.w, acc[i][j]);
+                    }
                 }
             }
         } else {  // a last, shorter group (F32 shapes only)
             for (int c = 0; c < len; c++)
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    acc[0][j] = __fmaf_rn(w0[c], xc[(s0 + j) * 68 + c], acc[0][j]);
-                    acc[1][j] = __fmaf_rn(w1[c], xc[(s0 + j) * 68 + c], acc[1][j]);
-                }
+                for (int j = 0; j < SK; j++)
+#pragma unroll
+                    for (int i = 0; i < RB; i++) acc[i][j] = __fmaf_rn(wr[i][c], xc[(s0 + j) * 68 + c], acc[i][j]);
         }
 #pragma unroll
-        for (int i = 0; i < 2; i++)
+        for (int i = 0; i < RB; i++)
 #pragma unroll
-            for (int j = 0; j < 4; j++)
+            for (int j = 0; j < SK; j++)
                 if (r0 + i < M && s0 + j < ns) part[((size_t)(b0 + s0 + j) * G + g) * M + r0 + i] = acc[i][j];
     }
     __shared__ int s_last;
