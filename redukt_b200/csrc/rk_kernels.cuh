@@ -738,12 +738,15 @@ __global__ void __launch_bounds__(256) k_xproj_part(int M, int K, const float* _
         }
     }
     __syncthreads();
-    const int nsb = (ns + SK - 1) / SK, nblk = ((M + RB - 1) / RB) * nsb;
+    // thread (row set rq, stream lane sl) runs rows rq + RQ i and streams sl + SQ j: consecutive
+    // lanes read consecutive 68-float rows, so a warp's 16-byte shared loads hit distinct banks
+    constexpr int SQ = SPB / SK;
+    const int RQ = (M + RB - 1) / RB, nblk = RQ * SQ;
     for (int t = tid; t < nblk; t += 256) {
-        const int r0 = (t / nsb) * RB, s0 = (t % nsb) * SK;
+        const int rq = t / SQ, sl = t - rq * SQ;
         const float* wr[RB];
 #pragma unroll
-        for (int i = 0; i < RB; i++) wr[i] = xw + min(r0 + i, M - 1) * 68;
+        for (int i = 0; i < RB; i++) wr[i] = xw + min(rq + RQ * i, M - 1) * 68;
         float acc[RB][SK];
 #pragma unroll
         for (int i = 0; i < RB; i++)
@@ -757,7 +760,7 @@ __global__ void __launch_bounds__(256) k_xproj_part(int M, int K, const float* _
                 for (int i = 0; i < RB; i++) w4[i] = *reinterpret_cast<const float4*>(wr[i] + c);
 #pragma unroll
                 for (int j = 0; j < SK; j++) {
-                    const float4 xv = *reinterpret_cast<const float4*>(xc + (s0 + j) * 68 + c);
+                    const float4 xv = *reinterpret_cast<const float4*>(xc + (sl + SQ * j) * 68 + c);
 #pragma unroll
                     for (int i = 0; i < RB; i++) {
                         acc[i][j] = __fmaf_rn(w4[i].x, xv.x, acc[i][j]);
@@ -772,13 +775,15 @@ __global__ void __launch_bounds__(256) k_xproj_part(int M, int K, const float* _
 #pragma unroll
                 for (int j = 0; j < SK; j++)
 #pragma unroll
-                    for (int i = 0; i < RB; i++) acc[i][j] = __fmaf_rn(wr[i][c], xc[(s0 + j) * 68 + c], acc[i][j]);
+                    for (int i = 0; i < RB; i++) acc[i][j] = __fmaf_rn(wr[i][c], xc[(sl + SQ * j) * 68 + c], acc[i][j]);
         }
 #pragma unroll
         for (int i = 0; i < RB; i++)
 #pragma unroll
-            for (int j = 0; j < SK; j++)
-                if (r0 + i < M && s0 + j < ns) part[((size_t)(b0 + s0 + j) * G + g) * M + r0 + i] = acc[i][j];
+            for (int j = 0; j < SK; j++) {
+                const int r = rq + RQ * i, sidx = sl + SQ * j;
+                if (r < M && sidx < ns) part[((size_t)(b0 + sidx) * G + g) * M + r] = acc[i][j];
+            }
     }
     __shared__ int s_last;
     __syncthreads();
