@@ -75,22 +75,25 @@ def rwkv7_bytes(d: rwkv7_rbin.Rwkv7Dims):
     return weights, per_stream
 
 
-def kernel_bytes(cls: str, n: int, dims: rbin.MambaDims, profile: str) -> int:
-    """Algorithmic bytes of ONE launch of a kernel class for n streams."""
+def kernel_bytes(cls: str, n: int, dims: rbin.MambaDims, profile: str, conv_in_xproj: bool = True) -> int:
+    """Algorithmic bytes of ONE launch of a kernel class for n streams.  The conv1d state (read and
+    written) and the conv output belong to x_proj when it runs the conv (option conv_defer, the
+    default), else to in_proj's epilogue."""
     d, di, xr, dr, V = dims.d_model, dims.d_inner, dims.xr, dims.dt_rank, dims.vocab
     q8 = profile != "f32"
     act = (lambda K: n * (3 * K + (K // 64) * 4)) if q8 else (lambda K: n * K * 4)
     mat = (lambda r, c: r * c + r * (c // 64) * 4) if q8 else (lambda r, c: r * c * 4)
     if cls == "scan":
         return (n * di * 16 * 4 * 2 + (di * dr + di + 16 * di + di) * 4 + n * (xr + 2 * di) * 4 + act(di))
+    conv = n * di * 3 * 4 * 2 + 5 * di * 4 + n * di * 4  # state R/W, taps + bias, one [n][di] pass
     if cls == "in_proj":
-        return mat(2 * di, d) + act(d) + n * di * 3 * 4 * 2 + 5 * di * 4 + n * 2 * di * 4
+        return mat(2 * di, d) + act(d) + n * 2 * di * 4 + (0 if conv_in_xproj else conv)
     if cls == "out_proj":
         return mat(d, di) + act(di) + n * d * 4 * 2
     if cls == "head":
         return mat(V, d) + act(d) + n * V * 4
     if cls == "x_proj":
-        return xr * di * 4 + n * di * 4 + n * xr * 4
+        return xr * di * 4 + n * di * 4 + n * xr * 4 + (conv if conv_in_xproj else 0)
     if cls == "norm":
         return n * d * 4 + d * 4 + act(d)
     if cls == "embed":

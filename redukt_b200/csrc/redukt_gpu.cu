@@ -140,6 +140,8 @@ struct Model {
     // fused small-batch step (rk_fused.cuh)
     bool fused = true;          // option "fused"
     bool scan_blk = true;       // option "scan_blk": stream-blocked scan above 64 streams
+    bool conv_defer = true;     // option "conv_defer": conv1d + SiLU in the x_proj kernel's staging
+                                //   pass (1) or in the in_proj epilogue (0); the same bits
     int large_tile = 0;         // option "large_tile": above 256 streams, 0 = 64-stream tensor-core
                                 //   tiles (one CTA per SM), 1 = 32-stream tiles, two CTAs per SM
     int fused_nc = 0;           // norm chunks of the instantiated kernel, 0 = shape not supported
@@ -592,19 +594,28 @@ void gemv_f32(int M, int K, const float* W, const float* act, int ld, int n, Epi
 // x_proj of every profile: group chains into p.xpart[b][g][r], summed in group order into p.zp.
 // Above 128 streams, 64-stream tiles (the group's weights staged once per 64 streams, 4 x 8
 // register blocks); the chains and their group-order sums are the same either way.
-void launch_xproj(const float* W, const Pool& p, int n, cudaStream_t st) {
+// The in_proj epilogue of layer li: with conv_defer the x-branch is stored before the conv and
+// launch_xproj runs conv1d + SiLU in its staging pass (same arithmetic, same bits).
+EpiInProj in_proj_epi(const Layer& L, int li, const Pool& p, const uint32_t* vs) {
+    EpiInProj e{G.di, (int)p.cap, li, vs, p.rflag, p.conv, L.conv_t, L.conv_b, p.conv_out, p.z};
+    e.defer = G.conv_defer;
+    return e;
+}
+
+void launch_xproj(const Layer& L, int li, const Pool& p, int n, const uint32_t* vs, cudaStream_t st) {
     const int ng = (G.di + kXGroup - 1) / kXGroup;
+    XConv cv{G.conv_defer, (int)p.cap, li, vs, p.rflag, p.conv, L.conv_t, L.conv_b, p.conv_out};
     if (n > 128) {
         const size_t smem = ((size_t)G.xr * 68 + 64 * 68) * sizeof(float);
         allow_smem(k_xproj_part<64, 4, 8>, smem);
-        launch(k_xproj_part<64, 4, 8>, dim3(ng, (n + 63) / 64), dim3(256), smem, st, G.xr, G.di, W,
-               (const float*)p.conv_out, n, p.xpart, p.zp, p.xcount);
+        launch(k_xproj_part<64, 4, 8>, dim3(ng, (n + 63) / 64), dim3(256), smem, st, G.xr, G.di, (const float*)L.x_proj,
+               (const float*)p.conv_out, n, p.xpart, p.zp, p.xcount, cv);
         return;
     }
     const size_t smem = ((size_t)G.xr * 68 + 16 * 68) * sizeof(float);
     allow_smem(k_xproj_part<16, 2, 4>, smem);
-    launch(k_xproj_part<16, 2, 4>, dim3(ng, (n + 15) / 16), dim3(256), smem, st, G.xr, G.di, W,
-           (const float*)p.conv_out, n, p.xpart, p.zp, p.xcount);
+    launch(k_xproj_part<16, 2, 4>, dim3(ng, (n + 15) / 16), dim3(256), smem, st, G.xr, G.di, (const float*)L.x_proj,
+           (const float*)p.conv_out, n, p.xpart, p.zp, p.xcount, cv);
 }
 
 template <int NS, int GI, class Epi>
@@ -969,17 +980,17 @@ int enqueue_step(Pool& p, int n, const uint32_t* d_slots, const uint32_t* d_toke
         }
         {
             KScope k(kKInProj, st);
-            EpiInProj ein{G.di, (int)p.cap, li, vs, p.rflag, p.conv, L.conv_t, L.conv_b, p.conv_out, p.z};
-            project(L.in_proj, p, n, ein, st);
+            project(L.in_proj, p, n, in_proj_epi(L, li, p, vs), st);
         }
         {
             KScope k(kKXProj, st);
-            launch_xproj(L.x_proj, p, n, st);
+            launch_xproj(L, li, p, n, vs, st);
         }
         {
             KScope k(kKScan, st);
             ScanArgs sc{G.di, G.dr, G.xr, (int)p.cap, li, vs, p.rflag, p.zp, p.conv_out, p.z,
                         L.dt_wt, L.dt_b, L.a_t, L.dvec, p.ssm};
+            sc.x_late = G.conv_defer;
             ActOut ao{p.act_f, p.act_q, p.act_e, p.cap_pad, G.di};
             if (G.profile != kF32) ao.f = nullptr;
             else ao.q = nullptr;
@@ -1539,13 +1550,13 @@ int32_t redukt_b200_time_kernel(int32_t cls, uint32_t n, uint32_t reps, float* m
                 const Layer& L = G.layers[li];
                 if (cls == kKNorm) launch_norm(p, nn, L.norm_w, L.norm_b, G.d, st);
                 if (cls == kKInProj) {
-                    EpiInProj ein{G.di, (int)p.cap, li, p.d_slots, p.rflag, p.conv, L.conv_t, L.conv_b, p.conv_out, p.z};
-                    project(L.in_proj, p, nn, ein, st);
+                    project(L.in_proj, p, nn, in_proj_epi(L, li, p, p.d_slots), st);
                 }
-                if (cls == kKXProj) launch_xproj(L.x_proj, p, nn, st);
+                if (cls == kKXProj) launch_xproj(L, li, p, nn, p.d_slots, st);
                 if (cls == kKScan) {
                     ScanArgs sc{G.di, G.dr, G.xr, (int)p.cap, li, p.d_slots, p.rflag, p.zp, p.conv_out, p.z,
                                 L.dt_wt, L.dt_b, L.a_t, L.dvec, p.ssm};
+                    sc.x_late = G.conv_defer;
                     ActOut ao{p.act_f, p.act_q, p.act_e, p.cap_pad, G.di};
                     if (G.profile != kF32) ao.f = nullptr;
                     else ao.q = nullptr;
@@ -1655,8 +1666,9 @@ int32_t redukt_b200_set_option(const char* key, int64_t value) {
         clear_dev_graphs();
         return BACKEND_OK;
     }
-    if (!strcmp(key, "scan_blk") || !strcmp(key, "large_tile")) {
+    if (!strcmp(key, "scan_blk") || !strcmp(key, "large_tile") || !strcmp(key, "conv_defer")) {
         if (!strcmp(key, "scan_blk")) G.scan_blk = value != 0;
+        else if (!strcmp(key, "conv_defer")) G.conv_defer = value != 0;
         else if (value < 0 || value > 1) return BACKEND_INVALID_ARGUMENT;
         else G.large_tile = (int)value;
         for (Pool* p : {&G.v1, &G.batch}) {

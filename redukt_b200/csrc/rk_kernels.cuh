@@ -424,6 +424,7 @@ struct EpiInProj {
     const float* conv_b;      // [di]
     float* conv_out;          // [stream][di]
     float* z;                 // [stream][di]
+    bool defer = false;       // store the x-branch before the conv; k_xproj_part runs conv + SiLU
 
     __device__ __forceinline__ float conv_silu(int j, float s0, float s1, float s2, float v) const {
         return conv_silu_taps(s0, s1, s2, v, conv_t[j], conv_t[di + j], conv_t[2 * di + j], conv_t[3 * di + j],
@@ -433,6 +434,10 @@ struct EpiInProj {
     __device__ __forceinline__ void operator()(int row, int b, float v) const {
         if (row >= di) {
             z[(size_t)b * di + (row - di)] = v;
+            return;
+        }
+        if (defer) {
+            conv_out[(size_t)b * di + row] = v;
             return;
         }
         int j = row;
@@ -467,10 +472,11 @@ struct EpiInProj {
     template <int CH>
     __device__ __forceinline__ void apply(int row, int b0, int nb, const float (&v)[CH], TileMeta meta,
                                           int t0) const {
-        if (row >= di) {
+        if (row >= di || defer) {
+            float* dst = row >= di ? z + (row - di) : conv_out + row;
 #pragma unroll
             for (int i = 0; i < CH; i++)
-                if (i < nb) z[(size_t)(b0 + i) * di + (row - di)] = v[i];
+                if (i < nb) dst[(size_t)(b0 + i) * di] = v[i];
             return;
         }
         const int j = row;
@@ -502,10 +508,11 @@ struct EpiInProj {
 
     template <int CH>
     __device__ __forceinline__ void apply(int row, int b0, int nb, const float (&v)[CH]) const {
-        if (row >= di) {
+        if (row >= di || defer) {
+            float* dst = row >= di ? z + (row - di) : conv_out + row;
 #pragma unroll
             for (int i = 0; i < CH; i++)
-                if (i < nb) z[(size_t)(b0 + i) * di + (row - di)] = v[i];
+                if (i < nb) dst[(size_t)(b0 + i) * di] = v[i];
             return;
         }
         const int j = row;
@@ -697,9 +704,27 @@ __device__ __forceinline__ void xproj_sum_groups(const float* pb, int G, int M, 
 // batches use 64-stream tiles with 4 x 8 blocks, so the weights are staged once per 64 streams.
 // The last of a stream tile's G CTAs (a per-tile arrival counter, reset by that CTA) adds each
 // (stream, row)'s chains in group order into zp[b][r].
+//
+// With cv.on the activations are the in_proj x-branch before the conv (EpiInProj::defer): the
+// staging pass runs the causal conv1d + SiLU of its (stream, channel) block exactly as the in_proj
+// epilogue would (state shift, conv_silu_taps, rejected streams untouched), writes conv_out and the
+// state, and stages the result.  Every (stream, channel) belongs to exactly one CTA, so converting
+// conv_out in place is safe; many CTAs per SM keep far more state loads in flight than the
+// tensor-core epilogue's eight warps.
+struct XConv {
+    bool on;
+    int cap, layer;
+    const uint32_t* slots;    // validated slots (kRejected: leave the stream alone)
+    const uint32_t* rflag;    // per stream: read zeros instead of the stored state
+    float* state;             // [layer][slot][3][di]
+    const float* taps;        // [4][di]
+    const float* bias;        // [di]
+    float* out;               // conv_out, the same buffer as act
+};
+
 template <int SPB, int RB, int SK>
 __global__ void __launch_bounds__(256) k_xproj_part(int M, int K, const float* __restrict__ W, const float* act,
-                                                    int n, float* part, float* zp, uint32_t* tile_count) {
+                                                    int n, float* part, float* zp, uint32_t* tile_count, XConv cv) {
     static_assert(SPB % SK == 0, "stream blocks tile the stream tile");
     extern __shared__ float4 smem_f4[];
     float* xw = reinterpret_cast<float*>(smem_f4);  // [M][68]
@@ -707,6 +732,13 @@ __global__ void __launch_bounds__(256) k_xproj_part(int M, int K, const float* _
     const int g = blockIdx.x, G = gridDim.x, b0 = blockIdx.y * SPB, ns = min(SPB, n - b0);
     const int c0 = g * kXGroup, len = min(kXGroup, K - c0);
     const int tid = threadIdx.x;
+    __shared__ float s_tap[5][kXGroup];  // conv taps 0..3 and bias of the group's channels
+    __shared__ uint32_t s_slot[SPB], s_rd[SPB];
+    if (cv.on && tid < kXGroup) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) s_tap[k][tid] = tid < len ? __ldg(cv.taps + (size_t)k * K + c0 + tid) : 0.0f;
+        s_tap[4][tid] = tid < len ? __ldg(cv.bias + c0 + tid) : 0.0f;
+    }
     // the weights are constant: staged before the dependency wait, eight loads in flight per
     // thread before their stores
     for (int base = 0; base < M * 64; base += 8 * 256) {
@@ -724,17 +756,59 @@ __global__ void __launch_bounds__(256) k_xproj_part(int M, int K, const float* _
     }
     pdl_wait();
     pdl_trigger();
-    for (int base = 0; base < SPB * 64; base += 4 * 256) {
-        float v[4];
+    if (!cv.on) {
+        for (int base = 0; base < SPB * 64; base += 4 * 256) {
+            float v[4];
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const int i = base + u * 256 + tid, sidx = i >> 6, c = i & 63;
-            v[u] = (i < SPB * 64 && sidx < ns && c < len) ? act[(size_t)(b0 + sidx) * K + c0 + c] : 0.0f;
+            for (int u = 0; u < 4; u++) {
+                const int i = base + u * 256 + tid, sidx = i >> 6, c = i & 63;
+                v[u] = (i < SPB * 64 && sidx < ns && c < len) ? act[(size_t)(b0 + sidx) * K + c0 + c] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = base + u * 256 + tid;
+                if (i < SPB * 64) xc[(i >> 6) * 68 + (i & 63)] = v[u];
+            }
         }
+    } else {
+        for (int i = tid; i < SPB; i += 256) {
+            const uint32_t sl = i < ns ? cv.slots[b0 + i] : kRejected;
+            s_slot[i] = sl;
+            s_rd[i] = sl < (uint32_t)cv.cap && cv.rflag[b0 + i] == 0;
+        }
+        __syncthreads();
+        // kU (stream, channel) elements per thread and pass: every load is issued before the
+        // stores that could alias it
+        constexpr int kU = SPB >= 64 ? 8 : 4;
+        for (int base = 0; base < SPB * 64; base += kU * 256) {
+            float x[kU], s0[kU], s1[kU], s2[kU];
+            float* st[kU];
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const int i = base + u * 256 + tid;
-            if (i < SPB * 64) xc[(i >> 6) * 68 + (i & 63)] = v[u];
+            for (int u = 0; u < kU; u++) {
+                const int i = base + u * 256 + tid, sidx = i >> 6, c = i & 63;
+                const bool in = i < SPB * 64 && sidx < ns && c < len;
+                const uint32_t sl = in ? s_slot[sidx] : kRejected;
+                const bool live = sl < (uint32_t)cv.cap, rd = live && s_rd[sidx];
+                st[u] = live ? cv.state + conv_off(cv.layer, cv.cap, sl, K, 0, c0 + c) : nullptr;
+                x[u] = live ? act[(size_t)(b0 + sidx) * K + c0 + c] : 0.0f;
+                s0[u] = rd ? st[u][0] : 0.0f;
+                s1[u] = rd ? st[u][K] : 0.0f;
+                s2[u] = rd ? st[u][2 * K] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < kU; u++) {
+                const int i = base + u * 256 + tid, sidx = i >> 6, c = i & 63;
+                float y = 0.0f;
+                if (st[u]) {
+                    st[u][0] = s1[u];
+                    st[u][K] = s2[u];
+                    st[u][2 * K] = x[u];
+                    y = conv_silu_taps(s0[u], s1[u], s2[u], x[u], s_tap[0][c], s_tap[1][c], s_tap[2][c], s_tap[3][c],
+                                       s_tap[4][c]);
+                    cv.out[(size_t)(b0 + sidx) * K + c0 + c] = y;
+                }
+                if (i < SPB * 64) xc[sidx * 68 + c] = y;
+            }
         }
     }
     __syncthreads();
@@ -943,6 +1017,8 @@ struct ScanArgs {
     const float* a_t;      // [16][di]
     const float* dvec;     // [di]
     float* ssm;            // [layer][slot][16][di]
+    bool x_late = false;   // conv_out comes from the kernel just before (k_xproj_part with the conv):
+                           //   read it after the dependency wait, not before
 };
 
 // One thread per channel (large batches: no repeated work) or four (small batches: shorter
@@ -989,12 +1065,13 @@ __device__ __forceinline__ void scan_block(const ScanArgs& a, const ActOut& out,
     // Everything except x_proj's (dt_raw, B, C) is read before the dependency wait: the state and
     // the reset flag come from earlier steps and kernels, conv_out and z from the in_proj two
     // launches back (complete, since every kernel waits for its predecessor before it lets the
-    // next one start), the weights are constant.
+    // next one start), the weights are constant.  With x_late conv_out is written by x_proj itself
+    // and is read after the wait.
     float s[kSt];
 #pragma unroll
     for (int k = 0; k < kSt; k++) s[k] = (ok && !fresh) ? st[(t + TPC * k) * 64] : 0.0f;
     const int jj = ok ? j : 0;
-    const float xv = a.conv_out[(size_t)b * a.di + jj];
+    float xv = a.x_late ? 0.0f : a.conv_out[(size_t)b * a.di + jj];
     const float zv = a.z[(size_t)b * a.di + jj];
     // dt_proj row, 8-lane dot order: lane l accumulates columns c + l of the 8-aligned body
     const float* wt = a.dt_wt + jj;
@@ -1014,6 +1091,7 @@ __device__ __forceinline__ void scan_block(const ScanArgs& a, const ActOut& out,
     for (int k = 0; k < kSt; k++) at[k] = __ldg(a.a_t + (size_t)(t + TPC * k) * a.di + jj);
     const float dtb = __ldg(a.dt_b + jj), dv = __ldg(a.dvec + jj);
     fill(zs);
+    if (a.x_late) xv = a.conv_out[(size_t)b * a.di + jj];
     float dt;
     if constexpr (TPC == 1) {
         dt = dt_dot8_body(zs, body, [&](int c) { return wt[(size_t)c * a.di]; });
@@ -1136,7 +1214,7 @@ __global__ void __launch_bounds__(256) k_scan_blk(ScanArgs a, ActOut out, int n)
         bool ok, fresh;
         uint32_t slot;
     };
-    auto load = [&](int pass, Op& o) {
+    auto load = [&](int pass, Op& o, bool with_x) {
         const int b = b0 + pass * 4 + sl;
         o.ok = false;
         o.fresh = false;
@@ -1146,7 +1224,7 @@ __global__ void __launch_bounds__(256) k_scan_blk(ScanArgs a, ActOut out, int n)
             o.slot = a.slots[b];
             o.ok = o.slot < (uint32_t)a.cap;
             o.fresh = a.rflag[b] != 0;
-            o.xv = a.conv_out[(size_t)b * a.di + j];
+            if (with_x) o.xv = a.conv_out[(size_t)b * a.di + j];
             o.zv = a.z[(size_t)b * a.di + j];
         }
         const float* st = a.ssm + ssm_off(a.layer, a.cap, o.ok ? o.slot : 0u, a.di, 0, j);
@@ -1154,9 +1232,10 @@ __global__ void __launch_bounds__(256) k_scan_blk(ScanArgs a, ActOut out, int n)
         for (int k = 0; k < kDState; k++) o.s[k] = (o.ok && !o.fresh) ? st[k * 64] : 0.0f;
     };
     Op cur;
-    load(0, cur);
+    load(0, cur, !a.x_late);
     pdl_wait();
     pdl_trigger();
+    if (a.x_late && b0 + sl < n) cur.xv = a.conv_out[(size_t)(b0 + sl) * a.di + j];
     for (int i = tid; i < SB * a.xr; i += 256) {
         const int s = i / a.xr, b = b0 + s;
         zs[i] = b < n ? a.zp[(size_t)b * a.xr + (i - s * a.xr)] : 0.0f;
@@ -1167,7 +1246,7 @@ __global__ void __launch_bounds__(256) k_scan_blk(ScanArgs a, ActOut out, int n)
     const int body = a.dr & ~7;
     for (int pass = 0; pass < SB / 4; pass++) {
         Op nxt;
-        if (pass + 1 < SB / 4) load(pass + 1, nxt);
+        if (pass + 1 < SB / 4) load(pass + 1, nxt, true);
         const int s = pass * 4 + sl, b = b0 + s;
         const float* zb = zs + s * a.xr;
         float dt = dt_dot8_body(zb, body, [&](int c) { return w[c * 64 + ch]; });

@@ -332,3 +332,70 @@ def test_softmax_edge_rows_follow_softmax_into(ref_test_rbin):
         want = O.softmax(rows[r])
         assert np.max(np.abs(np.log(p[r].astype(np.float64)) - np.log(want.astype(np.float64)))) < 1e-5, r
     assert np.allclose(p[3, :3], 1.0 / 3, rtol=1e-6)
+
+
+@pytest.mark.parametrize("quant", ["q8", "q8row"])
+def test_large_batch_tile_shapes_bit_identical(small_gauss_rbin, mamba130m_rbin, quant):
+    """Above 256 streams the projections run as 64-stream tiles, one CTA per SM (large_tile 0), or
+    32-stream tiles, two CTAs per SM (1).  The accumulation order is the same in both: logits,
+    probabilities and states agree bit for bit."""
+    for path in (q8(small_gauss_rbin, quant == "q8row"), q8(mamba130m_rbin, quant == "q8row")):
+        b = backend(path)
+        V = b.vocab_size
+        for n in (257, 300, 640):
+            toks = zipf_tokens(n, 3, vocab=V, seed_base=11 * n)
+            outs = {}
+            try:
+                for mode in (0, 1):
+                    b.set_option("large_tile", mode)
+                    b.batch_init(2 * n)
+                    lg_slots, pr_slots = list(range(n)), list(range(n, 2 * n))
+                    for t in range(3):
+                        lg = b.forward_batch(lg_slots, toks[:, t]).copy()
+                        pr = b.forward_batch_probs(pr_slots, toks[:, t]).copy()
+                    outs[mode] = (lg, pr, b.get_state(n - 1)[1])
+            finally:
+                b.set_option("large_tile", 0)
+            for i in range(3):
+                assert np.array_equal(bits(outs[0][i]), bits(outs[1][i])), (path, n, i)
+            assert b.device_error() == 0
+
+
+@pytest.mark.parametrize("quant", ["f32", "q8"])
+def test_conv_in_xproj_staging_bit_identical(small_gauss_rbin, mamba130m_rbin, quant):
+    """conv1d + SiLU runs either in the in_proj epilogue (conv_defer 0) or in the x_proj kernel's
+    staging pass (1, in_proj then stores the x-branch before the conv).  Same arithmetic on the same
+    inputs: logits, conv state and SSM state agree bit for bit, also with one stream of a
+    device-path step rejected (its slot untouched)."""
+    import torch
+
+    dev = torch.device("cuda:0")
+    paths = [small_gauss_rbin, mamba130m_rbin]
+    for path in (paths if quant == "f32" else [q8(p) for p in paths]):
+        b = backend(path)
+        V = b.vocab_size
+        for n in (40, 130):
+            toks = zipf_tokens(n, 3, vocab=V, seed_base=13 * n)
+            outs = {}
+            try:
+                for mode in (0, 1):
+                    b.set_option("conv_defer", mode)
+                    b.batch_init(n)
+                    slots = list(range(n))
+                    b.forward_batch(slots, toks[:, 0])
+                    tk = toks[:, 1].astype(np.int32).copy()
+                    tk[n // 2] = V  # rejected on the device
+                    d_slots = torch.tensor(slots, dtype=torch.int32, device=dev)
+                    d_tok = torch.from_numpy(tk).to(dev)
+                    d_out = torch.empty((n, V), dtype=torch.float32, device=dev)
+                    b.forward_batch_device(n, d_slots.data_ptr(), d_tok.data_ptr(), d_out.data_ptr())
+                    torch.cuda.synchronize()
+                    assert b.device_error() & 1
+                    lg1 = d_out.cpu().numpy()
+                    lg2 = b.forward_batch(slots, toks[:, 2]).copy()
+                    outs[mode] = (lg1, lg2) + tuple(b.get_state(n - 1)) + tuple(b.get_state(n // 2))
+            finally:
+                b.set_option("conv_defer", 1)
+            for i in range(len(outs[0])):
+                assert np.array_equal(bits(outs[0][i]), bits(outs[1][i])), (path, n, i)
+            assert b.device_error() == 0
