@@ -1231,6 +1231,7 @@ __global__ void __launch_bounds__(256) k_scan_blk(ScanArgs a, ActOut out, int n)
 #pragma unroll
         for (int k = 0; k < kDState; k++) o.s[k] = (o.ok && !o.fresh) ? st[k * 64] : 0.0f;
     };
+    const f2 z2 = f2_zero();
     Op cur;
     load(0, cur, !a.x_late);
     pdl_wait();
@@ -1256,11 +1257,15 @@ __global__ void __launch_bounds__(256) k_scan_blk(ScanArgs a, ActOut out, int n)
         const float* C = zb + a.dr + kDState;
         const bool update = !(fabsf(dt) < 1e-6f);
         if (update) {
-            const float dtx = __fmul_rn(dt, cur.xv);
+            // states in pairs on the packed f32x2 pipe: the same per-state operations and bits
+            const f2 dt2 = f2_splat(dt), dtx2 = f2_splat(__fmul_rn(dt, cur.xv));
 #pragma unroll
-            for (int k = 0; k < kDState; k++) {
-                const float da = lane_expf(__fsub_rn(0.0f, __fmul_rn(dt, at[k * 64 + ch])));
-                cur.s[k] = __fadd_rn(__fmul_rn(da, cur.s[k]), __fmul_rn(dtx, B[k]));
+            for (int k = 0; k < kDState; k += 2) {
+                const f2 arg = f2_sub(f2_splat(0.0f), f2_mulz(dt2, f2_pack(at[k * 64 + ch], at[(k + 1) * 64 + ch]), z2));
+                const f2 da = lane_expf2(arg, z2);
+                const f2 sn = f2_add(f2_mulz(da, f2_pack(cur.s[k], cur.s[k + 1]), z2),
+                                     f2_mulz(dtx2, f2_pack(B[k], B[k + 1]), z2));
+                f2_unpack(sn, cur.s[k], cur.s[k + 1]);
             }
         }
         if (cur.ok && (update || cur.fresh)) {

@@ -58,6 +58,76 @@ __device__ __forceinline__ float lane_expf(float x) {
     return cephes_exp_core(x);
 }
 
+// ---- Two lanes per instruction (sm_100 packed f32x2) -------------------------------------
+// add/sub/mul/fma.rn.f32x2 round each 32-bit half exactly as the scalar .rn instruction does (no
+// flush to zero), so a pair of element-wise chains can run with half the instructions.  One trap:
+// the assembler contracts a packed multiply that feeds a packed add into one fused multiply-add
+// even with .rn (measured: about 1 % of Cephes exps one ulp off), which the scalar __fmul_rn /
+// __fadd_rn never allow.  So every product that feeds an add or subtract is written as
+// fma(a, b, z) with z = -0.0 held in memory the compiler cannot see into (g_f2_zero): that is the
+// correctly rounded product (x + -0 = x for every x, including +0 and -0), and nothing is left to
+// contract.  f2 holds (lo, hi) in one 64-bit register pair.
+typedef unsigned long long f2;
+
+__device__ float g_f2_zero = -0.0f;  // never written
+
+__device__ __forceinline__ f2 f2_pack(float lo, float hi) {
+    f2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(f2 v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f2 f2_splat(float v) { return f2_pack(v, v); }
+// (-0.0, -0.0) as a run-time value: read once per thread, passed to f2_mulz
+__device__ __forceinline__ f2 f2_zero() { return f2_splat(*(volatile const float*)&g_f2_zero); }
+__device__ __forceinline__ f2 f2_mul(f2 a, f2 b) {  // only where the product feeds no add
+    f2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2 f2_mulz(f2 a, f2 b, f2 z) {  // a * b rounded once, never contracted
+    f2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(z));
+    return r;
+}
+__device__ __forceinline__ f2 f2_add(f2 a, f2 b) {
+    f2 r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2 f2_sub(f2 a, f2 b) {
+    f2 r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// lane_expf of both halves (z from f2_zero): the clamp per half (a NaN half becomes kExpLo, as
+// fmaxf returns the non-NaN operand), cephes_exp_core's operations as packed pairs, and the 2^n
+// scale from the magic-sum bits of both halves at once: bits - (0x4B400000 - 127) is n + 127 in
+// [1, 255] per half (no borrow across halves), and shifting the 64-bit pair left by 23 moves each
+// half's 8-bit value into its own exponent field.
+__device__ __forceinline__ f2 lane_expf2(f2 x, f2 z) {
+    float x0, x1;
+    f2_unpack(x, x0, x1);
+    const f2 xc = f2_pack(fminf(fmaxf(x0, kExpLo), kExpHi), fminf(fmaxf(x1, kExpLo), kExpHi));
+    const f2 fx = f2_mulz(xc, f2_splat(1.44269504088896341f), z);
+    const f2 big = f2_add(fx, f2_splat(12582912.0f));
+    const f2 nf = f2_sub(big, f2_splat(12582912.0f));
+    const f2 r = f2_sub(f2_sub(xc, f2_mulz(nf, f2_splat(6.93145751953125E-1f), z)),
+                        f2_mulz(nf, f2_splat(1.42860682030941723212E-6f), z));
+    const f2 r2 = f2_mul(r, r);
+    f2 y = f2_add(f2_mulz(f2_splat(1.9875691500E-4f), r, z), f2_splat(1.3981999507E-3f));
+    y = f2_add(f2_mulz(y, r, z), f2_splat(8.3334519073E-3f));
+    y = f2_add(f2_mulz(y, r, z), f2_splat(4.1665795894E-2f));
+    y = f2_add(f2_mulz(y, r, z), f2_splat(1.6666665459E-1f));
+    y = f2_add(f2_mulz(y, r, z), f2_splat(5.0000001201E-1f));
+    y = f2_add(f2_add(f2_mulz(y, r2, z), r), f2_splat(1.0f));
+    const f2 pow2n = (big - 0x4B3FFF814B3FFF81ull) << 23;
+    return f2_mul(y, pow2n);
+}
+
 // ---- musl/FreeBSD logf (tensor.rs:799-837) ------------------------------------------------
 __device__ __forceinline__ float portable_lnf(float x) {
     const float LN2_HI = 6.9313812256e-01f, LN2_LO = 9.0580006145e-06f;
