@@ -92,6 +92,11 @@ __device__ __forceinline__ f2 f2_mulz(f2 a, f2 b, f2 z) {  // a * b rounded once
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(z));
     return r;
 }
+__device__ __forceinline__ f2 f2_fma(f2 a, f2 b, f2 c) {  // a * b + c rounded once
+    f2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
 __device__ __forceinline__ f2 f2_add(f2 a, f2 b) {
     f2 r;
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
@@ -254,6 +259,21 @@ __device__ __forceinline__ float small_int_to_float(int a) {
 __device__ __forceinline__ float digit_value(int a1, int a2, int a3) {
     float v = __fmaf_rn(small_int_to_float(a2), 0.0078125f, small_int_to_float(a1));
     return __fmaf_rn(small_int_to_float(a3), 6.103515625e-05f, v);
+}
+
+// digit_value + group_accumulate of two streams of one row and group on the packed pipe: the same
+// operations per lane (exact conversions, the two exact-product FMAs, rn(ws * ae), the product
+// written with f2_mulz so it cannot be contracted into the add), so the same bits.
+__device__ __forceinline__ void group_accumulate2(float& acc0, float& acc1, int a1_0, int a1_1, int a2_0, int a2_1,
+                                                  int a3_0, int a3_1, float w_scale, f2 a_scale, f2 z) {
+    const f2 big = f2_splat(12582912.0f);
+    const f2 x1 = f2_sub(f2_pack(__int_as_float(0x4B400000 + a1_0), __int_as_float(0x4B400000 + a1_1)), big);
+    const f2 x2 = f2_sub(f2_pack(__int_as_float(0x4B400000 + a2_0), __int_as_float(0x4B400000 + a2_1)), big);
+    const f2 x3 = f2_sub(f2_pack(__int_as_float(0x4B400000 + a3_0), __int_as_float(0x4B400000 + a3_1)), big);
+    f2 v = f2_fma(x2, f2_splat(0.0078125f), x1);
+    v = f2_fma(x3, f2_splat(6.103515625e-05f), v);
+    const f2 acc = f2_add(f2_pack(acc0, acc1), f2_mulz(v, f2_mul(f2_splat(w_scale), a_scale), z));
+    f2_unpack(acc, acc0, acc1);
 }
 
 // Accumulation order of a Q8 projection row (every path): the G groups are cut into

@@ -79,7 +79,7 @@ struct alignas(1024) Smem {
     int last;                             // split-K: this CTA combines the tile
     uint32_t tmem_base;
     int abort;
-    float ae[BN * 32];                    // 2^e of the tile's streams for up to 32 groups
+    alignas(16) float ae[32 * BN];        // 2^e of the tile's streams for up to 32 groups, [group][stream]
     float ws[32 * kBM];                   // weight scales of the tile's rows, [group][row]
 };
 
@@ -396,11 +396,12 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
                 int i = et + k * kET;
                 if (i < acnt) {
                     int b = i / G, g = i - b * G;
-                    S.ae[b * 32 + g] = ta[k];
+                    S.ae[g * BN + b] = ta[k];
                 }
             }
             asm volatile("bar.sync 1, %0;" ::"r"(kET) : "memory");  // epilogue warps only
         }
+        const f2 z2 = f2_zero();     // group_accumulate2's hidden -0.0
         float acc[kSPT], tot[kSPT];  // running sum of the current split; sum of the finished splits
 #pragma unroll
         for (int b = 0; b < kSPT; b++) acc[b] = tot[b] = 0.0f;
@@ -443,11 +444,12 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
                     tmem_ld16(base + (uint32_t)((u0 + c) * 48 + 16), a2);
                     tmem_ld16(base + (uint32_t)((u0 + c) * 48 + 32), a3);
                     tmem_wait_ld();
+                    const f2* ae2 = reinterpret_cast<const f2*>(&S.ae[g * BN + half * kSPT + c * 16]);
 #pragma unroll
-                    for (int q = 0; q < 16; q++) {
+                    for (int q = 0; q < 16; q += 2) {
                         const int b = c * 16 + q;
-                        acc[b] = group_accumulate(acc[b], digit_value(a1[q], a2[q], a3[q]), wsg,
-                                                  S.ae[(half * kSPT + b) * 32 + g]);
+                        group_accumulate2(acc[b], acc[b + 1], a1[q], a1[q + 1], a2[q], a2[q + 1], a3[q], a3[q + 1], wsg,
+                                          ae2[q >> 1], z2);
                     }
                 }
                 tc_fence_before();
@@ -481,10 +483,11 @@ k_proj_q8_tc(const int8_t* __restrict__ wq, const int8_t* __restrict__ dq, int M
                     }
                 }
                 const float wsg = S.ws[g * kBM + rl];
+                const f2* ae2 = reinterpret_cast<const f2*>(&S.ae[g * BN + half * kSPT]);
 #pragma unroll
-                for (int b = 0; b < kSPT; b++)
-                    acc[b] = group_accumulate(acc[b], digit_value(cur[0][b], cur[1][b], cur[2][b]), wsg,
-                                              S.ae[(half * kSPT + b) * 32 + g]);
+                for (int b = 0; b < kSPT; b += 2)
+                    group_accumulate2(acc[b], acc[b + 1], cur[0][b], cur[0][b + 1], cur[1][b], cur[1][b + 1], cur[2][b],
+                                      cur[2][b + 1], wsg, ae2[b >> 1], z2);
                 tc_fence_before();
                 mbar_arrive(&S.tempty[buf]);
                 split_end(g);
