@@ -287,13 +287,12 @@ __device__ __forceinline__ void q8_tile16_split(const int8_t* at, int RT, int rl
     const uint32_t sw = ((uint32_t)ra >> 1) & 3u;
 #pragma unroll
     for (int i = 0; i < 4; i++) acc[i] = 0.0f;
-    auto fold = [&](const int (&ds)[3][4], int g) {
+    const f2 z2 = f2_zero();
+    auto fold = [&](const int (&ds)[3][4], int g) {  // (row, stream pair) on the packed pipe
         const float wsa = ws[ra * G + g], wsb = ws[(ra + 8) * G + g];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float v = digit_value(ds[0][i], ds[1][i], ds[2][i]);
-            acc[i] = group_accumulate(acc[i], v, i < 2 ? wsa : wsb, ae[(2 * tig + (i & 1)) * kEStride + g]);
-        }
+        const f2 ae2 = f2_pack(ae[(2 * tig) * kEStride + g], ae[(2 * tig + 1) * kEStride + g]);
+        group_accumulate2(acc[0], acc[1], ds[0][0], ds[0][1], ds[1][0], ds[1][1], ds[2][0], ds[2][1], wsa, ae2, z2);
+        group_accumulate2(acc[2], acc[3], ds[0][2], ds[0][3], ds[1][2], ds[1][3], ds[2][2], ds[2][3], wsb, ae2, z2);
     };
     int g = g0;
     for (; g + 1 < g1; g += 2) {  // two groups in flight; folded in group order
@@ -742,12 +741,14 @@ __device__ __forceinline__ bool run_b(const FusedArgs& a, const StepMeta& m, int
             const float* B = zb + a.dr;
             const float* C = zb + a.dr + kDState;
             const bool update = !(fabsf(dt) < 1e-6f);
-            if (update) {
-                const float dtx = __fmul_rn(dt, xv);
+            if (update) {  // state pairs on the packed pipe (same bits)
+                const f2 z2 = f2_zero(), dt2 = f2_splat(dt), dtx2 = f2_splat(__fmul_rn(dt, xv));
 #pragma unroll
-                for (int k = 0; k < kDState; k++) {
-                    const float da = lane_expf(__fsub_rn(0.0f, __fmul_rn(dt, at[k * 64 + ch])));
-                    st[k] = __fadd_rn(__fmul_rn(da, st[k]), __fmul_rn(dtx, B[k]));
+                for (int k = 0; k < kDState; k += 2) {
+                    const f2 arg = f2_sub(f2_splat(0.0f), f2_mulz(dt2, f2_pack(at[k * 64 + ch], at[(k + 1) * 64 + ch]), z2));
+                    const f2 sn = f2_add(f2_mulz(lane_expf2(arg, z2), f2_pack(st[k], st[k + 1]), z2),
+                                         f2_mulz(dtx2, f2_pack(B[k], B[k + 1]), z2));
+                    f2_unpack(sn, st[k], st[k + 1]);
                 }
             }
             if (ok && (update || fresh)) {
@@ -838,13 +839,15 @@ __device__ __forceinline__ bool run_b1(const FusedArgs& a, const StepMeta& m, in
     const float* B = zs + a.dr;
     const float* C = zs + a.dr + kDState;
     const bool update = !(fabsf(dt) < 1e-6f);
-    if (update) {
-        const float dtx = __fmul_rn(dt, xv);
+    if (update) {  // states t + 4k, t + 4k + 4 in pairs on the packed pipe (same bits)
+        const f2 z2 = f2_zero(), dt2 = f2_splat(dt), dtx2 = f2_splat(__fmul_rn(dt, xv));
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
+        for (int k = 0; k < 4; k += 2) {
             const int n2 = t + 4 * k;
-            const float da = lane_expf(__fsub_rn(0.0f, __fmul_rn(dt, at[n2 * 64 + ch])));
-            st[k] = __fadd_rn(__fmul_rn(da, st[k]), __fmul_rn(dtx, B[n2]));
+            const f2 arg = f2_sub(f2_splat(0.0f), f2_mulz(dt2, f2_pack(at[n2 * 64 + ch], at[(n2 + 4) * 64 + ch]), z2));
+            const f2 sn = f2_add(f2_mulz(lane_expf2(arg, z2), f2_pack(st[k], st[k + 1]), z2),
+                                 f2_mulz(dtx2, f2_pack(B[n2], B[n2 + 4]), z2));
+            f2_unpack(sn, st[k], st[k + 1]);
         }
     }
     if (ok && (update || fresh)) {

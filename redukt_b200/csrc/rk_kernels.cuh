@@ -1120,13 +1120,15 @@ __device__ __forceinline__ void scan_block(const ScanArgs& a, const ActOut& out,
     const float* B = zs + a.dr;
     const float* C = zs + a.dr + kDState;
     const bool update = !(fabsf(dt) < 1e-6f);
-    if (update) {
-        const float dtx = __fmul_rn(dt, xv);
+    if (update) {  // state pairs on the packed pipe (same bits)
+        const f2 z2 = f2_zero(), dt2 = f2_splat(dt), dtx2 = f2_splat(__fmul_rn(dt, xv));
 #pragma unroll
-        for (int k = 0; k < kSt; k++) {
+        for (int k = 0; k < kSt; k += 2) {
             const int n2 = t + TPC * k;
-            const float da = lane_expf(__fsub_rn(0.0f, __fmul_rn(dt, at[k])));
-            s[k] = __fadd_rn(__fmul_rn(da, s[k]), __fmul_rn(dtx, B[n2]));
+            const f2 arg = f2_sub(f2_splat(0.0f), f2_mulz(dt2, f2_pack(at[k], at[k + 1]), z2));
+            const f2 sn = f2_add(f2_mulz(lane_expf2(arg, z2), f2_pack(s[k], s[k + 1]), z2),
+                                 f2_mulz(dtx2, f2_pack(B[n2], B[n2 + TPC]), z2));
+            f2_unpack(sn, s[k], s[k + 1]);
         }
     }
     if (ok && (update || fresh)) {
