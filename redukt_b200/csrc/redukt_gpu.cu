@@ -723,13 +723,15 @@ void project_head_softmax(const Pool& p, int n, float* out, int tiles, cudaStrea
 // Four threads per channel while the batch is small (latency), one when it is large (no repeated
 // per-channel work); both give the same bits.
 // Above 64 streams, stream blocks of 16 or 32 per CTA with the group's weights staged once
-// (k_scan_blk, same bits) where d_inner is a multiple of 64.
+// (k_scan_blk, same bits) where d_inner is a multiple of 64 and dt_rank and x_proj's rows are
+// multiples of 4 (its 16-byte shared loads).
 void launch_scan(const ScanArgs& sc, const ActOut& ao, int n, cudaStream_t st) {
     if (n <= 64) {
         launch(k_scan<4>, dim3(G.di / 64, n), dim3(256), G.xr * sizeof(float), st, sc, ao);
-    } else if (G.di % 64 == 0 && G.scan_blk) {
+    } else if (G.di % 64 == 0 && G.dr % 4 == 0 && G.xr % 4 == 0 && G.scan_blk) {
         const int sb = n >= 512 ? 32 : 16;
-        const size_t smem = ((size_t)(G.dr + kDState + 2) * 64 + (size_t)sb * G.xr) * sizeof(float);
+        const size_t smem =
+            ((size_t)64 * (scan_blk_wstride(G.dr) + kScanAStride + 2) + (size_t)sb * G.xr) * sizeof(float);
         if (sb == 32) {
             allow_smem(k_scan_blk<32>, smem);
             launch(k_scan_blk<32>, dim3(G.di / 64, (n + 31) / 32), dim3(256), smem, st, sc, ao, n);

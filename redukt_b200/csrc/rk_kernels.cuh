@@ -1038,6 +1038,42 @@ __device__ __forceinline__ float dt_dot8_body(const float* zs, int body, W w) {
                      __fadd_rn(__fadd_rn(l[1], l[5]), __fadd_rn(l[3], l[7])));
 }
 
+// Row stride (words) of the stream-blocked scan's channel-major dt_proj copy: dt_rank rounded up
+// to 8, plus 4, so 16-byte loads of eight consecutive channels hit distinct banks.
+__host__ __device__ __forceinline__ int scan_blk_wstride(int dr) { return ((dr + 7) & ~7) + 4; }
+constexpr int kScanAStride = 18;  // A's 16 states: 2 mod 4 words, so 8-byte loads are conflict-free
+
+// dt_dot8_body with the channel's dt_proj row w (16-byte aligned, body a multiple of 8) and zs
+// (16-byte aligned): lanes (l, l+1) as packed pairs, two 16-byte loads of each per 8 columns, the
+// same partial sums and the same hsum8 tree ((l0+l4)+(l2+l6)) + ((l1+l5)+(l3+l7)).
+__device__ __forceinline__ float dt_dot8_body_v(const float* zs, const float* w, int body, f2 z) {
+    f2 l01 = f2_splat(0.0f), l23 = l01, l45 = l01, l67 = l01;
+    for (int c = 0; c < body; c += 8) {
+        const float4 w0 = *reinterpret_cast<const float4*>(w + c), w1 = *reinterpret_cast<const float4*>(w + c + 4);
+        const float4 z0 = *reinterpret_cast<const float4*>(zs + c), z1 = *reinterpret_cast<const float4*>(zs + c + 4);
+        l01 = f2_add(l01, f2_mulz(f2_pack(w0.x, w0.y), f2_pack(z0.x, z0.y), z));
+        l23 = f2_add(l23, f2_mulz(f2_pack(w0.z, w0.w), f2_pack(z0.z, z0.w), z));
+        l45 = f2_add(l45, f2_mulz(f2_pack(w1.x, w1.y), f2_pack(z1.x, z1.y), z));
+        l67 = f2_add(l67, f2_mulz(f2_pack(w1.z, w1.w), f2_pack(z1.z, z1.w), z));
+    }
+    float r0, r1;  // ((l0+l4)+(l2+l6), (l1+l5)+(l3+l7))
+    f2_unpack(f2_add(f2_add(l01, l45), f2_add(l23, l67)), r0, r1);
+    return __fadd_rn(r0, r1);
+}
+
+// ssm_out16 with C 8-byte aligned: lanes (q, q+1) as packed pairs, the same tree.
+__device__ __forceinline__ float ssm_out16_v(const float (&s)[kDState], const float* C, f2 z) {
+    f2 ln[4];
+#pragma unroll
+    for (int q = 0; q < 8; q += 2)
+        ln[q >> 1] = f2_add(f2_mulz(f2_pack(s[q], s[q + 1]), *reinterpret_cast<const f2*>(C + q), z),
+                            f2_mulz(f2_pack(s[q + 8], s[q + 9]), *reinterpret_cast<const f2*>(C + q + 8), z));
+    float p0, p1, q0, q1;  // (l0+l4, l1+l5), (l2+l6, l3+l7)
+    f2_unpack(f2_add(ln[0], ln[2]), p0, p1);
+    f2_unpack(f2_add(ln[1], ln[3]), q0, q1);
+    return __fadd_rn(__fadd_rn(p0, p1), __fadd_rn(q0, q1));
+}
+
 __device__ __forceinline__ float ssm_out16(const float (&s)[kDState], const float* C) {
     float ln[8];
 #pragma unroll
@@ -1192,22 +1228,31 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a, ActOut out) {
 // memory once per CTA instead of being re-read from L2 for every stream (the one-stream CTAs of
 // k_scan), and the next pass's state, conv output and z are loaded while the current pass
 // computes.  The arithmetic is scan_block<1>'s (same bits); d_inner must be a multiple of 64.
+// 32-stream blocks (1,024 streams: 79 vs 90 us) run three CTAs per SM, 16-stream blocks two.
 template <int SB>
-__global__ void __launch_bounds__(256) k_scan_blk(ScanArgs a, ActOut out, int n) {
+__global__ void __launch_bounds__(256, SB >= 32 ? 3 : 2) k_scan_blk(ScanArgs a, ActOut out, int n) {
     extern __shared__ float4 smem_f4[];
-    float* w = reinterpret_cast<float*>(smem_f4);   // [dr][64] dt_proj, [16][64] A, [64] dt bias, [64] D
-    float* zs = w + (a.dr + kDState + 2) * 64;       // [SB][xr]
+    // channel-major copies of the group's operands, so a thread's columns are wide shared loads
+    // without bank conflicts: dt_proj [64][ws] (16-byte loads, row stride 4 mod 8 words) and A
+    // [64][18] (8-byte loads, 2 mod 4), then the dt bias and D [64] each, then (dt_raw, B, C) of
+    // the block's streams [SB][xr] (xr and dt_rank multiples of 4)
+    const int ws = scan_blk_wstride(a.dr);
+    float* wt = reinterpret_cast<float*>(smem_f4);
+    float* atc = wt + 64 * ws;
+    float* w = atc + 64 * kScanAStride;              // [64] dt bias, [64] D
+    float* zs = w + 2 * 64;
     __shared__ float s_max[2][8];
     const int g = blockIdx.x, b0 = blockIdx.y * SB;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ch = tid & 63, sl = tid >> 6, j = g * 64 + ch;
-    // constant operands (before the dependency wait): the group's columns, coalesced
-    for (int i = tid; i < a.dr * 64; i += 256) w[i] = __ldg(a.dt_wt + (size_t)(i >> 6) * a.di + g * 64 + (i & 63));
+    // constant operands (before the dependency wait): the group's columns, coalesced reads
+    for (int i = tid; i < a.dr * 64; i += 256)
+        wt[(i & 63) * ws + (i >> 6)] = __ldg(a.dt_wt + (size_t)(i >> 6) * a.di + g * 64 + (i & 63));
     for (int i = tid; i < kDState * 64; i += 256)
-        w[a.dr * 64 + i] = __ldg(a.a_t + (size_t)(i >> 6) * a.di + g * 64 + (i & 63));
+        atc[(i & 63) * kScanAStride + (i >> 6)] = __ldg(a.a_t + (size_t)(i >> 6) * a.di + g * 64 + (i & 63));
     if (tid < 64) {
-        w[(a.dr + kDState) * 64 + tid] = __ldg(a.dt_b + j);
-        w[(a.dr + kDState + 1) * 64 + tid] = __ldg(a.dvec + j);
+        w[tid] = __ldg(a.dt_b + j);
+        w[64 + tid] = __ldg(a.dvec + j);
     }
     // one pass's per-thread operands: state, conv output, z (written by earlier kernels)
     struct Op {
@@ -1244,16 +1289,17 @@ __global__ void __launch_bounds__(256) k_scan_blk(ScanArgs a, ActOut out, int n)
         zs[i] = b < n ? a.zp[(size_t)b * a.xr + (i - s * a.xr)] : 0.0f;
     }
     __syncthreads();
-    const float* at = w + a.dr * 64;
-    const float dtb = w[(a.dr + kDState) * 64 + ch], dv = w[(a.dr + kDState + 1) * 64 + ch];
+    const float* wrow = wt + ch * ws;
+    const float* arow = atc + ch * kScanAStride;
+    const float dtb = w[ch], dv = w[64 + ch];
     const int body = a.dr & ~7;
     for (int pass = 0; pass < SB / 4; pass++) {
         Op nxt;
         if (pass + 1 < SB / 4) load(pass + 1, nxt, true);
         const int s = pass * 4 + sl, b = b0 + s;
         const float* zb = zs + s * a.xr;
-        float dt = dt_dot8_body(zb, body, [&](int c) { return w[c * 64 + ch]; });
-        for (int c = body; c < a.dr; c++) dt = __fadd_rn(dt, __fmul_rn(w[c * 64 + ch], zb[c]));
+        float dt = dt_dot8_body_v(zb, wrow, body, z2);
+        for (int c = body; c < a.dr; c++) dt = __fadd_rn(dt, __fmul_rn(wrow[c], zb[c]));
         dt = softplus(__fadd_rn(dt, dtb));
         const float* B = zb + a.dr;
         const float* C = zb + a.dr + kDState;
@@ -1263,10 +1309,10 @@ __global__ void __launch_bounds__(256) k_scan_blk(ScanArgs a, ActOut out, int n)
             const f2 dt2 = f2_splat(dt), dtx2 = f2_splat(__fmul_rn(dt, cur.xv));
 #pragma unroll
             for (int k = 0; k < kDState; k += 2) {
-                const f2 arg = f2_sub(f2_splat(0.0f), f2_mulz(dt2, f2_pack(at[k * 64 + ch], at[(k + 1) * 64 + ch]), z2));
+                const f2 arg = f2_sub(f2_splat(0.0f), f2_mulz(dt2, *reinterpret_cast<const f2*>(arow + k), z2));
                 const f2 da = lane_expf2(arg, z2);
                 const f2 sn = f2_add(f2_mulz(da, f2_pack(cur.s[k], cur.s[k + 1]), z2),
-                                     f2_mulz(dtx2, f2_pack(B[k], B[k + 1]), z2));
+                                     f2_mulz(dtx2, *reinterpret_cast<const f2*>(B + k), z2));
                 f2_unpack(sn, cur.s[k], cur.s[k + 1]);
             }
         }
@@ -1275,7 +1321,7 @@ __global__ void __launch_bounds__(256) k_scan_blk(ScanArgs a, ActOut out, int n)
 #pragma unroll
             for (int k = 0; k < kDState; k++) st[k * 64] = cur.s[k];
         }
-        const float y = __fadd_rn(ssm_out16(cur.s, C), __fmul_rn(dv, cur.xv));
+        const float y = __fadd_rn(ssm_out16_v(cur.s, C, z2), __fmul_rn(dv, cur.xv));
         const float gated = cur.ok ? __fmul_rn(y, __fmul_rn(cur.zv, lane_sigmoid(cur.zv))) : 0.0f;
         if (out.f) {
             if (cur.ok) out.f[(size_t)b * out.K + j] = gated;
