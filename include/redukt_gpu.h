@@ -152,6 +152,8 @@ int32_t redukt_b200_info(uint32_t* out, uint32_t n);
  *                  group's weights staged once (1, default) or one stream per CTA (0); same bits
  *   "large_tile"   0/1 = above 256 streams, tensor-core tiles of 64 streams, one CTA per SM (0) or
  *                  of 32 streams, two CTAs per SM (1); same bits
+ *   "f32_pairs"    0/1 = F32 projections of 8 or more streams on packed stream-pair FMAs with a
+ *                  reduce-scatter butterfly (1, default) or the plain CUDA-core GEMV (0); same bits
  *   "conv_defer"   0/1 = outside the fused step, conv1d + SiLU runs in the x_proj kernel's staging
  *                  pass with in_proj storing the x-branch before the conv (1, default) or in the
  *                  in_proj epilogue (0); same bits

@@ -140,6 +140,7 @@ struct Model {
     // fused small-batch step (rk_fused.cuh)
     bool fused = true;          // option "fused"
     bool scan_blk = true;       // option "scan_blk": stream-blocked scan above 64 streams
+    bool f32_pairs = true;      // option "f32_pairs": F32 GEMV from 8 streams on as k_gemv_f32_p
     bool conv_defer = true;     // option "conv_defer": conv1d + SiLU in the x_proj kernel's staging
                                 //   pass (1) or in the in_proj epilogue (0); the same bits
     int large_tile = 0;         // option "large_tile": above 256 streams, 0 = 64-stream tensor-core
@@ -585,6 +586,12 @@ void gemv_f32_ns(int M, int K, const float* W, const float* act, int ld, int n, 
 
 template <int RW, class Epi>
 void gemv_f32(int M, int K, const float* W, const float* act, int ld, int n, Epi epi, cudaStream_t st) {
+    if (RW == 4 && n >= 8 && G.f32_pairs) {  // 4 rows x 8 streams per warp on the packed pipe (same bits)
+        const size_t smem = (size_t)8 * ((K + 127) / 128) * 128 * sizeof(float);
+        allow_smem(k_gemv_f32_p<Epi>, smem);
+        launch(k_gemv_f32_p<Epi>, dim3((n + 7) / 8, (M + 31) / 32), dim3(256), smem, st, M, K, W, act, ld, n, epi);
+        return;
+    }
     if (n >= 8) gemv_f32_ns<RW, 8>(M, K, W, act, ld, n, epi, st);
     else if (n >= 4) gemv_f32_ns<RW, 4>(M, K, W, act, ld, n, epi, st);
     else if (n >= 2) gemv_f32_ns<RW, 2>(M, K, W, act, ld, n, epi, st);
@@ -1668,8 +1675,10 @@ int32_t redukt_b200_set_option(const char* key, int64_t value) {
         clear_dev_graphs();
         return BACKEND_OK;
     }
-    if (!strcmp(key, "scan_blk") || !strcmp(key, "large_tile") || !strcmp(key, "conv_defer")) {
+    if (!strcmp(key, "scan_blk") || !strcmp(key, "large_tile") || !strcmp(key, "conv_defer") ||
+        !strcmp(key, "f32_pairs")) {
         if (!strcmp(key, "scan_blk")) G.scan_blk = value != 0;
+        else if (!strcmp(key, "f32_pairs")) G.f32_pairs = value != 0;
         else if (!strcmp(key, "conv_defer")) G.conv_defer = value != 0;
         else if (value < 0 || value > 1) return BACKEND_INVALID_ARGUMENT;
         else G.large_tile = (int)value;

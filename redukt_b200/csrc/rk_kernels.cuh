@@ -649,6 +649,98 @@ __global__ void __launch_bounds__(256) k_gemv_f32(int M, int K, const float* __r
             if (((r * NS + s) & 31) == lane && s < ns && r0 + r < M) epi(r0 + r, b0 + s, acc[r][s]);
 }
 
+// The same GEMV for 4 rows x 8 streams per warp (the large-batch shape), with the same bits and
+// about half the instructions:
+//  * the activations are staged as stream pairs interleaved by column, in lane order within each
+//    128-column chunk ([pair][chunk][column half][lane][2 columns][2 streams]), so one
+//    conflict-free 16-byte shared load gives a lane two columns of a stream pair, and each
+//    (row, stream pair) runs its two
+//    sequential FMA chains as one packed fma.rn.f32x2 (a fused multiply-add is the same operation
+//    on the packed pipe; nothing is left to contract);
+//  * the 32 lane sums of the warp's 32 outputs are reduced by a reduce-scatter over the same xor
+//    butterfly (offsets 16, 8, 4, 2, 1): at each level a lane keeps the half of its outputs whose
+//    index bit matches its own lane bit and adds its partner's copy, so every output gets exactly
+//    warp_allsum's tree (IEEE addition is commutative) and lane l ends holding output l
+//    (row l / 8, stream l % 8), with 62 shuffles instead of 160.
+template <class Epi>
+__global__ void __launch_bounds__(256) k_gemv_f32_p(int M, int K, const float* __restrict__ W,
+                                                    const float* __restrict__ act, int ld_act, int n, Epi epi) {
+    constexpr int RW = 4, NS = 8;
+    extern __shared__ float4 smem_f4[];
+    float* xs = reinterpret_cast<float*>(smem_f4);  // [NS / 2][nch][2][32][4]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = blockIdx.y * (8 * RW) + warp * RW;
+    pdl_wait();
+    pdl_trigger();
+    const int b0 = blockIdx.x * NS, ns = min(NS, n - b0);
+    const int K4 = K >> 2, nch = (K + 127) >> 7;
+    for (int i = threadIdx.x; i < NS * K4; i += blockDim.x) {
+        const int s = i / K4, k4 = i - s * K4;  // columns 4 k4 .. 4 k4 + 3 = chunk c, lane k4 % 32
+        const float4 v = s < ns ? reinterpret_cast<const float4*>(act + (size_t)(b0 + s) * ld_act)[k4]
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        float* d = xs + ((size_t)((s >> 1) * nch + (k4 >> 5)) * 2) * 128 + (k4 & 31) * 4 + (s & 1);
+        d[0] = v.x;
+        d[2] = v.y;
+        d[128] = v.z;
+        d[130] = v.w;
+    }
+    __syncthreads();
+    if (r0 >= M) return;
+    f2 acc[RW][NS / 2];
+#pragma unroll
+    for (int r = 0; r < RW; r++)
+#pragma unroll
+        for (int q = 0; q < NS / 2; q++) acc[r][q] = f2_splat(0.0f);
+    for (int c = 0; c < nch; c++) {
+        const int k = c * 128 + lane * 4;
+        if (k < K) {
+            f2 w2[RW][4];
+#pragma unroll
+            for (int r = 0; r < RW; r++) {
+                const float4 wv = (r0 + r < M) ? __ldg(reinterpret_cast<const float4*>(W + (size_t)(r0 + r) * K + k))
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                w2[r][0] = f2_splat(wv.x);
+                w2[r][1] = f2_splat(wv.y);
+                w2[r][2] = f2_splat(wv.z);
+                w2[r][3] = f2_splat(wv.w);
+            }
+#pragma unroll
+            for (int q = 0; q < NS / 2; q++) {
+                const float* xq = xs + ((size_t)(q * nch + c) * 2) * 128 + lane * 4;
+                const float4 xa = *reinterpret_cast<const float4*>(xq);        // columns k, k + 1
+                const float4 xb = *reinterpret_cast<const float4*>(xq + 128);  // columns k + 2, k + 3
+                const f2 x0 = f2_pack(xa.x, xa.y), x1 = f2_pack(xa.z, xa.w);
+                const f2 x2 = f2_pack(xb.x, xb.y), x3 = f2_pack(xb.z, xb.w);
+#pragma unroll
+                for (int r = 0; r < RW; r++) {
+                    acc[r][q] = f2_fma(w2[r][0], x0, acc[r][q]);
+                    acc[r][q] = f2_fma(w2[r][1], x1, acc[r][q]);
+                    acc[r][q] = f2_fma(w2[r][2], x2, acc[r][q]);
+                    acc[r][q] = f2_fma(w2[r][3], x3, acc[r][q]);
+                }
+            }
+        }
+    }
+    // reduce-scatter: output j = r * 8 + s
+    float v[32];
+#pragma unroll
+    for (int r = 0; r < RW; r++)
+#pragma unroll
+        for (int q = 0; q < NS / 2; q++) f2_unpack(acc[r][q], v[r * 8 + 2 * q], v[r * 8 + 2 * q + 1]);
+#pragma unroll
+    for (int d = 16, L = 32; d >= 1; d >>= 1, L >>= 1) {
+        const bool up = (lane & d) != 0;
+#pragma unroll
+        for (int i = 0; i < L / 2; i++) {
+            const float keep = up ? v[L / 2 + i] : v[i];
+            const float give = up ? v[i] : v[L / 2 + i];
+            v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, give, d));
+        }
+    }
+    const int r = lane >> 3, sidx = lane & 7;
+    if (sidx < ns && r0 + r < M) epi(r0 + r, b0 + sidx, v[0]);
+}
+
 // ------------------------------------------------------------------------------------------
 // x_proj: (dt_raw, B, C)[b][r] = W_x[r] . conv_out[b] in a fixed two-level order.  Each 64-channel
 // group g gives a sequential FMA chain over its channels from zero (xproj_chain); the group sums

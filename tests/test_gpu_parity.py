@@ -399,3 +399,26 @@ def test_conv_in_xproj_staging_bit_identical(small_gauss_rbin, mamba130m_rbin, q
             for i in range(len(outs[0])):
                 assert np.array_equal(bits(outs[0][i]), bits(outs[1][i])), (path, n, i)
             assert b.device_error() == 0
+
+
+def test_f32_pair_gemv_bit_identical(ref_test_rbin, small_gauss_rbin):
+    """From 8 streams on, the F32 projections run k_gemv_f32_p (stream pairs on packed FMAs, a
+    reduce-scatter butterfly) unless option f32_pairs is 0 (k_gemv_f32).  The per-(row, stream)
+    FMA chains and the butterfly tree are the same: logits and states agree bit for bit."""
+    for path in (ref_test_rbin, small_gauss_rbin):
+        b = backend(path)
+        V = b.vocab_size
+        for n in (8, 9, 40, 130):
+            toks = zipf_tokens(n, 3, vocab=V, seed_base=17 * n)
+            outs = {}
+            try:
+                for mode in (0, 1):
+                    b.set_option("f32_pairs", mode)
+                    b.batch_init(n)
+                    for t in range(3):
+                        lg = b.forward_batch(list(range(n)), toks[:, t]).copy()
+                    outs[mode] = (lg,) + tuple(b.get_state(n - 1))
+            finally:
+                b.set_option("f32_pairs", 1)
+            for i in range(len(outs[0])):
+                assert np.array_equal(bits(outs[0][i]), bits(outs[1][i])), (path, n, i)
