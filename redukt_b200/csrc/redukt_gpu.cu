@@ -194,7 +194,7 @@ void pool_free(Pool* p) {
 
 constexpr int kSoftmaxTile = 2048;  // logits per partial (max, sum) of the probability pass
 constexpr int kSplitMaxTiles = 1024;    // split-K tile counters
-constexpr int kSplitMaxN = 64;          // split launches use the 16-stream tile (n <= 64)
+constexpr int kSplitMaxN = 256;         // split launches use the 16-stream tile (n <= 256)
 int g_split_target = 148;               // CTAs a split launch may use (one wave on 148 SMs)
 
 size_t split_part_floats(int rows, int groups, int n) {
@@ -694,8 +694,19 @@ void project(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st) {
         gemv_f32<4>(m.rows, m.cols, m.f, p.act_f, m.cols, n, epi, st);
     } else if (use_tc(n)) {
         // narrow stream tiles at small n put more CTAs on the weights (re-reads hit L2)
-        if (n <= 64) project_tc_bn<16>(m, p, n, epi, st);
-        else if (n <= 256) project_tc_bn<32>(m, p, n, epi, st);
+        const int rt = (m.rows + tc::kBM - 1) / tc::kBM;
+        if (n <= 64) {
+            project_tc_bn<16>(m, p, n, epi, st);
+        } else if (n <= 256) {
+            // few row tiles (out_proj): 16-stream tiles whose K splits run in parallel CTAs, when
+            // that fills the GPU better; else the narrowest tile that still fits one wave
+            if (p.part && split_for(((n + 15) / 16) * rt, m.rows, m.cols / kGroup, n, p.part_cap) > 1)
+                project_tc_bn<16>(m, p, n, epi, st);
+            else if (((n + 31) / 32) * rt > G.num_sms && ((n + 63) / 64) * rt <= G.num_sms)
+                project_tc_bn<64>(m, p, n, epi, st);
+            else
+                project_tc_bn<32>(m, p, n, epi, st);
+        }
         else if (G.large_tile == 1) project_tc_bn<32, Epi, 6, 2>(m, p, n, epi, st);  // two CTAs per SM
         else project_tc_bn<64>(m, p, n, epi, st);
     } else {
