@@ -599,8 +599,9 @@ void gemv_f32(int M, int K, const float* W, const float* act, int ld, int n, Epi
 }
 
 // x_proj of every profile: group chains into p.xpart[b][g][r], summed in group order into p.zp.
-// Above 128 streams, 64-stream tiles (the group's weights staged once per 64 streams, 4 x 8
-// register blocks); the chains and their group-order sums are the same either way.
+// Above 512 streams, 64-stream tiles (the group's weights staged once per 64 streams, 4 x 8
+// register blocks; below that they leave SMs idle); the chains and their group-order sums are the
+// same either way.
 // The in_proj epilogue of layer li: with conv_defer the x-branch is stored before the conv and
 // launch_xproj runs conv1d + SiLU in its staging pass (same arithmetic, same bits).
 EpiInProj in_proj_epi(const Layer& L, int li, const Pool& p, const uint32_t* vs) {
@@ -612,7 +613,7 @@ EpiInProj in_proj_epi(const Layer& L, int li, const Pool& p, const uint32_t* vs)
 void launch_xproj(const Layer& L, int li, const Pool& p, int n, const uint32_t* vs, cudaStream_t st) {
     const int ng = (G.di + kXGroup - 1) / kXGroup;
     XConv cv{G.conv_defer, (int)p.cap, li, vs, p.rflag, p.conv, L.conv_t, L.conv_b, p.conv_out};
-    if (n > 128) {
+    if (n > 512) {
         const size_t smem = ((size_t)G.xr * 68 + 64 * 68) * sizeof(float);
         allow_smem(k_xproj_part<64, 4, 8>, smem);
         launch(k_xproj_part<64, 4, 8>, dim3(ng, (n + 63) / 64), dim3(256), smem, st, G.xr, G.di, (const float*)L.x_proj,
