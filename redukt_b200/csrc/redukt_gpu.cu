@@ -692,7 +692,12 @@ void project_tc_bn(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st)
 template <class Epi>
 void project(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st) {
     if (G.profile == kF32) {
-        gemv_f32<4>(m.rows, m.cols, m.f, p.act_f, m.cols, n, epi, st);
+        // below 8 streams, fewer rows per warp when 4 would leave the GPU short of CTAs (out_proj:
+        // 24 CTAs at one stream); the per-(row, stream) arithmetic does not depend on it
+        const long ct = (long)((n + 7) / 8) * ((m.rows + 31) / 32);
+        if (n >= 8 || ct >= 2 * G.num_sms) gemv_f32<4>(m.rows, m.cols, m.f, p.act_f, m.cols, n, epi, st);
+        else if (2 * ct >= 2 * G.num_sms) gemv_f32<2>(m.rows, m.cols, m.f, p.act_f, m.cols, n, epi, st);
+        else gemv_f32<1>(m.rows, m.cols, m.f, p.act_f, m.cols, n, epi, st);
     } else if (use_tc(n)) {
         // narrow stream tiles at small n put more CTAs on the weights (re-reads hit L2)
         const int rt = (m.rows + tc::kBM - 1) / tc::kBM;
@@ -1294,6 +1299,7 @@ BackendResult redukt_backend_init(const uint8_t* weights_path, int32_t device_id
         return BACKEND_INIT_FAILED;
     }
     int maj = 0, min = 0;
+    cudaDeviceGetAttribute(&G.num_sms, cudaDevAttrMultiProcessorCount, G.device);  // launch shapes, every profile
     cudaDeviceGetAttribute(&maj, cudaDevAttrComputeCapabilityMajor, G.device);
     cudaDeviceGetAttribute(&min, cudaDevAttrComputeCapabilityMinor, G.device);
     if (maj != 10 || min != 0) {
