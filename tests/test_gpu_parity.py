@@ -422,3 +422,26 @@ def test_f32_pair_gemv_bit_identical(ref_test_rbin, small_gauss_rbin):
                 b.set_option("f32_pairs", 1)
             for i in range(len(outs[0])):
                 assert np.array_equal(bits(outs[0][i]), bits(outs[1][i])), (path, n, i)
+
+
+def test_head_tile_shapes_bit_identical(small_gauss_rbin, mamba130m_rbin):
+    """Above 64 streams the head runs as 32-stream tiles two CTAs per SM (head_wide 1) or with the
+    layer projections' tiles (0); logits and probabilities agree bit for bit."""
+    for path in (q8(small_gauss_rbin), q8(mamba130m_rbin)):
+        b = backend(path)
+        V = b.vocab_size
+        for n in (65, 200, 300):
+            toks = zipf_tokens(n, 2, vocab=V, seed_base=19 * n)
+            outs = {}
+            try:
+                for mode in (0, 1):
+                    b.set_option("head_wide", mode)
+                    b.batch_init(2 * n)
+                    for t in range(2):
+                        lg = b.forward_batch(list(range(n)), toks[:, t]).copy()
+                        pr = b.forward_batch_probs(list(range(n, 2 * n)), toks[:, t]).copy()
+                    outs[mode] = (lg, pr)
+            finally:
+                b.set_option("head_wide", 1)
+            assert np.array_equal(bits(outs[0][0]), bits(outs[1][0])), (path, n)
+            assert np.array_equal(bits(outs[0][1]), bits(outs[1][1])), (path, n)
