@@ -148,8 +148,9 @@ int32_t redukt_b200_info(uint32_t* out, uint32_t n);
  *                  (only with proj_path 0; same bits as the per-kernel step)
  *   "head_ctas"    1 or 2 = tensor-core head tiles per SM at up to 64 streams (2: a 6-stage pipeline
  *                  so two CTAs share an SM; 1: the 12-stage tile of the other projections)
- *   "head_wide"    0/1 = above 64 streams, the head as 32-stream tensor-core tiles two CTAs per SM
- *                  (1, default) or with the layer projections' tile choice (0); same bits
+ *   "head_wide"    0/1 = above 16 streams, the head as 32-stream tensor-core tiles two CTAs per SM
+ *                  (1, default) or 16-stream tiles up to 64 streams, then the layer projections'
+ *                  tile choice (0); same bits
  *   "scan_blk"     0/1 = above 64 streams, scan blocks of 16-32 streams per CTA with the channel
  *                  group's weights staged once (1, default) or one stream per CTA (0); same bits
  *   "large_tile"   0/1 = above 256 streams, tensor-core tiles of 64 streams, one CTA per SM (0) or

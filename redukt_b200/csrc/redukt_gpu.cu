@@ -147,7 +147,7 @@ struct Model {
                                 //   tiles (one CTA per SM), 1 = 32-stream tiles, two CTAs per SM
     int fused_nc = 0;           // norm chunks of the instantiated kernel, 0 = shape not supported
     int head_ctas = 2;          // option "head_ctas": 2 = the two-CTAs-per-SM head tiles at small batch
-    bool head_wide = true;      // option "head_wide": above 64 streams, 32-stream head tiles two per SM
+    bool head_wide = true;      // option "head_wide": above 16 streams, 32-stream head tiles two per SM
     bool q8_payload = false;    // the loaded file stores its Q8 matrices quantised (flag bit 6)
     int num_sms = 0;
     FusedLayer* d_fused = nullptr;  // [nl] device copy of the layer pointers
@@ -723,14 +723,15 @@ void project(const Mat& m, const Pool& p, int n, Epi epi, cudaStream_t st) {
 
 // The LM head: hundreds of row tiles, so at small batch a shallower pipeline (6 stages) that lets
 // two CTAs share an SM (TMEM: 2 x 256 columns) keeps more tiles in flight than one deep CTA.
-// Above 64 streams the head's hundreds of row tiles run as 32-stream tiles two CTAs per SM
-// (option head_wide 1, default; 0: the layer projections' tile choice), which keeps two tiles'
-// epilogues and copies in flight per SM.
+// Above 16 streams the head's hundreds of row tiles run as 32-stream tiles two CTAs per SM
+// (option head_wide 1, default; 0: 16-stream tiles up to 64 streams, then the layer projections'
+// tile choice), which keeps two tiles' epilogues and copies in flight per SM.
 void project_head(const Pool& p, int n, float* out, cudaStream_t st) {
-    if (G.profile != kF32 && use_tc(n) && n <= 64 && G.head_ctas == 2)
-        project_tc_bn<16, EpiStore, 6, 2>(G.head, p, n, EpiStore{out, G.V}, st);
-    else if (G.profile != kF32 && use_tc(n) && n > 64 && G.head_wide)
+    const bool tc = G.profile != kF32 && use_tc(n);
+    if (tc && n > 16 && G.head_wide)
         project_tc_bn<32, EpiStore, 6, 2>(G.head, p, n, EpiStore{out, G.V}, st);
+    else if (tc && n <= 64 && G.head_ctas == 2)
+        project_tc_bn<16, EpiStore, 6, 2>(G.head, p, n, EpiStore{out, G.V}, st);
     else
         project(G.head, p, n, EpiStore{out, G.V}, st);
 }
@@ -743,9 +744,10 @@ void project_head_softmax(const Pool& p, int n, float* out, int tiles, cudaStrea
     e.ld = G.V;
     e.red = p.red;
     e.parts = tiles;
-    if (n <= 64 && G.head_ctas == 2) project_tc_bn<16, EpiStoreSoftmax, 6, 2>(G.head, p, n, e, st);
+    if (n > 16 && G.head_wide) project_tc_bn<32, EpiStoreSoftmax, 6, 2>(G.head, p, n, e, st);
+    else if (n <= 64 && G.head_ctas == 2) project_tc_bn<16, EpiStoreSoftmax, 6, 2>(G.head, p, n, e, st);
     else if (n <= 64) project_tc_bn<16>(G.head, p, n, e, st);
-    else if (G.head_wide || G.large_tile == 1) project_tc_bn<32, EpiStoreSoftmax, 6, 2>(G.head, p, n, e, st);
+    else if (G.large_tile == 1) project_tc_bn<32, EpiStoreSoftmax, 6, 2>(G.head, p, n, e, st);
     else if (n <= 256) project_tc_bn<32>(G.head, p, n, e, st);
     else project_tc_bn<64>(G.head, p, n, e, st);
 }

@@ -425,12 +425,12 @@ def test_f32_pair_gemv_bit_identical(ref_test_rbin, small_gauss_rbin):
 
 
 def test_head_tile_shapes_bit_identical(small_gauss_rbin, mamba130m_rbin):
-    """Above 64 streams the head runs as 32-stream tiles two CTAs per SM (head_wide 1) or with the
-    layer projections' tiles (0); logits and probabilities agree bit for bit."""
+    """Above 16 streams the head runs as 32-stream tiles two CTAs per SM (head_wide 1) or with
+    16-stream tiles / the layer projections' tiles (0); logits and probabilities agree bit for bit."""
     for path in (q8(small_gauss_rbin), q8(mamba130m_rbin)):
         b = backend(path)
         V = b.vocab_size
-        for n in (65, 200, 300):
+        for n in (17, 32, 65, 200, 300):
             toks = zipf_tokens(n, 2, vocab=V, seed_base=19 * n)
             outs = {}
             try:
